@@ -1,0 +1,501 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 LFM3 backbone step (one JSON line on rank 0).
+
+Workload (steady state; configs[1] is a parity
+case): per GPU, 8 sessions of the graded synthetic LFM3 geometry (Q8_0,
+hidden 2048, FFN 8192, 16/4 heads, vocab 65536, 24 layers) with prompt
+lengths uniform in [64, 4096] (seed 1, + rank), prefilled through 512-row
+prompt passes; then decode rounds of all 8 ragged rows. A "step" is one
+decode round (8 tokens per GPU); `value` is whole-job decode tok/s with every
+input resident on the device (ForwardBatchInputs, logits left in HBM), `e2e`
+is the same through the host API (ForwardBatch with pinned host token and
+logits buffers, greedy tokens chosen on the host). Prefill tok/s of the
+workload's 512-row passes and of a standalone 512-row pass go beside it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun: one process per GPU, each an independent model
+replica with its own sessions (no collective on the data path); timing is the
+maximum over ranks.
+"""
+import argparse
+import concurrent.futures
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+METRIC = "decode tok/s (8 ragged sessions, Q8_0) + 512-chunk prefill tok/s; % roofline"
+SESSIONS = 8
+PROMPT_RANGE = (64, 4096)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt-max", type=int, default=PROMPT_RANGE[1])
+    return ap.parse_args()
+
+
+# ---- roofline arithmetic ------------------------------------------------------------
+def layer_counts(cfg):
+    kinds = [cfg.layer_type[i] for i in range(cfg.n_layers)]
+    return kinds.count(0), kinds.count(1), kinds.count(2)  # conv, global, sliding
+
+
+def matrix_elements(cfg):
+    """Q8_0 matrix elements read by one decode round (all layers + LM head)."""
+    H, F, A = cfg.hidden, cfg.intermediate, cfg.heads * 128
+    total = 0
+    for i in range(cfg.n_layers):
+        total += 3 * F * H
+        if cfg.layer_type[i] == 0:
+            total += 3 * H * H + H * H
+        else:
+            kv = cfg.kv_heads[i] * 128
+            total += A * H + 2 * kv * H + cfg.heads * H + H * A
+    return total + cfg.vocab * H
+
+
+def small_tensor_bytes(cfg):
+    """F32 norm, convolution and RoPE weights read by one round."""
+    H = cfg.hidden
+    total = 4 * H * 4 * cfg.n_layers + H * 4 + 64 * 4
+    for i in range(cfg.n_layers):
+        total += H * cfg.conv_width * 4 if cfg.layer_type[i] == 0 else 2 * 128 * 4
+    return total
+
+
+def decode_round_bytes(cfg, depths):
+    """Algorithmic HBM bytes of one decode round whose rows sit at `depths`
+    keys before them: Q8 weights once, plus per row the K/V rows attention
+    reads, the new K/V row, convolution state read+write, logits and the
+    embedding row."""
+    conv, full, sliding = layer_counts(cfg)
+    W = matrix_elements(cfg) * 34 // 32
+    kv_key = {i: 2 * cfg.kv_heads[i] * 128 * 2 for i in range(cfg.n_layers)}
+    per_key = max(kv_key.values()) if kv_key else 0
+    total = W + small_tensor_bytes(cfg)
+    for d in depths:
+        keys = d + 1
+        for i in range(cfg.n_layers):
+            t = cfg.layer_type[i]
+            if t == 1:
+                total += kv_key[i] * keys + kv_key[i]
+            elif t == 2:
+                total += kv_key[i] * min(keys, cfg.window) + kv_key[i]
+            else:
+                total += 2 * cfg.hidden * (cfg.conv_width - 1) * 4
+        total += cfg.vocab * 4 + cfg.hidden * 34 // 32
+    del per_key
+    return total
+
+
+def prefill_flops(cfg, n, position, logits=True):
+    """Dense FLOPs of one prompt pass of n rows at position, with the
+    engine's live-row pruning after the last full-attention layer; attention
+    counts QK and PV over the keys each live query sees; dequantisation and
+    per-block scaling are not counted."""
+    H, F, A, L = cfg.hidden, cfg.intermediate, cfg.heads * 128, cfg.n_layers
+    live_in, live_out = [n] * L, [n] * L
+    need = 1
+    for i in reversed(range(L)):
+        t = cfg.layer_type[i]
+        if t == 2:
+            break
+        live_out[i] = min(n, need)
+        if t == 1:
+            break
+        need = min(n, need + cfg.conv_width - 1)
+        live_in[i] = need
+    flops = 0
+    for i in range(L):
+        rin, rout = live_in[i], live_out[i]
+        if cfg.layer_type[i] == 0:
+            flops += 2 * rin * 3 * H * H + 2 * rout * H * H
+        else:
+            kv = cfg.kv_heads[i] * 128
+            flops += 2 * n * (A * H + 2 * kv * H + cfg.heads * H)
+            keys = 0
+            for q in range(n - rout, n):
+                k = position + q + 1
+                keys += min(k, cfg.window) if cfg.layer_type[i] == 2 else k
+            flops += 4 * cfg.heads * 128 * keys + 2 * rout * H * A
+        flops += 2 * rout * 3 * F * H
+    if logits:
+        flops += 2 * cfg.vocab * H
+    return flops
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p.get("bf16_tflops_sustained"), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per q8_gemv launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "q8_gemv_decode.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---- clocks ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.lines, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- CPU baseline ------------------------------------------------------------------------
+def cpu_decode_rate(weights, threads, tokens_per_session, warm_steps, prefer_reference=True):
+    """Decode tok/s of `threads` independent sessions, one per host thread,
+    on the reference's CPU oracle (oracle/_ref, compiled reference.cpp) when
+    present, else on the oracle's C restatement. Each session first advances
+    warm_steps tokens (depth), then times tokens_per_session logits steps."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    kind = "reference" if prefer_reference and oracle.reference_available() else "port"
+    make = (lambda: oracle.ReferenceOracle(weights, 256)) if kind == "reference" else (
+        lambda: oracle.Oracle(weights, 256, threads=1))
+    sessions = [make() for _ in range(threads)]
+    barrier = threading.Barrier(threads)
+    times = [0.0] * threads
+
+    def run(i):
+        s = sessions[i]
+        for t in range(warm_steps):
+            s.step((7 * i + t) % weights.config.vocab, False)
+        barrier.wait()
+        t0 = time.perf_counter()
+        for t in range(tokens_per_session):
+            s.step((11 * i + t) % weights.config.vocab, True)
+        times[i] = time.perf_counter() - t0
+
+    with concurrent.futures.ThreadPoolExecutor(threads) as pool:
+        list(pool.map(run, range(threads)))
+    for s in sessions:
+        s.close()
+    elapsed = max(times)
+    return threads * tokens_per_session / elapsed, elapsed, kind
+
+
+def reference_arm(args):
+    """The reference's own CPU implementation of the path on this host."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
+    weights = lfm3.SyntheticWeights(seed=0)
+    threads = max(1, min(SESSIONS, os.cpu_count() or 1))
+    # one step = one decode token per session; warm-up steps deepen the rows
+    rate, elapsed, kind = cpu_decode_rate(weights.weights, threads, args.steps,
+                                          args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{threads} sessions on {threads} host threads, one decode "
+                               f"token per session per step after {args.warmup} warm-up "
+                               "tokens (the CPU cannot prefill 4096-token prompts in minutes)",
+                   "model": "LFM3 synthetic 24L h2048 f8192 16/4x128 v65536 Q8_0",
+                   "parallelism": "threads"},
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": kind,
+                         "sample": f"{threads} sessions x {args.steps} decode tokens"},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm ---------------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def sync_max(value):
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
+    weights = lfm3.SyntheticWeights(seed=0)
+    cfg = weights.config
+    model = lfm3.Model(weights.weights)
+    rng = np.random.default_rng([1, rank])
+    lengths = rng.integers(PROMPT_RANGE[0], args.prompt_max + 1, SESSIONS)
+    total_steps = args.warmup * 2 + args.steps * 3 + 8
+    sessions = [model.session(int(n) + total_steps + 16) for n in lengths]
+    prompts = [rng.integers(0, cfg.vocab, int(n)).astype(np.uint32) for n in lengths]
+
+    def stream_of(s):
+        return torch.cuda.ExternalStream(s.stream)
+
+    # ---- prefill of the workload (512-row passes), device-timed per session
+    prefill_ms, prefill_tokens, prefill_fl = 0.0, 0, 0.0
+    launches0 = lfm3.launch_count()
+    for s, p in zip(sessions, prompts):
+        st = stream_of(s)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(st)
+        s.forward(p)
+        end.record(st)
+        end.synchronize()
+        prefill_ms += start.elapsed_time(end)
+        prefill_tokens += len(p)
+        for first in range(0, len(p), 512):
+            n = min(512, len(p) - first)
+            prefill_fl += prefill_flops(cfg, n, first, logits=first + n == len(p))
+    # ---- a standalone 512-row pass at position 0 (reference's pp512 unit)
+    probe = model.session(1024)
+    pass_tokens = np.random.default_rng(5).integers(0, cfg.vocab, 512).astype(np.uint32)
+    st = stream_of(probe)
+    pass_times = []
+    for rep in range(4):
+        probe.reset()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(st)
+        probe.forward(pass_tokens)
+        end.record(st)
+        end.synchronize()
+        if rep:
+            pass_times.append(start.elapsed_time(end))
+    pass_ms = min(pass_times)
+    pass_flops = prefill_flops(cfg, 512, 0)
+    probe.close()
+
+    hbm_peak, tensor_peak, tensor_sustained, peak_source = measured_peaks()
+    front = sessions[0]
+    fst = stream_of(front)
+    tokens = [int(np.argmax(s.read_logits())) for s in sessions]
+
+    def device_rounds(k):
+        for step in range(k):
+            lfm3.Session.forward_batch_inputs(
+                sessions, [(t + step) % cfg.vocab for t in tokens], logits=True)
+
+    # ---- warm-up, then the device-resident timed region
+    device_rounds(args.warmup)
+    depths = [s.position for s in sessions]
+    barrier()
+    sampler = ClockSampler(local)
+    with sampler:
+        launches_before = lfm3.launch_count()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(fst)
+        device_rounds(args.steps)
+        end.record(fst)
+        end.synchronize()
+        launches = lfm3.launch_count() - launches_before
+        decode_ms = start.elapsed_time(end)
+    barrier()
+    decode_ms_max = sync_max(decode_ms)
+    step_bytes = decode_round_bytes(cfg, [d + args.steps // 2 for d in depths])
+
+    # ---- end to end through the host API: pinned token/logit buffers
+    pinned_logits = [torch.empty(cfg.vocab, dtype=torch.float32, pin_memory=True).numpy()
+                     for _ in sessions]
+    pinned_tokens = torch.empty(SESSIONS, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+    for r, s in enumerate(sessions):
+        pinned_logits[r][:] = s.read_logits()
+    pinned_tokens[:] = [int(np.argmax(l)) for l in pinned_logits]
+
+    def host_rounds(k):
+        for _ in range(k):
+            lfm3.Session.forward_batch(sessions, pinned_tokens, outs=pinned_logits)
+            for r in range(SESSIONS):
+                pinned_tokens[r] = int(np.argmax(pinned_logits[r]))
+
+    host_rounds(args.warmup)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    start.record(fst)
+    host_rounds(args.steps)
+    end.record(fst)
+    end.synchronize()
+    e2e_ms = max(start.elapsed_time(end), (time.perf_counter() - t0) * 1e3)
+    barrier()
+    e2e_ms_max = sync_max(e2e_ms)
+
+    # ---- profiled pass (events around each kernel; not the headline timing)
+    front.set_profiling(True)
+    front.take_profile()
+    device_rounds(min(args.steps, 10))
+    prof = front.take_profile()
+    front.set_profiling(False)
+    proj_ms, proj_launches = prof["decode_projection"]
+    profiled_rounds = min(args.steps, 10)
+    proj_bytes = matrix_elements(cfg) * 34 // 32 * profiled_rounds
+    gemv_gbs = proj_bytes / (proj_ms * 1e-3) / 1e9 if proj_ms else 0.0
+    traffic = committed_traffic()
+
+    # ---- CPU baseline (rank 0, one GPU only; bounded sample)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = max(1, min(SESSIONS, os.cpu_count() or 1))
+        rate, elapsed, kind = cpu_decode_rate(weights.weights, threads, 2, 3)
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": kind,
+               "sample": f"{threads} sessions x 2 decode tokens at depth 3, one session "
+                         f"per host thread ({elapsed:.1f} s)"}
+
+    tokens_all = SESSIONS * world * args.steps
+    value = tokens_all / (decode_ms_max / 1e3)
+    e2e = tokens_all / (e2e_ms_max / 1e3)
+    prefill_rate = prefill_tokens * world / (sync_max(prefill_ms) / 1e3)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    clocks = sampler.summary()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": decode_ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q8_0 codes x fp16 pairs -> fp32",
+        "data": "synthetic",
+        "config": {
+            "workload": "config3 steady decode: 8 sessions/GPU, prompts U[64,4096] "
+                        "(seed 1) prefilled in 512-row passes, then decode rounds of the "
+                        "8 ragged rows; logits on device each round",
+            "model": "LFM3 synthetic 24L h2048 f8192 16/4x128 v65536 Q8_0 (random init)",
+            "global_batch": SESSIONS * world,
+            "depths": [int(d) for d in depths],
+            "parallelism": f"replicas x{world} (sessions partitioned, no collective)",
+            "l2": "inputs larger than L2: each round streams 1.78 GB of weights",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": "q8_gemv_kernel (decode projections + LM head)",
+            "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",
+            "frac": gemv_gbs / hbm_peak, "traffic": traffic,
+            "peak_source": f"{peak_source} hbm_gbs",
+            "how": f"Q8 weight bytes of {profiled_rounds} rounds / summed CUDA-event time "
+                   f"of their {proj_launches} q8_gemv launches (profiled pass)",
+        },
+        "step_roofline": {
+            "bound": "hbm", "bytes_per_step": step_bytes,
+            "achieved": step_bytes / (decode_ms_max / args.steps * 1e-3) / 1e9,
+            "peak": hbm_peak, "unit": "GB/s",
+            "frac": step_bytes / (decode_ms_max / args.steps * 1e-3) / 1e9 / hbm_peak,
+        },
+        "prefill": {
+            "value": prefill_rate, "unit": "tok/s",
+            "tflops": prefill_fl / (prefill_ms * 1e-3) / 1e12,
+            "pass512_ms": pass_ms, "pass512_tok_s": 512 / (pass_ms * 1e-3) * world,
+            "pass512_tflops": pass_flops / (pass_ms * 1e-3) / 1e12,
+            "roofline": {"bound": "tensor", "achieved": pass_flops / (pass_ms * 1e-3) / 1e12,
+                         "peak": tensor_peak, "unit": "TFLOP/s",
+                         "frac": pass_flops / (pass_ms * 1e-3) / 1e12 / tensor_peak,
+                         "peak_source": f"{peak_source} bf16_tflops (dense, burst)"},
+        },
+        "kernel_ms_per_round": {k: v[0] / profiled_rounds for k, v in prof.items() if v[1]},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 136,
+                "d2h_bytes_per_step": 4 * cfg.vocab * SESSIONS},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,246 @@
+/* C ABI of the B200 (sm_100a) LFM3 backbone step library, liblfm3_cuda.so.
+ *
+ * Two layers, both plain C: pointers, sizes, POD descriptors, no exceptions.
+ *
+ * 1. Operators (lfm3_cuda_*): one entry point per function of the
+ *    reference's operator surface, namespace gufo::models::lfm3::gpu in
+ *    hip/ops.hpp (cited per function). Pointer arguments are device
+ *    pointers, `stream` is a cudaStream_t passed as void* (NULL: legacy
+ *    default stream), tensors are lfm3_tensor descriptors whose data points
+ *    to device memory in the reference's GGUF encodings.
+ * 2. Engine (lfm3_model_* / lfm3_session_*): the reference's Model and
+ *    Session (engine.hpp:17-163) over those operators. Host buffers unless
+ *    stated.
+ *
+ * Every function returns LFM3_OK (0) or a negative LFM3_ERR_* code; the
+ * message of the last failure on the calling thread is lfm3_last_error().
+ * The reference's operators return void / bool and throw
+ * std::invalid_argument on unsupported shapes (hip/ops.hip:2293-2294); here
+ * those become LFM3_ERR_UNSUPPORTED and nothing is launched.
+ */
+#ifndef LFM3_CUDA_H_
+#define LFM3_CUDA_H_
+#include <stddef.h>
+#include <stdint.h>
+
+#include "lfm3_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum lfm3_status {
+  LFM3_OK = 0,
+  LFM3_ERR_INVALID = -1,     /* bad argument or refused input */
+  LFM3_ERR_CUDA = -2,        /* a CUDA call failed */
+  LFM3_ERR_UNSUPPORTED = -3, /* shape or format this build does not run */
+  LFM3_ERR_POISONED = -4,    /* session needs lfm3_session_reset */
+  LFM3_ERR_DEVICE_WAIT = -5, /* a bounded device wait gave up */
+};
+
+/* Message of the last failure on this thread ("" if none). */
+const char* lfm3_last_error(void);
+/* Reads and clears the device error word set by bounded waits that gave up
+ * (0: none). */
+unsigned lfm3_cuda_take_device_error(void);
+
+/* ---- operators (hip/ops.hpp) -------------------------------------------- */
+
+/* DenseWorkspace (hip/ops.hpp:21-26): quantized holds FP16 prompt
+ * activations or split decode activations, row_max one word per row,
+ * partial and tickets (zeroed once, kept zero between calls) the split-K
+ * fix-up of the decode projections. */
+typedef struct lfm3_dense_workspace {
+  void* quantized;
+  unsigned* row_max;
+  float* partial;
+  unsigned* tickets;
+} lfm3_dense_workspace;
+
+/* DenseWorkspaceBytes (hip/ops.hpp:27): bytes of `quantized` for rows x K. */
+size_t lfm3_cuda_dense_workspace_bytes(size_t rows, size_t K);
+/* Bytes of `partial` and words of `tickets` (SplitPartialBytes,
+ * hip/ops.hpp:35; kMaxSplitUnits, hip/ops.hpp:28). */
+size_t lfm3_cuda_split_partial_bytes(void);
+size_t lfm3_cuda_split_ticket_words(void);
+/* kPromptRows (hip/ops.hpp:33): projections of at least this many rows
+ * read FP16 row-scaled activations; fewer rows keep FP32 inputs (as two
+ * fp16 terms on the tensor cores). */
+int lfm3_cuda_prompt_rows(void);
+
+/* Embed (hip/ops.hpp:13-14): out[r] = row tokens[r] of weight, FP32. */
+int lfm3_cuda_embed(const lfm3_tensor* weight, const uint32_t* tokens,
+                    float* out, int n, void* stream);
+
+/* Dense (hip/ops.hpp:72-73): out[n][rows] = x[n][cols] . weight^T. */
+int lfm3_cuda_dense(const lfm3_tensor* weight, const float* x, float* out,
+                    int n, void* stream, const lfm3_dense_workspace* workspace);
+
+/* Output (hip/ops.hpp:37-40). */
+typedef struct lfm3_output {
+  const lfm3_tensor* weight;
+  float* out;
+} lfm3_output;
+
+/* Project (hip/ops.hpp:46-48): up to four weights with the same column
+ * count read one input. */
+int lfm3_cuda_project(const lfm3_output* outputs, int count, const float* x,
+                      int n, void* stream,
+                      const lfm3_dense_workspace* workspace);
+/* ProjectSwiGLU (hip/ops.hpp:51-53): out = silu(gate x) * (up x). */
+int lfm3_cuda_project_swiglu(const lfm3_tensor* gate, const lfm3_tensor* up,
+                             const float* x, float* out, float* up_scratch,
+                             int n, void* stream,
+                             const lfm3_dense_workspace* workspace);
+/* ProjectFfn (hip/ops.hpp:55-58): out = down(silu(gate x) * (up x)), the
+ * activation left in hidden. */
+int lfm3_cuda_project_ffn(const lfm3_tensor* gate, const lfm3_tensor* up,
+                          const lfm3_tensor* down, const float* x,
+                          float* hidden, float* up_scratch, float* out, int n,
+                          void* stream, const lfm3_dense_workspace* workspace);
+
+/* ResidualNorm (hip/ops.hpp:62-65): x += post_norm(branch) (branch and
+ * post_norm may be NULL), then z = norm(x) unless norm is NULL. With split
+ * set, z goes to workspace->quantized as FP16 prompt activations instead.
+ * Returns LFM3_ERR_UNSUPPORTED for widths this build does not run (the
+ * reference returns false). */
+int lfm3_cuda_residual_norm(const float* branch, const lfm3_tensor* post_norm,
+                            float* x, const lfm3_tensor* norm, float* z, int n,
+                            int hidden, float eps, int split, void* stream,
+                            const lfm3_dense_workspace* workspace);
+
+/* ShortConv (hip/ops.hpp:76-78): gated width-L causal convolution over n
+ * rows of projection [B | C | x] (3 * hidden floats per row), reading
+ * history (f32 [hidden][L - 1]) before the first row and, with update,
+ * storing the last L - 1 B*x products back into it. */
+int lfm3_cuda_short_conv(const float* projection, const float* weight,
+                         float* history, float* out, int n, int hidden,
+                         int width, void* stream, int update);
+
+/* RopeFrequencies (hip/ops.hpp:80): out[i] = float(pow(double theta,
+ * -2i/dim)), dim / 2 values. */
+int lfm3_cuda_rope_frequencies(float* out, int dim, float theta, void* stream);
+/* Rope (hip/ops.hpp:81-82): rotates pairs (i, i + dim/2) of n rows of heads
+ * heads by (position + row) * frequencies[i] / factors[i] (factors may be
+ * NULL). */
+int lfm3_cuda_rope(float* x, const float* frequencies, const float* factors,
+                   int n, int heads, int dim, int position, void* stream);
+
+/* Attention (hip/ops.hpp:94-98): causal gated GQA attention of n query
+ * rows at position. Keys at or after position come from k/v (n F16 rows),
+ * earlier keys from the ring cache_k/cache_v (slot t % capacity); window > 0
+ * keeps each query's last `window` keys. n == 1 keeps Q and probabilities
+ * in FP32; prompts use FP16 Q and probabilities on the tensor cores. dim
+ * must be 128 and heads / kv_heads 2, 4 or 8. */
+int lfm3_cuda_attention(const float* q, const uint16_t* k, const uint16_t* v,
+                        const float* gate, const uint16_t* cache_k,
+                        const uint16_t* cache_v, float* out, int n, int heads,
+                        int kv_heads, int dim, int position, int capacity,
+                        int window, void* stream, float* scratch);
+/* AttentionScratchBytes (hip/ops.hpp:99). */
+size_t lfm3_cuda_attention_scratch_bytes(int heads, int dim, int context,
+                                         int rows);
+
+/* PromptHeads / DecodeHeads (hip/ops.hpp:133-146): per-head Q/K RMSNorm
+ * and RoPE in place on q and k; F16 K and V rows to k16/v16 rows 0..n-1
+ * (prompt) or to ring slot position % capacity (decode). */
+int lfm3_cuda_prompt_heads(float* q, float* k, const float* v,
+                           const float* q_norm, const float* k_norm,
+                           const float* frequencies, const float* factors,
+                           uint16_t* k16, uint16_t* v16, int n, int heads,
+                           int kv_heads, int dim, int position, float eps,
+                           void* stream);
+int lfm3_cuda_decode_heads(float* q, float* k, const float* v,
+                           const float* q_norm, const float* k_norm,
+                           const float* frequencies, const float* factors,
+                           uint16_t* cache_k, uint16_t* cache_v, int heads,
+                           int kv_heads, int dim, int position, int capacity,
+                           float eps, void* stream);
+
+/* StoreKV (hip/ops.hpp:126-127) and PackKV (hip/ops.hpp:123-124). */
+int lfm3_cuda_store_kv(const uint16_t* k, const uint16_t* v, uint16_t* cache_k,
+                       uint16_t* cache_v, int n, int stride, int position,
+                       int capacity, void* stream);
+int lfm3_cuda_pack_kv(const float* k, const float* v, uint16_t* k16,
+                      uint16_t* v16, size_t count, void* stream);
+/* SelectRows (hip/ops.hpp:120-121): copies packed rows rows[i] of source. */
+int lfm3_cuda_select_rows(const lfm3_tensor* source, const uint32_t* rows,
+                          void* out, int count, void* stream);
+
+/* LaunchBatchedRMSNorm (hip/ops.hpp:148-150): out = x * rsqrt(mean x^2 +
+ * eps) * weight per row (bf16 output not supported: out_bf16 must be NULL). */
+int lfm3_cuda_batched_rmsnorm(const float* x, const float* weight, float* out,
+                              void* out_bf16, size_t batch, size_t dim,
+                              float eps, void* stream);
+
+/* ---- engine (engine.hpp) --------------------------------------------------- */
+
+typedef struct lfm3_model lfm3_model;
+typedef struct lfm3_session lfm3_session;
+
+/* Model::Load (engine.hpp:27-30) from host tensors: validates the geometry,
+ * copies the packed payloads to the current CUDA device. NULL on failure. */
+lfm3_model* lfm3_model_load(const lfm3_weights* host);
+void lfm3_model_free(lfm3_model* model);
+int lfm3_model_config(const lfm3_model* model, lfm3_config* out);
+size_t lfm3_model_weight_bytes(const lfm3_model* model);
+
+/* Model::CreateSession (engine.hpp:31-32). NULL on failure. */
+lfm3_session* lfm3_session_create(lfm3_model* model, uint32_t context);
+void lfm3_session_free(lfm3_session* session);
+
+/* Session::Forward (engine.hpp:98-101): logits (vocab floats) may be NULL. */
+int lfm3_session_forward(lfm3_session* session, const uint32_t* tokens,
+                         size_t n, float* logits);
+/* Session::ForwardBatch (engine.hpp:103-106): one token per session, up to
+ * eight distinct sessions; logits may be NULL or hold NULL entries. */
+int lfm3_session_forward_batch(lfm3_session* const* sessions,
+                               const uint32_t* tokens, size_t count,
+                               float* const* logits);
+/* Session::ForwardBatchInputs (engine.hpp:107-114): one row per session;
+ * rows[i] (device embedding rows) must be NULL in this build (tokens[i] is
+ * the input). With logits set, each session's logits are computed into its
+ * device buffer (lfm3_session_continuation_data tensor 0) without a copy to
+ * the host. */
+int lfm3_session_forward_batch_inputs(lfm3_session* const* sessions,
+                                      const uint32_t* tokens,
+                                      const float* const* rows, size_t count,
+                                      int logits);
+int lfm3_session_read_logits(lfm3_session* session, float* logits);
+int lfm3_session_read_hidden(lfm3_session* session, float* hidden);
+int lfm3_session_reset(lfm3_session* session);
+uint32_t lfm3_session_position(const lfm3_session* session);
+int lfm3_session_is_coherent(const lfm3_session* session);
+void* lfm3_session_stream(const lfm3_session* session);
+/* ContinuationData (engine.hpp:143-144): tensor 0 logits, 1 frontier,
+ * 2 convolution, 3 key ring, 4 value ring (device pointers). */
+void* lfm3_session_continuation_data(const lfm3_session* session, int tensor,
+                                     size_t layer);
+uint32_t lfm3_session_ring_capacity(const lfm3_session* session,
+                                    size_t layer);
+/* Snapshot v2 (engine.hpp:127-131). */
+size_t lfm3_session_snapshot_bytes(const lfm3_session* session);
+int lfm3_session_save_snapshot(lfm3_session* session, uint8_t* out,
+                               size_t bytes);
+int lfm3_session_restore_snapshot(lfm3_session* session, const uint8_t* data,
+                                  size_t bytes);
+/* Test hook (no reference counterpart): the k-th CUDA call of this
+ * session's next passes reports a failure, to exercise poisoning. */
+int lfm3_session_inject_failure(lfm3_session* session, int after_calls);
+
+/* Measurement hooks (no reference counterpart). With profiling on, CUDA
+ * events bracket every kernel of this session's passes (and of rounds it
+ * leads), which serialises them: use a separate profiled pass. take_profile
+ * adds the milliseconds and launch counts of the 6 kernel classes (decode
+ * projection, decode attention, row kernels, prompt projection, prompt
+ * attention, other prompt kernels) to ms[6] / launches[6] and clears them. */
+int lfm3_session_set_profiling(lfm3_session* session, int on);
+int lfm3_session_take_profile(lfm3_session* session, double* ms,
+                              long long* launches);
+/* Kernels launched by this library in this process so far. */
+unsigned long long lfm3_cuda_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

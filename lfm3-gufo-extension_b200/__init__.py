@@ -1,0 +1,311 @@
+"""B200-native LFM3 backbone step (sm_100a).
+
+Python handle on liblfm3_cuda.so (include/lfm3_cuda.h): the engine (Model /
+Session, the reference's engine.hpp) and the synthetic-weight generator. The
+kernels and the engine are native; this module only declares the C ABI and
+wraps host buffers. It fails loudly when the library is missing: there is no
+other implementation to fall back to.
+
+Import with importlib (the directory name is not an identifier):
+
+    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
+"""
+import ctypes
+import importlib
+import os
+
+import numpy as np
+
+abi = importlib.import_module(__name__ + ".abi")
+
+_lib = None
+
+
+class Lfm3Error(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__(f"LFM3 error {code}: {message}")
+        self.code = code
+
+
+def library():
+    """Loads lib/liblfm3_cuda.so once (raises if it was never built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(abi.LIBRARY):
+        raise FileNotFoundError(
+            f"{abi.LIBRARY} is not built: run build.py in the package")
+    lib = ctypes.CDLL(abi.LIBRARY)
+    abi.declare_synth(lib)
+    P, I, U32, SZ, F = (ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32,
+                        ctypes.c_size_t, ctypes.c_float)
+    sigs = {
+        "lfm3_last_error": ([], ctypes.c_char_p),
+        "lfm3_cuda_take_device_error": ([], ctypes.c_uint),
+        "lfm3_cuda_dense_workspace_bytes": ([SZ, SZ], SZ),
+        "lfm3_cuda_split_partial_bytes": ([], SZ),
+        "lfm3_cuda_split_ticket_words": ([], SZ),
+        "lfm3_cuda_prompt_rows": ([], I),
+        "lfm3_cuda_embed": ([P, P, P, I, P], I),
+        "lfm3_cuda_dense": ([P, P, P, I, P, P], I),
+        "lfm3_cuda_project": ([P, I, P, I, P, P], I),
+        "lfm3_cuda_project_swiglu": ([P, P, P, P, P, I, P, P], I),
+        "lfm3_cuda_project_ffn": ([P, P, P, P, P, P, P, I, P, P], I),
+        "lfm3_cuda_residual_norm": ([P, P, P, P, P, I, I, F, I, P, P], I),
+        "lfm3_cuda_short_conv": ([P, P, P, P, I, I, I, P, I], I),
+        "lfm3_cuda_rope_frequencies": ([P, I, F, P], I),
+        "lfm3_cuda_rope": ([P, P, P, I, I, I, I, P], I),
+        "lfm3_cuda_attention": ([P, P, P, P, P, P, P, I, I, I, I, I, I, I, P,
+                                 P], I),
+        "lfm3_cuda_attention_scratch_bytes": ([I, I, I, I], SZ),
+        "lfm3_cuda_prompt_heads": ([P, P, P, P, P, P, P, P, P, I, I, I, I, I,
+                                    F, P], I),
+        "lfm3_cuda_decode_heads": ([P, P, P, P, P, P, P, P, P, I, I, I, I, I,
+                                    F, P], I),
+        "lfm3_cuda_store_kv": ([P, P, P, P, I, I, I, I, P], I),
+        "lfm3_cuda_pack_kv": ([P, P, P, P, SZ, P], I),
+        "lfm3_cuda_select_rows": ([P, P, P, I, P], I),
+        "lfm3_cuda_batched_rmsnorm": ([P, P, P, P, SZ, SZ, F, P], I),
+        "lfm3_model_load": ([ctypes.POINTER(abi.Weights)], P),
+        "lfm3_model_free": ([P], None),
+        "lfm3_model_config": ([P, ctypes.POINTER(abi.Config)], I),
+        "lfm3_model_weight_bytes": ([P], SZ),
+        "lfm3_session_create": ([P, U32], P),
+        "lfm3_session_free": ([P], None),
+        "lfm3_session_forward": ([P, P, SZ, P], I),
+        "lfm3_session_forward_batch": ([P, P, SZ, P], I),
+        "lfm3_session_forward_batch_inputs": ([P, P, P, SZ, I], I),
+        "lfm3_session_read_logits": ([P, P], I),
+        "lfm3_session_read_hidden": ([P, P], I),
+        "lfm3_session_reset": ([P], I),
+        "lfm3_session_position": ([P], U32),
+        "lfm3_session_is_coherent": ([P], I),
+        "lfm3_session_stream": ([P], P),
+        "lfm3_session_continuation_data": ([P, I, SZ], P),
+        "lfm3_session_ring_capacity": ([P, SZ], U32),
+        "lfm3_session_snapshot_bytes": ([P], SZ),
+        "lfm3_session_save_snapshot": ([P, P, SZ], I),
+        "lfm3_session_restore_snapshot": ([P, P, SZ], I),
+        "lfm3_session_inject_failure": ([P, I], I),
+        "lfm3_session_set_profiling": ([P, I], I),
+        "lfm3_session_take_profile": ([P, P, P], I),
+        "lfm3_cuda_launch_count": ([], ctypes.c_ulonglong),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def launch_count():
+    """Kernels this library has launched in this process."""
+    return int(library().lfm3_cuda_launch_count())
+
+
+def check(code):
+    """Raises Lfm3Error for a nonzero status of the C ABI."""
+    if code != 0:
+        raise Lfm3Error(code, library().lfm3_last_error().decode())
+    return code
+
+
+def _ptr(array):
+    return ctypes.c_void_p(array.ctypes.data) if array is not None else None
+
+
+# ---- synthetic weights -----------------------------------------------------------
+
+def default_config():
+    cfg = abi.Config()
+    library().lfm3_synth_default_config(ctypes.byref(cfg))
+    return cfg
+
+
+def small_config(hidden=256, intermediate=512, vocab=1024, heads=4, kv_heads=2,
+                 window=32, context=4096, pattern="CSGCSG"):
+    """A small geometry of the same architecture, for fast tests."""
+    cfg = default_config()
+    cfg.hidden, cfg.intermediate, cfg.vocab = hidden, intermediate, vocab
+    cfg.heads, cfg.window, cfg.context = heads, window, context
+    if library().lfm3_synth_set_layers(ctypes.byref(cfg), pattern.encode(),
+                                       kv_heads):
+        raise ValueError("invalid layer pattern " + pattern)
+    return cfg
+
+
+class SyntheticWeights:
+    """Host weights from lfm3_synth_generate (freed with the object)."""
+
+    def __init__(self, config=None, seed=0, matrix_type=abi.Q8_0,
+                 norm_jitter=0.0, threads=0):
+        self.model = abi.SynthModel()
+        cfg = config if config is not None else default_config()
+        rc = library().lfm3_synth_generate(
+            ctypes.byref(cfg), seed, matrix_type, norm_jitter, threads,
+            ctypes.byref(self.model))
+        if rc:
+            raise ValueError(f"lfm3_synth_generate failed ({rc})")
+
+    @property
+    def weights(self):
+        return self.model.weights
+
+    @property
+    def config(self):
+        return self.model.weights.config
+
+    def close(self):
+        if _lib is not None and self.model.storage:
+            _lib.lfm3_synth_free(ctypes.byref(self.model))
+
+    def __del__(self):
+        self.close()
+
+
+# ---- engine --------------------------------------------------------------------------
+
+class Model:
+    """Model::Load (engine.hpp:27-30): weights copied to the current device."""
+
+    def __init__(self, weights):
+        lib = library()
+        self._weights = weights  # the host copy must outlive nothing here
+        self.handle = lib.lfm3_model_load(ctypes.byref(weights))
+        if not self.handle:
+            raise Lfm3Error(-1, lib.lfm3_last_error().decode())
+        self.config = abi.Config()
+        check(lib.lfm3_model_config(self.handle, ctypes.byref(self.config)))
+
+    @property
+    def weight_bytes(self):
+        return library().lfm3_model_weight_bytes(self.handle)
+
+    def session(self, context):
+        return Session(self, context)
+
+    def close(self):
+        if self.handle:
+            library().lfm3_model_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+class Session:
+    """Session (engine.hpp:46-163)."""
+
+    PREFILL_CHUNK = 512
+    MAX_BATCH = 8
+
+    def __init__(self, model, context):
+        lib = library()
+        self.model = model
+        self.vocab = model.config.vocab
+        self.hidden = model.config.hidden
+        self.handle = lib.lfm3_session_create(model.handle, context)
+        if not self.handle:
+            raise Lfm3Error(-1, lib.lfm3_last_error().decode())
+
+    def forward(self, tokens, logits=True, out=None):
+        """Advances tokens; returns the last row's logits (or None)."""
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        if logits and out is None:
+            out = np.empty(self.vocab, np.float32)
+        check(library().lfm3_session_forward(
+            self.handle, _ptr(toks), toks.size, _ptr(out) if logits else None))
+        return out if logits else None
+
+    @staticmethod
+    def forward_batch(sessions, tokens, logits=True, outs=None):
+        """One token per session (ForwardBatch); returns a list of logits."""
+        lib = library()
+        n = len(sessions)
+        handles = (ctypes.c_void_p * n)(*[s.handle for s in sessions])
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        if logits and outs is None:
+            outs = [np.empty(s.vocab, np.float32) for s in sessions]
+        ptrs = ((ctypes.c_void_p * n)(*[o.ctypes.data for o in outs])
+                if logits else None)
+        check(lib.lfm3_session_forward_batch(handles, _ptr(toks), n, ptrs))
+        return outs if logits else None
+
+    @staticmethod
+    def forward_batch_inputs(sessions, tokens, logits=True):
+        """ForwardBatchInputs: one token per session, logits left on the
+        device."""
+        n = len(sessions)
+        handles = (ctypes.c_void_p * n)(*[s.handle for s in sessions])
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        check(library().lfm3_session_forward_batch_inputs(
+            handles, _ptr(toks), None, n, int(bool(logits))))
+
+    def read_logits(self):
+        out = np.empty(self.vocab, np.float32)
+        check(library().lfm3_session_read_logits(self.handle, _ptr(out)))
+        return out
+
+    def read_hidden(self):
+        out = np.empty(self.hidden, np.float32)
+        check(library().lfm3_session_read_hidden(self.handle, _ptr(out)))
+        return out
+
+    def reset(self):
+        check(library().lfm3_session_reset(self.handle))
+
+    @property
+    def position(self):
+        return library().lfm3_session_position(self.handle)
+
+    @property
+    def coherent(self):
+        return bool(library().lfm3_session_is_coherent(self.handle))
+
+    @property
+    def stream(self):
+        return library().lfm3_session_stream(self.handle)
+
+    def continuation_data(self, tensor, layer=0):
+        return library().lfm3_session_continuation_data(self.handle, tensor,
+                                                        layer)
+
+    def ring_capacity(self, layer):
+        return library().lfm3_session_ring_capacity(self.handle, layer)
+
+    def save_snapshot(self):
+        lib = library()
+        n = lib.lfm3_session_snapshot_bytes(self.handle)
+        buf = np.empty(n, np.uint8)
+        check(lib.lfm3_session_save_snapshot(self.handle, _ptr(buf), n))
+        return buf
+
+    def restore_snapshot(self, payload):
+        payload = np.ascontiguousarray(payload, dtype=np.uint8)
+        check(library().lfm3_session_restore_snapshot(
+            self.handle, _ptr(payload), payload.size))
+
+    PROFILE_CLASSES = ("decode_projection", "decode_attention", "row_kernels",
+                       "prompt_projection", "prompt_attention", "prompt_other")
+
+    def set_profiling(self, on):
+        check(library().lfm3_session_set_profiling(self.handle, int(bool(on))))
+
+    def take_profile(self):
+        """{class: (milliseconds, launches)} since the last call."""
+        ms = np.zeros(6, np.float64)
+        n = np.zeros(6, np.int64)
+        check(library().lfm3_session_take_profile(self.handle, _ptr(ms), _ptr(n)))
+        return {c: (float(ms[i]), int(n[i])) for i, c in enumerate(self.PROFILE_CLASSES)}
+
+    def inject_failure(self, after_calls):
+        check(library().lfm3_session_inject_failure(self.handle, after_calls))
+
+    def close(self):
+        if self.handle:
+            library().lfm3_session_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()

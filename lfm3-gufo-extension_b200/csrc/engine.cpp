@@ -1,0 +1,1107 @@
+// Host engine: weight upload, sessions, prompt passes and decode rounds.
+//
+// The per-layer sequence follows Session::Impl::Run (engine.cpp:257-527 of
+// the reference): sandwich norms around a convolution or gated-attention
+// mixer and a SwiGLU FFN, live-row pruning after the last full-attention
+// layer for prompt passes, and batched decode rounds that share every
+// weight read between up to eight sessions.
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <stdexcept>
+#include <unordered_set>
+
+#include "kernels.cuh"
+
+namespace lfm3 {
+namespace {
+
+void Throw(cudaError_t status) {
+  if (status != cudaSuccess)
+    throw std::runtime_error(cudaGetErrorString(status));
+}
+
+// Geometry this build supports (config.cpp:39-45 plus the kernels' tiling).
+std::string Validate(const lfm3_weights& w) {
+  const auto& c = w.config;
+  if (!c.n_layers || c.n_layers > LFM3_MAX_LAYERS || c.head_dim != 128 ||
+      !c.heads || !c.hidden || !c.intermediate || !c.vocab || !c.context ||
+      c.conv_width < 2 || c.conv_width > 32 || !c.window)
+    return "unsupported LFM3 dimensions";
+  if (c.hidden % 256 || c.intermediate % 256 || (c.heads * 128) % 256)
+    return "LFM3 widths must be multiples of 256";
+  if (c.hidden > 8192)
+    return "LFM3 hidden width above 8192";
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    const uint32_t h = c.kv_heads[i];
+    if ((c.layer_type[i] == LFM3_CONV) != (h == 0))
+      return "invalid LFM3 layer heads";
+    if (h && (c.heads % h || (c.heads / h != 2 && c.heads / h != 4 &&
+                              c.heads / h != 8)))
+      return "LFM3 GQA group must be 2, 4 or 8";
+  }
+  const auto matrix = [](const lfm3_tensor& t) {
+    return t.data && t.type == LFM3_Q8_0;
+  };
+  if (!matrix(w.embedding) || !matrix(w.output))
+    return "this build needs Q8_0 embedding and output matrices";
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    const auto& l = w.layers[i];
+    if (!matrix(l.gate) || !matrix(l.up) || !matrix(l.down))
+      return "this build needs Q8_0 FFN matrices";
+    if (c.layer_type[i] == LFM3_CONV) {
+      if (!matrix(l.in_proj) || !matrix(l.out_proj) || !l.conv.data ||
+          l.conv.type != LFM3_F32)
+        return "invalid LFM3 convolution layer";
+    } else if (!matrix(l.q) || !matrix(l.k) || !matrix(l.v) ||
+               !matrix(l.attn_gate) || !matrix(l.attn_out) ||
+               !l.q_norm.data || !l.k_norm.data) {
+      return "invalid LFM3 attention layer";
+    }
+    if (!l.norm.data || !l.ffn_norm.data)
+      return "missing LFM3 norm";
+  }
+  if (!w.output_norm.data || !w.rope_freqs.data)
+    return "missing LFM3 output norm or RoPE factors";
+  return {};
+}
+
+template <class F>
+void VisitTensors(lfm3_weights& w, F f) {
+  f(w.embedding);
+  f(w.output);
+  f(w.output_norm);
+  f(w.rope_freqs);
+  for (uint32_t i = 0; i < w.config.n_layers; ++i) {
+    auto& l = w.layers[i];
+    for (lfm3_tensor* t :
+         {&l.norm, &l.ffn_norm, &l.post_norm, &l.post_ffn_norm, &l.gate, &l.up,
+          &l.down, &l.conv, &l.in_proj, &l.out_proj, &l.q, &l.k, &l.v,
+          &l.q_norm, &l.k_norm, &l.attn_gate, &l.attn_out})
+      if (t->data)
+        f(*t);
+  }
+}
+
+int CeilDiv(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+// ---- DeviceBuffer -------------------------------------------------------------
+DeviceBuffer::DeviceBuffer(size_t bytes) : bytes_(bytes) {
+  if (bytes)
+    Throw(cudaMalloc(&data_, bytes));
+}
+DeviceBuffer::~DeviceBuffer() {
+  if (data_)
+    cudaFree(data_);
+}
+DeviceBuffer::DeviceBuffer(DeviceBuffer&& o) noexcept
+    : data_(o.data_), bytes_(o.bytes_) {
+  o.data_ = nullptr;
+  o.bytes_ = 0;
+}
+DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
+  std::swap(data_, o.data_);
+  std::swap(bytes_, o.bytes_);
+  return *this;
+}
+
+// ---- Model ----------------------------------------------------------------------
+Model::~Model() = default;
+
+std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
+                                   std::string* error) {
+  try {
+    const std::string problem = Validate(host);
+    if (!problem.empty())
+      throw std::invalid_argument(problem);
+    std::shared_ptr<Model> m(new Model);
+    m->device_ = host;
+    int device = 0;
+    Throw(cudaGetDevice(&device));
+    Throw(cudaDeviceGetAttribute(&m->sms_, cudaDevAttrMultiProcessorCount,
+                                 device));
+    // Distinct payloads in host order, packed into <=128 MiB segments with
+    // 256-byte alignment (upload.cpp:12-16, 33-68).
+    std::map<const void*, size_t> payloads;
+    VisitTensors(m->device_, [&](lfm3_tensor& t) {
+      auto& bytes = payloads[t.data];
+      bytes = std::max(bytes, t.bytes);
+    });
+    constexpr size_t kSegment = 128ull << 20, kAlign = 256;
+    std::map<const void*, void*> placed;
+    auto it = payloads.begin();
+    while (it != payloads.end()) {
+      size_t bytes = 0;
+      auto end = it;
+      while (end != payloads.end() &&
+             (end == it || bytes + end->second <= kSegment)) {
+        bytes += (end->second + kAlign - 1) / kAlign * kAlign;
+        ++end;
+      }
+      m->segments_.emplace_back(bytes);
+      char* dst = m->segments_.back().as<char>();
+      for (; it != end; ++it) {
+        Throw(cudaMemcpy(dst, it->first, it->second, cudaMemcpyHostToDevice));
+        placed[it->first] = dst;
+        dst += (it->second + kAlign - 1) / kAlign * kAlign;
+      }
+      m->weight_bytes_ += bytes;
+    }
+    VisitTensors(m->device_, [&](lfm3_tensor& t) { t.data = placed.at(t.data); });
+    // RoPE frequencies: float(pow(double theta, -2i/D)), global then sliding
+    // (hip/ops.hip:1045-1050, engine.cpp:225-232).
+    float freq[128];
+    const auto& c = host.config;
+    for (int i = 0; i < 64; ++i) {
+      freq[i] = float(std::pow(double(c.theta), double(-2.0F * i / 128)));
+      freq[64 + i] =
+          float(std::pow(double(c.theta_swa), double(-2.0F * i / 128)));
+    }
+    m->freq_ = DeviceBuffer(sizeof(freq));
+    Throw(cudaMemcpy(m->freq_.data(), freq, sizeof(freq),
+                     cudaMemcpyHostToDevice));
+    return m;
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return nullptr;
+  }
+}
+
+std::unique_ptr<Session> Model::CreateSession(uint32_t context,
+                                              std::string* error) {
+  try {
+    if (!context || context > config().context)
+      throw std::invalid_argument("invalid LFM3 context");
+    return std::unique_ptr<Session>(
+        new Session(shared_from_this(), context));
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return nullptr;
+  }
+}
+
+// ---- Session ------------------------------------------------------------------
+Session::Session(std::shared_ptr<Model> model, uint32_t context)
+    : model_(std::move(model)), context_(context) {
+  const auto& c = model_->config();
+  const size_t H = c.hidden, F = c.intermediate, A = size_t(c.heads) * 128;
+  const size_t R = kPrefillChunk;
+  uint32_t kv_max = 0;
+  for (uint32_t i = 0; i < c.n_layers; ++i)
+    kv_max = std::max(kv_max, c.kv_heads[i]);
+  const size_t KV = size_t(kv_max) * 128;
+  Throw(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  try {
+    // recurrent state (engine.cpp:55-77)
+    std::vector<LayerState> table(c.n_layers);
+    for (uint32_t i = 0; i < c.n_layers; ++i) {
+      State s;
+      if (c.layer_type[i] == LFM3_CONV) {
+        s.conv = DeviceBuffer(H * (c.conv_width - 1) * 4);
+        Throw(cudaMemset(s.conv.data(), 0, s.conv.bytes()));
+      } else {
+        s.capacity = c.layer_type[i] == LFM3_SLIDING_ATTENTION
+                         ? std::min(context, c.window)
+                         : context;
+        const size_t bytes = size_t(s.capacity) * c.kv_heads[i] * 128 * 2;
+        s.k = DeviceBuffer(bytes);
+        s.v = DeviceBuffer(bytes);
+      }
+      table[i] = {s.conv.as<float>(), s.k.as<__half>(), s.v.as<__half>(),
+                  int(s.capacity), 0};
+      states_.push_back(std::move(s));
+    }
+    layer_table_ = DeviceBuffer(table.size() * sizeof(LayerState));
+    Throw(cudaMemcpy(layer_table_.data(), table.data(), layer_table_.bytes(),
+                     cudaMemcpyHostToDevice));
+    frontier_ = DeviceBuffer(H * 4);
+    logits_ = DeviceBuffer(size_t(c.vocab) * 4);
+    // workspace
+    const size_t width = std::max({3 * H, F, A});
+    ids_ = DeviceBuffer(R * 4);
+    rows_ = DeviceBuffer(sizeof(DecodeRows));
+    x_ = DeviceBuffer(R * H * 4);
+    out_ = DeviceBuffer(R * H * 4);
+    p_ = DeviceBuffer(R * 3 * H * 4);
+    q_ = DeviceBuffer(R * A * 4);
+    k_ = DeviceBuffer(R * KV * 4);
+    v_ = DeviceBuffer(R * KV * 4);
+    gate_ = DeviceBuffer(R * c.heads * 4);
+    a_ = DeviceBuffer(R * std::max(A, H) * 4);
+    ff_ = DeviceBuffer(R * F * 4);
+    row_max_ = DeviceBuffer(R * 4);
+    half_ = DeviceBuffer(R * width * 2);
+    scale_ = DeviceBuffer(R * 4);
+    z_split_ = DeviceBuffer(kMaxBatch * H * 4);
+    a_split_ = DeviceBuffer(kMaxBatch * std::max(A, H) * 4);
+    h_split_ = DeviceBuffer(kMaxBatch * F * 4);
+    z32_ = DeviceBuffer(kMaxBatch * H * 4);
+    batch_logits_ = DeviceBuffer(kMaxBatch * size_t(c.vocab) * 4);
+    chunk_k_ = DeviceBuffer(R * KV * 2);
+    chunk_v_ = DeviceBuffer(R * KV * 2);
+    const int sms = model_->sms();
+    gemv_partials_ = DeviceBuffer(gemv_partial_floats(sms) * 4);
+    const size_t max_tiles = std::max<size_t>(
+        {size_t(c.vocab) / kGemvRows + 4, F / 32 + 4, H / 16 + 4,
+         (3 * H + A + 2 * KV) / kGemvRows + 8});
+    gemv_tickets_ = DeviceBuffer(max_tiles * 4);
+    Throw(cudaMemset(gemv_tickets_.data(), 0, gemv_tickets_.bytes()));
+    attn_partials_ =
+        DeviceBuffer(decode_attention_partial_floats(c.heads) * 4);
+    attn_tickets_ = DeviceBuffer(kMaxBatch * std::max(kv_max, 1u) * 4);
+    Throw(cudaMemset(attn_tickets_.data(), 0, attn_tickets_.bytes()));
+    prompt_scratch_ = DeviceBuffer(
+        std::max<size_t>(prompt_attention_scratch_floats(c.heads, R, context),
+                         1) *
+        4);
+    Throw(cudaMallocHost(reinterpret_cast<void**>(&host_rows_),
+                         sizeof(DecodeRows)));
+    Throw(cudaDeviceSynchronize());
+  } catch (...) {
+    if (host_rows_)
+      cudaFreeHost(host_rows_);
+    cudaStreamDestroy(stream_);
+    throw;
+  }
+}
+
+Session::~Session() {
+  if (stream_) {
+    cudaStreamSynchronize(stream_);
+    cudaStreamDestroy(stream_);
+  }
+  for (cudaEvent_t e : events_)
+    cudaEventDestroy(e);
+  if (host_rows_)
+    cudaFreeHost(host_rows_);
+}
+
+void Session::Check(cudaError_t status) {
+  if (inject_after_ > 0 && --inject_after_ == 0)
+    status = cudaErrorLaunchFailure;
+  Throw(status);
+}
+
+template <class F>
+void Session::Timed(int cls, F launch) {
+  if (!profiling_) {
+    launch();
+    return;
+  }
+  while (events_.size() < events_used_ + 2) {
+    cudaEvent_t e;
+    Check(cudaEventCreate(&e));
+    events_.push_back(e);
+  }
+  cudaEvent_t a = events_[events_used_++], b = events_[events_used_++];
+  Check(cudaEventRecord(a, stream_));
+  launch();
+  Check(cudaEventRecord(b, stream_));
+  pending_.push_back({cls, a, b});
+}
+
+void Session::CollectProfile() {
+  for (const auto& p : pending_) {
+    float ms = 0;
+    Check(cudaEventElapsedTime(&ms, p.start, p.end));
+    profile_ms_[p.cls] += ms;
+    profile_launches_[p.cls] += 1;
+  }
+  pending_.clear();
+  events_used_ = 0;
+}
+
+void Session::TakeProfile(double* ms, long long* launches) {
+  for (int i = 0; i < kProfileClasses; ++i) {
+    if (ms)
+      ms[i] += profile_ms_[i];
+    if (launches)
+      launches[i] += profile_launches_[i];
+    profile_ms_[i] = 0;
+    profile_launches_[i] = 0;
+  }
+}
+
+// ---- decode round -------------------------------------------------------------
+
+// Launches one projection of the round's rows (split input x).
+static cudaError_t RunGemv(GemvParams p, int sms, float* partials,
+                           unsigned* tickets, cudaStream_t stream) {
+  p.chunks = p.K / 256;
+  if (p.kind == kGemvPlain) {
+    int tiles = 0;
+    for (int j = 0; j < p.n_out; ++j) {
+      p.first_tile[j] = tiles;
+      tiles += CeilDiv(p.o[j].rows, kGemvRows);
+    }
+    p.first_tile[p.n_out] = tiles;
+    p.tiles = tiles;
+  } else if (p.kind == kGemvSwiGLU) {
+    p.tiles = CeilDiv(p.o[0].rows, 32);
+  } else {
+    p.tiles = CeilDiv(p.H, 16);
+  }
+  p.partials = partials;
+  p.tickets = tickets;
+  const int units = p.tiles * p.chunks;
+  return launch_q8_gemv(p, gemv_grid(units, sms), stream, true);
+}
+
+static GemvOutput Out(const lfm3_tensor& w, float* out, int ld) {
+  return {static_cast<const uint8_t*>(w.data), out, int(w.rows), ld};
+}
+
+void Session::LaunchLmHead(const void* split_rows, int rows, float* out) {
+  const auto& w = model_->weights();
+  const auto& c = w.config;
+  GemvParams p{};
+  p.kind = kGemvPlain;
+  p.K = c.hidden;
+  p.tokens = rows;
+  p.n_out = 1;
+  p.o[0] = Out(w.output, out, c.vocab);
+  p.x = split_rows;
+  Check(RunGemv(p, model_->sms(), gemv_partials_.as<float>(),
+                gemv_tickets_.as<unsigned>(), stream_));
+}
+
+void Session::DecodeRound(std::span<Session* const> batch,
+                          std::span<const uint32_t> tokens, bool logits) {
+  const auto& w = model_->weights();
+  const auto& c = w.config;
+  const int B = int(batch.size());
+  const int H = c.hidden, F = c.intermediate, A = c.heads * 128;
+  cudaStream_t s = stream_;
+  const int sms = model_->sms();
+  float* partials = gemv_partials_.as<float>();
+  unsigned* tickets = gemv_tickets_.as<unsigned>();
+  const auto gemv = [&](GemvParams p) {
+    Timed(kDecodeProjection,
+          [&] { Check(RunGemv(p, sms, partials, tickets, s)); });
+  };
+  // the rows of this round
+  Check(cudaStreamSynchronize(s));  // host_rows_ is reused between rounds
+  DecodeRows& rows = *host_rows_;
+  rows.count = B;
+  for (int r = 0; r < B; ++r) {
+    rows.position[r] = int(batch[r]->position_);
+    rows.token[r] = tokens[r];
+    rows.layers[r] = batch[r]->layer_table_.as<LayerState>();
+  }
+  const DecodeRows* dev_rows = rows_.as<DecodeRows>();
+  Check(cudaMemcpyAsync(rows_.data(), &rows, sizeof(DecodeRows),
+                        cudaMemcpyHostToDevice, s));
+  float* x = x_.as<float>();
+  float* out = out_.as<float>();
+  void* z = z_split_.data();
+  Timed(kRowKernels, [&] {
+    Check(launch_embed_norm(w.embedding.data, w.embedding.type, nullptr,
+                            reinterpret_cast<const uint32_t*>(
+                                reinterpret_cast<const char*>(dev_rows) +
+                                offsetof(DecodeRows, token)),
+                            x, static_cast<const float*>(w.layers[0].norm.data),
+                            NormOut{nullptr, z, nullptr, nullptr}, B, H, c.eps,
+                            s, true));
+  });
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    const auto& l = w.layers[i];
+    if (c.layer_type[i] == LFM3_CONV) {
+      GemvParams p{};
+      p.kind = kGemvConv;
+      p.K = H;
+      p.tokens = B;
+      p.n_out = 1;
+      p.o[0] = Out(l.in_proj, nullptr, 0);
+      p.x = z;
+      p.split_out = a_split_.data();
+      p.split_width = H;
+      p.conv_w = static_cast<const float*>(l.conv.data);
+      p.rows = dev_rows;
+      p.layer = int(i);
+      p.H = H;
+      p.L = int(c.conv_width);
+      gemv(p);
+      GemvParams o{};
+      o.kind = kGemvPlain;
+      o.K = H;
+      o.tokens = B;
+      o.n_out = 1;
+      o.o[0] = Out(l.out_proj, out, H);
+      o.x = a_split_.data();
+      gemv(o);
+    } else {
+      const int kv = int(c.kv_heads[i]) * 128;
+      GemvParams p{};
+      p.kind = kGemvPlain;
+      p.K = H;
+      p.tokens = B;
+      p.n_out = 4;
+      p.o[0] = Out(l.q, q_.as<float>(), A);
+      p.o[1] = Out(l.k, k_.as<float>(), kv);
+      p.o[2] = Out(l.v, v_.as<float>(), kv);
+      p.o[3] = Out(l.attn_gate, gate_.as<float>(), c.heads);
+      p.x = z;
+      gemv(p);
+      const bool swa = c.layer_type[i] == LFM3_SLIDING_ATTENTION;
+      DecodeAttentionParams ap{};
+      ap.q = q_.as<float>();
+      ap.k = k_.as<float>();
+      ap.v = v_.as<float>();
+      ap.gate = gate_.as<float>();
+      ap.ldq = A;
+      ap.ldk = kv;
+      ap.ldg = c.heads;
+      ap.q_norm = static_cast<const float*>(l.q_norm.data);
+      ap.k_norm = static_cast<const float*>(l.k_norm.data);
+      ap.freq = model_->frequencies(swa);
+      ap.factors = swa ? nullptr : static_cast<const float*>(w.rope_freqs.data);
+      ap.rows = dev_rows;
+      ap.layer = int(i);
+      ap.heads = c.heads;
+      ap.kv_heads = int(c.kv_heads[i]);
+      ap.window = swa ? int(c.window) : 0;
+      ap.eps = c.eps;
+      ap.out_split = a_split_.data();
+      ap.partials = attn_partials_.as<float>();
+      ap.tickets = attn_tickets_.as<unsigned>();
+      Timed(kDecodeAttention,
+            [&] { Check(launch_decode_attention(ap, B, s, true)); });
+      GemvParams o{};
+      o.kind = kGemvPlain;
+      o.K = A;
+      o.tokens = B;
+      o.n_out = 1;
+      o.o[0] = Out(l.attn_out, out, H);
+      o.x = a_split_.data();
+      gemv(o);
+    }
+    Timed(kRowKernels, [&] {
+      Check(launch_residual_norm(
+          out, static_cast<const float*>(l.post_norm.data), x,
+          static_cast<const float*>(l.ffn_norm.data),
+          NormOut{nullptr, z, nullptr, nullptr}, B, H, c.eps, s, true));
+    });
+    GemvParams f{};
+    f.kind = kGemvSwiGLU;
+    f.K = H;
+    f.tokens = B;
+    f.n_out = 2;
+    f.o[0] = Out(l.gate, nullptr, 0);
+    f.o[1] = Out(l.up, nullptr, 0);
+    f.x = z;
+    f.split_out = h_split_.data();
+    f.split_width = F;
+    gemv(f);
+    GemvParams d{};
+    d.kind = kGemvPlain;
+    d.K = F;
+    d.tokens = B;
+    d.n_out = 1;
+    d.o[0] = Out(l.down, out, H);
+    d.x = h_split_.data();
+    gemv(d);
+    const bool last = i + 1 == c.n_layers;
+    const float* next = static_cast<const float*>(
+        last ? w.output_norm.data : w.layers[i + 1].norm.data);
+    Timed(kRowKernels, [&] {
+      Check(launch_residual_norm(
+          out, static_cast<const float*>(l.post_ffn_norm.data), x, next,
+          NormOut{last ? z32_.as<float>() : nullptr, z, nullptr, nullptr}, B,
+          H, c.eps, s, true));
+    });
+  }
+  if (logits)
+    Timed(kDecodeProjection,
+          [&] { LaunchLmHead(z, B, batch_logits_.as<float>()); });
+  for (int r = 0; r < B; ++r) {
+    Session* row = batch[r];
+    Check(cudaMemcpyAsync(row->frontier_.data(), z32_.as<float>() + size_t(r) * H,
+                          size_t(H) * 4, cudaMemcpyDeviceToDevice, s));
+    if (logits)
+      Check(cudaMemcpyAsync(row->logits_.data(),
+                            batch_logits_.as<float>() + size_t(r) * c.vocab,
+                            size_t(c.vocab) * 4, cudaMemcpyDeviceToDevice, s));
+  }
+}
+
+// ---- prompt pass --------------------------------------------------------------
+void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
+  const auto& w = model_->weights();
+  const auto& c = w.config;
+  const int n = int(tokens.size());
+  const int H = c.hidden, F = c.intermediate, A = c.heads * 128;
+  const int L = int(c.n_layers);
+  cudaStream_t s = stream_;
+  Check(cudaMemcpyAsync(ids_.data(), tokens.data(), tokens.size_bytes(),
+                        cudaMemcpyHostToDevice, s));
+  // live rows (engine.cpp:304-323): after the last full-attention layer
+  // only the frontier row, plus conv_width - 1 rows per trailing conv.
+  std::vector<int> live_in(L, n), live_out(L, n);
+  {
+    int need = 1;
+    for (int i = L; i-- > 0;) {
+      if (c.layer_type[i] == LFM3_SLIDING_ATTENTION)
+        break;
+      live_out[i] = std::min(n, need);
+      if (c.layer_type[i] == LFM3_FULL_ATTENTION)
+        break;
+      need = std::min(n, need + int(c.conv_width) - 1);
+      live_in[i] = need;
+    }
+  }
+  float* x = x_.as<float>();
+  float* out = out_.as<float>();
+  __half* half = half_.as<__half>();
+  float* scale = scale_.as<float>();
+  const auto half_at = [&](int row, int width) { return half + size_t(row) * width; };
+  const auto prefill = [&](PrefillParams p) {
+    Timed(kPromptProjection, [&] { Check(launch_q8_prefill(p, s)); });
+  };
+  const auto other = [&](auto launch) { Timed(kPromptOther, launch); };
+  const auto rows = [&](auto launch) { Timed(kRowKernels, launch); };
+  const auto plain = [&](int K, int rows, int first_row,
+                         std::initializer_list<PrefillOutput> outs) {
+    PrefillParams p{};
+    p.kind = kPrefillPlain;
+    p.K = K;
+    p.tokens = rows;
+    p.n_out = int(outs.size());
+    int tiles = 0, j = 0;
+    for (const auto& o : outs) {
+      p.o[j] = o;
+      p.first_tile[j] = tiles;
+      tiles += CeilDiv(o.rows, 128);
+      ++j;
+    }
+    p.first_tile[j] = tiles;
+    p.row_tiles = tiles;
+    p.x = half_at(first_row, K);
+    p.scale = scale + first_row;
+    prefill(p);
+  };
+  const auto pout = [](const lfm3_tensor& t, float* o, int ld) {
+    return PrefillOutput{static_cast<const uint8_t*>(t.data), o, int(t.rows),
+                         ld};
+  };
+  // embedding + first norm over layer 0's input rows
+  {
+    const int o_in = n - live_in[0];
+    rows([&] {
+      Check(launch_embed_norm(w.embedding.data, w.embedding.type,
+                              ids_.as<uint32_t>(), nullptr, x, nullptr,
+                              NormOut{}, n, H, c.eps, s, false));
+    });
+    rows([&] {
+      Check(launch_residual_norm(
+          nullptr, nullptr, x + size_t(o_in) * H,
+          static_cast<const float*>(w.layers[0].norm.data),
+          NormOut{nullptr, nullptr, half_at(o_in, H), scale + o_in},
+          live_in[0], H, c.eps, s, false));
+    });
+  }
+  for (int i = 0; i < L; ++i) {
+    const auto& l = w.layers[i];
+    const int rows_in = live_in[i], rows_out = live_out[i];
+    const int o_in = n - rows_in, o = n - rows_out;
+    if (c.layer_type[i] == LFM3_CONV) {
+      float* p = p_.as<float>();
+      plain(H, rows_in, o_in, {pout(l.in_proj, p + size_t(o_in) * 3 * H, 3 * H)});
+      float* a = a_.as<float>();
+      other([&] {
+        Check(launch_short_conv(p + size_t(o_in) * 3 * H,
+                                static_cast<const float*>(l.conv.data),
+                                states_[i].conv.as<float>(),
+                                a + size_t(o_in) * H, rows_in, H,
+                                int(c.conv_width), true, s));
+      });
+      other([&] {
+        Check(launch_half_rows(a + size_t(o) * H, nullptr, half_at(o, H),
+                               scale + o, rows_out, H, s));
+      });
+      plain(H, rows_out, o, {pout(l.out_proj, out + size_t(o) * H, H)});
+    } else {
+      const int kvh = int(c.kv_heads[i]), kv = kvh * 128;
+      const size_t stride = size_t(kv);
+      const bool swa = c.layer_type[i] == LFM3_SLIDING_ATTENTION;
+      float *q = q_.as<float>(), *k = k_.as<float>(), *v = v_.as<float>(),
+            *g = gate_.as<float>();
+      plain(H, n, 0,
+            {pout(l.q, q, A), pout(l.k, k, kv), pout(l.v, v, kv),
+             pout(l.attn_gate, g, c.heads)});
+      auto& st = states_[i];
+      // full-attention rows never wrap: pack them in place in the cache
+      __half* kc = swa ? chunk_k_.as<__half>()
+                       : st.k.as<__half>() + size_t(position_) * stride;
+      __half* vc = swa ? chunk_v_.as<__half>()
+                       : st.v.as<__half>() + size_t(position_) * stride;
+      other([&] {
+        Check(launch_prompt_heads(
+            q, k, v, A, kv, static_cast<const float*>(l.q_norm.data),
+            static_cast<const float*>(l.k_norm.data), model_->frequencies(swa),
+            swa ? nullptr : static_cast<const float*>(w.rope_freqs.data), kc,
+            vc, n, c.heads, kvh, int(position_), c.eps, s));
+      });
+      const int skip = n - std::min(n, rows_out);
+      float* a = a_.as<float>();
+      Timed(kPromptAttention, [&] {
+        Check(launch_prompt_attention(
+            q + size_t(skip) * A, A, kc + size_t(skip) * stride,
+            vc + size_t(skip) * stride, st.k.as<__half>(), st.v.as<__half>(),
+            g + size_t(skip) * c.heads, c.heads, a + size_t(skip) * A,
+            n - skip, c.heads, kvh, int(position_) + skip, int(st.capacity),
+            swa ? int(c.window) : 0, prompt_scratch_.as<float>(), s));
+      });
+      if (swa)
+        other([&] {
+          Check(launch_store_kv(kc, vc, st.k.as<__half>(), st.v.as<__half>(),
+                                n, kv, int(position_), int(st.capacity), s));
+        });
+      other([&] {
+        Check(launch_half_rows(a + size_t(o) * A, nullptr, half_at(o, A),
+                               scale + o, rows_out, A, s));
+      });
+      plain(A, rows_out, o, {pout(l.attn_out, out + size_t(o) * H, H)});
+    }
+    rows([&] {
+      Check(launch_residual_norm(
+          out + size_t(o) * H, static_cast<const float*>(l.post_norm.data),
+          x + size_t(o) * H, static_cast<const float*>(l.ffn_norm.data),
+          NormOut{nullptr, nullptr, half_at(o, H), scale + o}, rows_out, H,
+          c.eps, s, false));
+    });
+    {
+      float* ff = ff_.as<float>();
+      unsigned* row_max = row_max_.as<unsigned>();
+      Check(cudaMemsetAsync(row_max + o, 0, size_t(rows_out) * 4, s));
+      PrefillParams p{};
+      p.kind = kPrefillSwiGLU;
+      p.K = H;
+      p.tokens = rows_out;
+      p.n_out = 2;
+      p.o[0] = pout(l.gate, ff + size_t(o) * F, F);
+      p.o[1] = pout(l.up, nullptr, F);
+      p.row_tiles = CeilDiv(F, 64);
+      p.x = half_at(o, H);
+      p.scale = scale + o;
+      p.row_max = row_max + o;
+      prefill(p);
+      other([&] {
+        Check(launch_half_rows(ff + size_t(o) * F, row_max + o,
+                               half_at(o, F), scale + o, rows_out, F, s));
+      });
+      plain(F, rows_out, o, {pout(l.down, out + size_t(o) * H, H)});
+    }
+    const bool last = i + 1 == L;
+    rows([&] {
+      Check(launch_residual_norm(
+          out + size_t(o) * H,
+          static_cast<const float*>(l.post_ffn_norm.data), x + size_t(o) * H,
+          last ? nullptr
+               : static_cast<const float*>(w.layers[i + 1].norm.data),
+          NormOut{nullptr, nullptr, last ? nullptr : half_at(o, H),
+                  last ? nullptr : scale + o},
+          rows_out, H, c.eps, s, false));
+    });
+  }
+  // frontier = output_norm(last row); logits from it when asked
+  rows([&] {
+    Check(launch_residual_norm(
+        nullptr, nullptr, x + size_t(n - 1) * H,
+        static_cast<const float*>(w.output_norm.data),
+        NormOut{frontier_.as<float>(), z_split_.data(), nullptr, nullptr}, 1,
+        H, c.eps, s, false));
+  });
+  if (want_logits)
+    Timed(kDecodeProjection,
+          [&] { LaunchLmHead(z_split_.data(), 1, logits_.as<float>()); });
+}
+
+void Session::EnsureLogits() {
+  if (logits_ready_)
+    return;
+  const auto& c = model_->config();
+  Check(launch_split_rows(frontier_.as<float>(), z_split_.data(), 1,
+                          int(c.hidden), stream_));
+  LaunchLmHead(z_split_.data(), 1, logits_.as<float>());
+  Check(cudaStreamSynchronize(stream_));
+  logits_ready_ = true;
+}
+
+// ---- public API -----------------------------------------------------------------
+bool Session::Forward(std::span<const uint32_t> tokens, std::span<float> logits,
+                      std::string* error) {
+  const auto& c = model_->config();
+  try {
+    if (poisoned_)
+      throw std::runtime_error("session is poisoned; Reset it first");
+    if (!logits.empty() && logits.size() != c.vocab)
+      throw std::invalid_argument("logits must hold vocab floats");
+    if (tokens.empty())
+      throw std::invalid_argument("no tokens");
+    if (size_t(position_) + tokens.size() > context_)
+      throw std::invalid_argument("LFM3 context overflow");
+    for (uint32_t t : tokens)
+      if (t >= c.vocab)
+        throw std::invalid_argument("invalid LFM3 token");
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+  try {
+    for (size_t first = 0; first < tokens.size(); first += kPrefillChunk) {
+      const auto chunk = tokens.subspan(
+          first, std::min(kPrefillChunk, tokens.size() - first));
+      const bool last = first + chunk.size() == tokens.size();
+      if (chunk.size() == 1) {
+        Session* self = this;
+        DecodeRound({&self, 1}, chunk, last && !logits.empty());
+      } else {
+        Prompt(chunk, last && !logits.empty());
+      }
+      Check(cudaStreamSynchronize(stream_));
+      if (const unsigned e = take_device_error())
+        throw std::runtime_error("device wait gave up, code " +
+                                 std::to_string(e));
+      CollectProfile();
+      position_ += uint32_t(chunk.size());
+    }
+    logits_ready_ = !logits.empty();
+    if (!logits.empty())
+      Check(cudaMemcpy(logits.data(), logits_.data(), logits.size_bytes(),
+                       cudaMemcpyDeviceToHost));
+    return true;
+  } catch (const std::exception& e) {
+    poisoned_ = true;
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::ForwardBatch(std::span<Session* const> sessions,
+                           std::span<const uint32_t> tokens,
+                           std::span<const std::span<float>> logits,
+                           std::string* error) {
+  return Batch(sessions, tokens, logits, false, error);
+}
+
+bool Session::ForwardBatchInputs(std::span<Session* const> sessions,
+                                 std::span<const uint32_t> tokens, bool logits,
+                                 std::string* error) {
+  return Batch(sessions, tokens, {}, logits, error);
+}
+
+bool Session::Batch(std::span<Session* const> sessions,
+                    std::span<const uint32_t> tokens,
+                    std::span<const std::span<float>> logits,
+                    bool device_logits, std::string* error) {
+  // every check before any mutation (engine.cpp:1178-1199)
+  try {
+    if (sessions.empty() || sessions.size() > kMaxBatch)
+      throw std::invalid_argument("batch must hold 1..8 sessions");
+    if (tokens.size() != sessions.size() ||
+        (!logits.empty() && logits.size() != sessions.size()))
+      throw std::invalid_argument("one token (and logits span) per session");
+    const auto& model = sessions.front()->model_;
+    std::unordered_set<const Session*> seen;
+    for (size_t r = 0; r < sessions.size(); ++r) {
+      const Session* s = sessions[r];
+      if (!s || s->model_ != model)
+        throw std::invalid_argument("batch sessions must share one model");
+      if (!seen.insert(s).second)
+        throw std::invalid_argument("duplicate batch session");
+      if (s->poisoned_)
+        throw std::runtime_error("batch session is poisoned");
+      if (s->position_ >= s->context_)
+        throw std::invalid_argument("LFM3 context overflow");
+      if (tokens[r] >= model->config().vocab)
+        throw std::invalid_argument("invalid LFM3 token");
+      if (!logits.empty() && !logits[r].empty() &&
+          logits[r].size() != model->config().vocab)
+        throw std::invalid_argument("logits must hold vocab floats");
+    }
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+  Session* front = sessions.front();
+  bool want = device_logits;
+  for (const auto& l : logits)
+    want = want || !l.empty();
+  try {
+    // all sessions' earlier work must be done before the front stream
+    // touches their state
+    for (Session* s : sessions)
+      if (s != front)
+        front->Check(cudaStreamSynchronize(s->stream_));
+    front->DecodeRound(sessions, tokens, want);
+    for (size_t r = 0; r < logits.size(); ++r)
+      if (!logits[r].empty())
+        front->Check(cudaMemcpyAsync(logits[r].data(),
+                                     sessions[r]->logits_.data(),
+                                     logits[r].size_bytes(),
+                                     cudaMemcpyDeviceToHost, front->stream_));
+    front->Check(cudaStreamSynchronize(front->stream_));
+    if (const unsigned e = take_device_error())
+      throw std::runtime_error("device wait gave up, code " +
+                               std::to_string(e));
+    front->CollectProfile();
+    for (size_t r = 0; r < sessions.size(); ++r) {
+      sessions[r]->position_ += 1;
+      sessions[r]->logits_ready_ = want;
+    }
+    return true;
+  } catch (const std::exception& e) {
+    for (Session* s : sessions)
+      s->poisoned_ = true;
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::ReadHidden(std::span<float> hidden, std::string* error) {
+  try {
+    if (hidden.size() != model_->config().hidden)
+      throw std::invalid_argument("hidden must hold hidden floats");
+    Check(cudaStreamSynchronize(stream_));
+    Check(cudaMemcpy(hidden.data(), frontier_.data(), hidden.size_bytes(),
+                     cudaMemcpyDeviceToHost));
+    return true;
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::ReadLogits(std::span<float> logits, std::string* error) {
+  try {
+    if (poisoned_)
+      throw std::runtime_error("session is poisoned");
+    if (logits.size() != model_->config().vocab)
+      throw std::invalid_argument("logits must hold vocab floats");
+    if (!position_)
+      throw std::runtime_error("no row advanced yet");
+    EnsureLogits();
+    Check(cudaMemcpy(logits.data(), logits_.data(), logits.size_bytes(),
+                     cudaMemcpyDeviceToHost));
+    return true;
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::Reset(std::string* error) {
+  try {
+    Throw(cudaStreamSynchronize(stream_));
+    const auto& c = model_->config();
+    for (size_t i = 0; i < states_.size(); ++i)
+      if (states_[i].conv.data())
+        Throw(cudaMemsetAsync(states_[i].conv.data(), 0,
+                              size_t(c.hidden) * (c.conv_width - 1) * 4,
+                              stream_));
+    Throw(cudaStreamSynchronize(stream_));
+    position_ = 0;
+    logits_ready_ = false;
+    poisoned_ = false;
+    inject_after_ = 0;
+    return true;
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+void* Session::ContinuationData(ContinuationTensor tensor, size_t layer) const {
+  switch (tensor) {
+    case ContinuationTensor::kLogits:
+      return logits_.data();
+    case ContinuationTensor::kFrontier:
+      return frontier_.data();
+    case ContinuationTensor::kConvolution:
+      return layer < states_.size() ? states_[layer].conv.data() : nullptr;
+    case ContinuationTensor::kKey:
+      return layer < states_.size() ? states_[layer].k.data() : nullptr;
+    case ContinuationTensor::kValue:
+      return layer < states_.size() ? states_[layer].v.data() : nullptr;
+  }
+  return nullptr;
+}
+
+uint32_t Session::RingCapacity(size_t layer) const {
+  return layer < states_.size() ? states_[layer].capacity : 0;
+}
+
+// ---- snapshot v2 (engine.cpp:1387-1574) ---------------------------------------
+namespace {
+constexpr uint32_t kSnapshotMagic = 0x334d464c, kSnapshotVersion = 2;
+constexpr size_t kSnapshotHeaderBytes = 32;
+void PutWord(uint8_t* data, size_t word, uint32_t value) {
+  for (int i = 0; i < 4; ++i)
+    data[word * 4 + i] = uint8_t(value >> (i * 8));
+}
+uint32_t GetWord(const uint8_t* data, size_t word) {
+  uint32_t value = 0;
+  for (int i = 0; i < 4; ++i)
+    value |= uint32_t(data[word * 4 + i]) << (i * 8);
+  return value;
+}
+// FNV-1a over the geometry that fixes the payload layout.
+uint32_t Signature(const lfm3_config& c, uint32_t context) {
+  uint32_t h = 2166136261u;
+  const auto mix = [&](uint32_t v) {
+    for (int i = 0; i < 4; ++i) {
+      h ^= (v >> (8 * i)) & 0xffu;
+      h *= 16777619u;
+    }
+  };
+  mix(c.hidden);
+  mix(c.vocab);
+  mix(c.n_layers);
+  mix(c.head_dim);
+  mix(c.conv_width);
+  mix(c.window);
+  mix(context);
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    mix(c.layer_type[i]);
+    mix(c.kv_heads[i]);
+  }
+  return h;
+}
+size_t RowsKept(uint32_t position, uint32_t capacity) {
+  return std::min(position, capacity);
+}
+}  // namespace
+
+size_t Session::SnapshotBytes() const {
+  const auto& c = model_->config();
+  size_t bytes = kSnapshotHeaderBytes + size_t(c.hidden) * 4 + size_t(c.vocab) * 4;
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    if (c.layer_type[i] == LFM3_CONV)
+      bytes += size_t(c.hidden) * (c.conv_width - 1) * 4;
+    else
+      bytes += 2 * RowsKept(position_, states_[i].capacity) * c.kv_heads[i] *
+               128 * 2;
+  }
+  return bytes;
+}
+
+std::vector<uint8_t> Session::SaveSnapshot() {
+  const auto& c = model_->config();
+  std::vector<uint8_t> out(SnapshotBytes());
+  if (position_ && !poisoned_)
+    EnsureLogits();
+  Throw(cudaStreamSynchronize(stream_));
+  uint8_t* p = out.data();
+  PutWord(p, 0, kSnapshotMagic);
+  PutWord(p, 1, kSnapshotVersion);
+  PutWord(p, 2, context_);
+  PutWord(p, 3, position_);
+  PutWord(p, 4, c.hidden);
+  PutWord(p, 5, c.vocab);
+  PutWord(p, 6, c.n_layers);
+  PutWord(p, 7, Signature(c, context_));
+  p += kSnapshotHeaderBytes;
+  Throw(cudaMemcpy(p, frontier_.data(), size_t(c.hidden) * 4,
+                   cudaMemcpyDeviceToHost));
+  p += size_t(c.hidden) * 4;
+  Throw(cudaMemcpy(p, logits_.data(), size_t(c.vocab) * 4,
+                   cudaMemcpyDeviceToHost));
+  p += size_t(c.vocab) * 4;
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    const auto& s = states_[i];
+    if (c.layer_type[i] == LFM3_CONV) {
+      const size_t bytes = size_t(c.hidden) * (c.conv_width - 1) * 4;
+      Throw(cudaMemcpy(p, s.conv.data(), bytes, cudaMemcpyDeviceToHost));
+      p += bytes;
+    } else {
+      const size_t bytes =
+          RowsKept(position_, s.capacity) * c.kv_heads[i] * 128 * 2;
+      Throw(cudaMemcpy(p, s.k.data(), bytes, cudaMemcpyDeviceToHost));
+      p += bytes;
+      Throw(cudaMemcpy(p, s.v.data(), bytes, cudaMemcpyDeviceToHost));
+      p += bytes;
+    }
+  }
+  return out;
+}
+
+bool Session::RestoreSnapshot(std::span<const uint8_t> payload,
+                              std::string* error) {
+  const auto& c = model_->config();
+  try {
+    if (payload.size() < kSnapshotHeaderBytes)
+      throw std::invalid_argument("truncated LFM3 snapshot");
+    const uint8_t* p = payload.data();
+    const uint32_t position = GetWord(p, 3);
+    if (GetWord(p, 0) != kSnapshotMagic || GetWord(p, 1) != kSnapshotVersion ||
+        GetWord(p, 2) != context_ || position > context_ ||
+        GetWord(p, 4) != c.hidden || GetWord(p, 5) != c.vocab ||
+        GetWord(p, 6) != c.n_layers || GetWord(p, 7) != Signature(c, context_))
+      throw std::invalid_argument("invalid LFM3 snapshot header");
+    size_t bytes = kSnapshotHeaderBytes + size_t(c.hidden) * 4 +
+                   size_t(c.vocab) * 4;
+    for (uint32_t i = 0; i < c.n_layers; ++i)
+      bytes += c.layer_type[i] == LFM3_CONV
+                   ? size_t(c.hidden) * (c.conv_width - 1) * 4
+                   : 2 * RowsKept(position, states_[i].capacity) *
+                         c.kv_heads[i] * 128 * 2;
+    if (payload.size() != bytes)
+      throw std::invalid_argument("LFM3 snapshot size mismatch");
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+  try {
+    Throw(cudaStreamSynchronize(stream_));
+    const uint8_t* p = payload.data();
+    const uint32_t position = GetWord(p, 3);
+    p += kSnapshotHeaderBytes;
+    Throw(cudaMemcpy(frontier_.data(), p, size_t(c.hidden) * 4,
+                     cudaMemcpyHostToDevice));
+    p += size_t(c.hidden) * 4;
+    Throw(cudaMemcpy(logits_.data(), p, size_t(c.vocab) * 4,
+                     cudaMemcpyHostToDevice));
+    p += size_t(c.vocab) * 4;
+    for (uint32_t i = 0; i < c.n_layers; ++i) {
+      auto& s = states_[i];
+      if (c.layer_type[i] == LFM3_CONV) {
+        const size_t bytes = size_t(c.hidden) * (c.conv_width - 1) * 4;
+        Throw(cudaMemcpy(s.conv.data(), p, bytes, cudaMemcpyHostToDevice));
+        p += bytes;
+      } else {
+        const size_t bytes =
+            RowsKept(position, s.capacity) * c.kv_heads[i] * 128 * 2;
+        Throw(cudaMemcpy(s.k.data(), p, bytes, cudaMemcpyHostToDevice));
+        p += bytes;
+        Throw(cudaMemcpy(s.v.data(), p, bytes, cudaMemcpyHostToDevice));
+        p += bytes;
+      }
+    }
+    position_ = position;
+    logits_ready_ = position > 0;
+    poisoned_ = false;
+    return true;
+  } catch (const std::exception& e) {
+    poisoned_ = true;
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+}  // namespace lfm3

@@ -1,0 +1,188 @@
+// Host engine for the LFM3 backbone step on one B200: the C++ counterpart of
+// the reference's Model / Session (engine.hpp:17-163), driving the sm_100a
+// kernels of this library on one CUDA stream per session.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <span>
+#include <string>
+#include <vector>
+
+#include "../../include/lfm3_types.h"
+#include "decode_types.cuh"
+
+namespace lfm3 {
+
+class Session;
+
+// Owns one device allocation.
+class DeviceBuffer {
+public:
+  DeviceBuffer() = default;
+  explicit DeviceBuffer(size_t bytes);
+  ~DeviceBuffer();
+  DeviceBuffer(DeviceBuffer&& other) noexcept;
+  DeviceBuffer& operator=(DeviceBuffer&& other) noexcept;
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(data_);
+  }
+  void* data() const { return data_; }
+  size_t bytes() const { return bytes_; }
+
+private:
+  void* data_ = nullptr;
+  size_t bytes_ = 0;
+};
+
+// Which continuation component ContinuationData returns
+// (engine.hpp:9-15, ContinuationTensor).
+enum class ContinuationTensor { kLogits, kFrontier, kConvolution, kKey, kValue };
+
+class Model : public std::enable_shared_from_this<Model> {
+public:
+  ~Model();
+  // Copies the packed tensors of host weights into 256-byte aligned device
+  // segments (upload.cpp:33-68); tied tensors share one copy. Returns null
+  // with *error set on invalid geometry or a CUDA failure.
+  static std::shared_ptr<Model> Load(const lfm3_weights& host,
+                                     std::string* error = nullptr);
+  std::unique_ptr<Session> CreateSession(uint32_t context,
+                                         std::string* error = nullptr);
+  const lfm3_config& config() const { return device_.config; }
+  // The weights with device payload pointers.
+  const lfm3_weights& weights() const { return device_; }
+  const float* frequencies(bool sliding) const {
+    return freq_.as<float>() + (sliding ? 64 : 0);
+  }
+  int sms() const { return sms_; }
+  // Device bytes of the weight segments.
+  size_t weight_bytes() const { return weight_bytes_; }
+
+private:
+  Model() = default;
+  lfm3_weights device_{};
+  std::vector<DeviceBuffer> segments_;
+  DeviceBuffer freq_;  // [2][64]: global then sliding theta
+  int sms_ = 148;
+  size_t weight_bytes_ = 0;
+  friend class Session;
+};
+
+class Session {
+public:
+  static constexpr size_t kPrefillChunk = 512;  // engine.hpp:47
+  static constexpr size_t kMaxBatch = 8;        // engine.hpp:48
+  ~Session();
+
+  // Advances tokens in passes of at most kPrefillChunk rows and, when
+  // logits is not empty, writes the final row's logits (host memory).
+  // Validates before any mutation; a device error poisons the session
+  // (engine.cpp:882-938).
+  bool Forward(std::span<const uint32_t> tokens, std::span<float> logits = {},
+               std::string* error = nullptr);
+  // One token per independent session (2..8, distinct, same model), sharing
+  // every weight read; logits[i] (host) may be empty (engine.cpp:1160-1216).
+  static bool ForwardBatch(std::span<Session* const> sessions,
+                           std::span<const uint32_t> tokens,
+                           std::span<const std::span<float>> logits,
+                           std::string* error = nullptr);
+  // ForwardBatchInputs (engine.hpp:107-114) for token rows: logits, when
+  // requested, stay in each session's device buffer (ContinuationData
+  // kLogits); DeviceHidden of every session is updated.
+  static bool ForwardBatchInputs(std::span<Session* const> sessions,
+                                 std::span<const uint32_t> tokens, bool logits,
+                                 std::string* error = nullptr);
+  // The final-normed hidden state / logits of the last advanced row.
+  bool ReadHidden(std::span<float> hidden, std::string* error = nullptr);
+  bool ReadLogits(std::span<float> logits, std::string* error = nullptr);
+  const float* DeviceHidden() const { return frontier_.as<float>(); }
+  void* DeviceStream() const { return stream_; }
+  bool Reset(std::string* error = nullptr);
+  uint32_t Position() const { return position_; }
+  bool IsCoherent() const { return !poisoned_; }
+  void* ContinuationData(ContinuationTensor tensor, size_t layer = 0) const;
+  uint32_t RingCapacity(size_t layer) const;
+  // Snapshot v2 (engine.cpp:1387-1574): 32-byte header, frontier, logits,
+  // then per layer the convolution history or K and V rows in physical ring
+  // order.
+  size_t SnapshotBytes() const;
+  std::vector<uint8_t> SaveSnapshot();
+  bool RestoreSnapshot(std::span<const uint8_t> payload,
+                       std::string* error = nullptr);
+  uint32_t context() const { return context_; }
+  const lfm3_config& config() const { return model_->config(); }
+  // Fault injection for tests: the k-th subsequent CUDA call made by this
+  // session's passes reports an error (0 disables).
+  void InjectFailure(int after_calls) { inject_after_ = after_calls; }
+
+  // Optional kernel timing by class, with events around every launch of this
+  // session's passes (and rounds it leads). Events between launches
+  // serialise them, so this is for a separate profiled pass, never for the
+  // headline timing.
+  enum ProfileClass {
+    kDecodeProjection,  // q8_gemv
+    kDecodeAttention,
+    kRowKernels,        // embedding, norms, splits
+    kPromptProjection,  // q8_prefill
+    kPromptAttention,
+    kPromptOther,       // heads, convolution, FP16 rows, ring store
+    kProfileClasses
+  };
+  void SetProfiling(bool on) { profiling_ = on; }
+  // Adds the accumulated milliseconds and launches per class and clears them.
+  void TakeProfile(double* ms, long long* launches);
+
+private:
+  Session(std::shared_ptr<Model> model, uint32_t context);
+  void Check(cudaError_t status);
+  void Prompt(std::span<const uint32_t> tokens, bool logits);
+  void DecodeRound(std::span<Session* const> batch,
+                   std::span<const uint32_t> tokens, bool logits);
+  void EnsureLogits();
+  static bool Batch(std::span<Session* const> sessions,
+                    std::span<const uint32_t> tokens,
+                    std::span<const std::span<float>> logits,
+                    bool device_logits, std::string* error);
+  void LaunchLmHead(const void* split_rows, int rows, float* out);
+
+  std::shared_ptr<Model> model_;
+  cudaStream_t stream_ = nullptr;
+  uint32_t context_ = 0, position_ = 0;
+  bool poisoned_ = false, logits_ready_ = false;
+  int inject_after_ = 0;
+  struct State {
+    DeviceBuffer conv, k, v;
+    uint32_t capacity = 0;
+  };
+  std::vector<State> states_;
+  DeviceBuffer layer_table_;  // LayerState[n_layers]
+  DeviceBuffer frontier_, logits_;
+  // workspace (this session's passes, and rounds it leads)
+  DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_, row_max_,
+      half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
+      chunk_k_, chunk_v_, gemv_partials_, gemv_tickets_, attn_partials_,
+      attn_tickets_, prompt_scratch_;
+  DecodeRows* host_rows_ = nullptr;  // pinned
+  bool profiling_ = false;
+  std::vector<cudaEvent_t> events_;
+  size_t events_used_ = 0;
+  struct Pending {
+    int cls;
+    cudaEvent_t start, end;
+  };
+  std::vector<Pending> pending_;
+  double profile_ms_[kProfileClasses] = {};
+  long long profile_launches_[kProfileClasses] = {};
+  template <class F>
+  void Timed(int cls, F launch);
+  void CollectProfile();
+  friend class Model;
+};
+
+}  // namespace lfm3

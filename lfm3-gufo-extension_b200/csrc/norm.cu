@@ -1,0 +1,318 @@
+// Row kernels: embedding gather, fused residual + sandwich RMSNorm, FP16
+// row scaling, split records. One CTA of 256 threads per row; each thread
+// owns 8 consecutive elements (H <= 2048 x ... in 8-element groups).
+#include "common.cuh"
+#include "norm.cuh"
+#include "kernels.cuh"
+
+namespace lfm3 {
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxGroups = 4;  // 8-element groups per thread: H <= 8192
+
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();
+  if (lane == 0)
+    scratch[warp] = v;
+  __syncthreads();
+  float total = 0;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w)
+    total += scratch[w];
+  return total;
+}
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+  v = warp_max(v);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();
+  if (lane == 0)
+    scratch[warp] = v;
+  __syncthreads();
+  float total = 0;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w)
+    total = fmaxf(total, scratch[w]);
+  return total;
+}
+
+__device__ __forceinline__ int row_exponent(float maximum) {
+  return maximum > 0 ? 14 - ilogbf(maximum) : 0;
+}
+
+// Normalises v (this thread's groups of row `row`) and writes every
+// requested output.
+__device__ void finish_norm(float (&v)[kNormMaxGroups][8], int groups,
+                            const float* norm_w, NormOut out, int row, int H,
+                            float eps, float* scratch) {
+  float squares = 0;
+  for (int j = 0; j < groups; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      squares = fmaf(v[j][i], v[j][i], squares);
+  const float inv = 1.0F / sqrtf(block_sum(squares, scratch) / float(H) + eps);
+  float maximum = 0;
+  for (int j = 0; j < groups; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    const float4 w0 = *reinterpret_cast<const float4*>(norm_w + k0);
+    const float4 w1 = *reinterpret_cast<const float4*>(norm_w + k0 + 4);
+    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[j][i] = (v[j][i] * inv) * w[i];
+      maximum = fmaxf(maximum, fabsf(v[j][i]));
+    }
+  }
+  for (int j = 0; j < groups; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    if (out.f32) {
+      float* dst = out.f32 + size_t(row) * H + k0;
+      *reinterpret_cast<float4*>(dst) =
+          make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      *reinterpret_cast<float4*>(dst + 4) =
+          make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+    }
+    if (out.split)
+      store_split8(out.split, row, H, k0, v[j]);
+  }
+  if (out.half) {
+    const int e = row_exponent(block_max(maximum, scratch));
+    if (threadIdx.x == 0)
+      out.scale[row] = ldexpf(1.0F, -e);
+    for (int j = 0; j < groups; ++j) {
+      const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+      union {
+        __half h[8];
+        uint4 u;
+      } pack;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        pack.h[i] = __float2half_rn(ldexpf(v[j][i], e));
+      *reinterpret_cast<uint4*>(out.half + size_t(row) * H + k0) = pack.u;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+    residual_norm_kernel(const float* __restrict__ branch,
+                         const float* __restrict__ post_w, float* x,
+                         const float* __restrict__ norm_w, NormOut out, int H,
+                         float eps) {
+  __shared__ float scratch[kNormThreads / 32];
+  grid_dependency_wait();
+  allow_dependents();
+  const int row = blockIdx.x, groups = H / 8 / kNormThreads + 1;
+  float v[kNormMaxGroups][8];
+  float b[kNormMaxGroups][8];
+  float* xr = x + size_t(row) * H;
+  int live = 0;
+  for (int j = 0; j < kNormMaxGroups; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    if (j >= groups || k0 >= H)
+      break;
+    live = j + 1;
+    const float4 a0 = *reinterpret_cast<const float4*>(xr + k0);
+    const float4 a1 = *reinterpret_cast<const float4*>(xr + k0 + 4);
+    v[j][0] = a0.x, v[j][1] = a0.y, v[j][2] = a0.z, v[j][3] = a0.w;
+    v[j][4] = a1.x, v[j][5] = a1.y, v[j][6] = a1.z, v[j][7] = a1.w;
+    if (branch) {
+      const float* br = branch + size_t(row) * H + k0;
+      const float4 c0 = *reinterpret_cast<const float4*>(br);
+      const float4 c1 = *reinterpret_cast<const float4*>(br + 4);
+      b[j][0] = c0.x, b[j][1] = c0.y, b[j][2] = c0.z, b[j][3] = c0.w;
+      b[j][4] = c1.x, b[j][5] = c1.y, b[j][6] = c1.z, b[j][7] = c1.w;
+    }
+  }
+  if (branch) {
+    if (post_w) {
+      float squares = 0;
+      for (int j = 0; j < live; ++j)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          squares = fmaf(b[j][i], b[j][i], squares);
+      const float inv =
+          1.0F / sqrtf(block_sum(squares, scratch) / float(H) + eps);
+      for (int j = 0; j < live; ++j) {
+        const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          b[j][i] = (b[j][i] * inv) * post_w[k0 + i];
+      }
+    }
+    for (int j = 0; j < live; ++j) {
+      const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[j][i] = v[j][i] + b[j][i];
+      *reinterpret_cast<float4*>(xr + k0) =
+          make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      *reinterpret_cast<float4*>(xr + k0 + 4) =
+          make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+    }
+  }
+  if (norm_w)
+    finish_norm(v, live, norm_w, out, row, H, eps, scratch);
+}
+
+__device__ __forceinline__ float half_bits(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+    embed_norm_kernel(const uint8_t* __restrict__ table, uint32_t type,
+                      const uint32_t* __restrict__ ids,
+                      const uint32_t* __restrict__ tokens, float* x,
+                      const float* __restrict__ norm_w, NormOut out, int H,
+                      float eps) {
+  __shared__ float scratch[kNormThreads / 32];
+  grid_dependency_wait();
+  allow_dependents();
+  const int row = blockIdx.x, groups = H / 8 / kNormThreads + 1;
+  const uint32_t token = ids ? ids[row] : tokens[row];
+  float v[kNormMaxGroups][8];
+  int live = 0;
+  for (int j = 0; j < kNormMaxGroups; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    if (j >= groups || k0 >= H)
+      break;
+    live = j + 1;
+    if (type == 8) {  // Q8_0: 8 codes of one block
+      const uint8_t* blk = table + size_t(token) * (H / 32) * 34 +
+                           size_t(k0 / 32) * 34;
+      const float d = half_bits(*reinterpret_cast<const uint16_t*>(blk));
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[j][i] = float(int8_t(blk[2 + k0 % 32 + i])) * d;
+    } else if (type == 30 || type == 1) {  // BF16 / F16
+      const uint16_t* r =
+          reinterpret_cast<const uint16_t*>(table) + size_t(token) * H + k0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[j][i] = type == 30 ? __uint_as_float(uint32_t(r[i]) << 16)
+                             : half_bits(r[i]);
+    } else {  // F32
+      const float* r = reinterpret_cast<const float*>(table) +
+                       size_t(token) * H + k0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[j][i] = r[i];
+    }
+    float* xr = x + size_t(row) * H + k0;
+    *reinterpret_cast<float4*>(xr) =
+        make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+    *reinterpret_cast<float4*>(xr + 4) =
+        make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+  }
+  if (norm_w)
+    finish_norm(v, live, norm_w, out, row, H, eps, scratch);
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+    half_rows_kernel(const float* __restrict__ x,
+                     const unsigned* __restrict__ row_max, __half* values,
+                     float* scale, int K) {
+  __shared__ float scratch[kNormThreads / 32];
+  const int row = blockIdx.x;
+  const float* src = x + size_t(row) * K;
+  float maximum;
+  if (row_max) {
+    maximum = __uint_as_float(row_max[row]);
+  } else {
+    float m = 0;
+    for (int k = threadIdx.x; k < K; k += kNormThreads)
+      m = fmaxf(m, fabsf(src[k]));
+    maximum = block_max(m, scratch);
+  }
+  const int e = row_exponent(maximum);
+  if (threadIdx.x == 0)
+    scale[row] = ldexpf(1.0F, -e);
+  for (int k = threadIdx.x; k < K; k += kNormThreads)
+    values[size_t(row) * K + k] = __float2half_rn(ldexpf(src[k], e));
+}
+
+__global__ void split_rows_kernel(const float* __restrict__ x, void* split,
+                                  int rows, int K) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // record index
+  const int per_row = K / 8;
+  if (i >= rows * per_row)
+    return;
+  const int row = i / per_row, k0 = (i % per_row) * 8;
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    v[j] = x[size_t(row) * K + k0 + j];
+  store_split8(split, row, K, k0, v);
+}
+
+cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block,
+                       cudaStream_t stream, bool pdl, void** args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  note_launch();
+  return cudaLaunchKernelExC(&config, func, args);
+}
+
+}  // namespace
+
+cudaError_t launch_residual_norm(const float* branch, const float* post_w,
+                                 float* x, const float* norm_w, NormOut out,
+                                 int rows, int H, float eps,
+                                 cudaStream_t stream, bool pdl) {
+  if (H % 8 || H > kNormThreads * 8 * kNormMaxGroups)
+    return cudaErrorInvalidValue;
+  if (!rows)
+    return cudaSuccess;
+  void* args[] = {&branch, &post_w, &x, &norm_w, &out, &H, &eps};
+  return launch_pdl(reinterpret_cast<const void*>(residual_norm_kernel),
+                    dim3(rows), dim3(kNormThreads), stream, pdl, args);
+}
+
+cudaError_t launch_embed_norm(const void* table, uint32_t type,
+                              const uint32_t* ids, const uint32_t* tokens,
+                              float* x, const float* norm_w, NormOut out,
+                              int rows, int H, float eps, cudaStream_t stream,
+                              bool pdl) {
+  if (H % 32 || H > kNormThreads * 8 * kNormMaxGroups)
+    return cudaErrorInvalidValue;
+  if (!rows)
+    return cudaSuccess;
+  const uint8_t* t = static_cast<const uint8_t*>(table);
+  void* args[] = {&t, &type, &ids, &tokens, &x, &norm_w, &out, &H, &eps};
+  return launch_pdl(reinterpret_cast<const void*>(embed_norm_kernel),
+                    dim3(rows), dim3(kNormThreads), stream, pdl, args);
+}
+
+cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
+                             __half* values, float* scale, int rows, int K,
+                             cudaStream_t stream) {
+  if (!rows)
+    return cudaSuccess;
+  note_launch();
+  half_rows_kernel<<<rows, kNormThreads, 0, stream>>>(x, row_max, values,
+                                                       scale, K);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_rows(const float* x, void* split, int rows, int K,
+                              cudaStream_t stream) {
+  if (K % 8)
+    return cudaErrorInvalidValue;
+  const int records = rows * (K / 8);
+  if (!records)
+    return cudaSuccess;
+  note_launch();
+  split_rows_kernel<<<(records + 255) / 256, 256, 0, stream>>>(x, split, rows,
+                                                               K);
+  return cudaGetLastError();
+}
+
+}  // namespace lfm3

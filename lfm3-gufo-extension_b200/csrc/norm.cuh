@@ -1,0 +1,46 @@
+// Row kernels around the projections: token embedding, the fused
+// residual-add + sandwich RMSNorm, and FP32 -> FP16 row-scaled conversion.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lfm3 {
+
+// Where a normalised row goes. Any subset may be set.
+struct NormOut {
+  float* f32;      // [rows][H] FP32
+  void* split;     // [rows][H / 8] split records (decode projections)
+  __half* half;    // [rows][H] FP16 scaled by 2^e (prompt projections)
+  float* scale;    // [rows] 2^-e for half
+};
+
+// x += RMSNorm_post(branch) (when branch; post_w may be null: plain add),
+// then out = RMSNorm(x) * norm_w (when norm_w). hip/ops.hip:890-970.
+cudaError_t launch_residual_norm(const float* branch, const float* post_w,
+                                 float* x, const float* norm_w, NormOut out,
+                                 int rows, int H, float eps,
+                                 cudaStream_t stream, bool pdl);
+
+// x[r] = embedding row ids[r] (F32 / F16 / BF16 / Q8_0 rows), then out =
+// RMSNorm(x) * norm_w. hip/ops.hip:858-875 fused with the first norm.
+// ids == nullptr takes the token from the decode rows descriptor (tokens).
+cudaError_t launch_embed_norm(const void* table, uint32_t type,
+                              const uint32_t* ids, const uint32_t* tokens,
+                              float* x, const float* norm_w, NormOut out,
+                              int rows, int H, float eps, cudaStream_t stream,
+                              bool pdl);
+
+// FP32 rows -> FP16 scaled so each row's maximum magnitude lies in
+// [2^14, 2^15), with scale 2^-e (hip/q8_prefill.hpp:27-51). With row_max
+// (FP32 bits of each row's maximum, known already) the reduction is skipped
+// (hip/q8_prefill.hpp:52-74).
+cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
+                             __half* values, float* scale, int rows, int K,
+                             cudaStream_t stream);
+
+// FP32 rows -> split records (x = hi + lo, fp16 each).
+cudaError_t launch_split_rows(const float* x, void* split, int rows, int K,
+                              cudaStream_t stream);
+
+}  // namespace lfm3

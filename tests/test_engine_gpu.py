@@ -1,0 +1,174 @@
+"""End-to-end parity of the B200 engine against the CPU oracle (the
+restatement of reference.cpp, itself pinned to the compiled reference), and
+the session invariants of the reference's tests/session_test.cpp: chunked vs
+serial prefill, batched vs serial decode at ragged depths, exact reset,
+snapshots, refusal of invalid input without mutation, poisoning."""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import GOLDEN, ensure_oracle_built, kl, lfm3, top2_margin
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+ensure_oracle_built()
+import oracle  # noqa: E402
+
+# north-star tolerances for Q8_0 logits
+MAX_ABS = 5e-2
+MAX_KL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def small():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    w = lfm3.SyntheticWeights(lfm3.small_config(), seed=0, norm_jitter=0.1)
+    model = lfm3.Model(w.weights)
+    return w, model
+
+
+def test_prompt_and_greedy_match_golden(small):
+    """Prompt pass (40 rows, sliding window 32 wraps) then 20 greedy decode
+    steps against the compiled reference's fixture."""
+    w, model = small
+    g = np.load(os.path.join(GOLDEN, "small.npz"))
+    s = model.session(256)
+    logits = s.forward(g["prompt"])
+    got = [logits]
+    for t in g["generated"]:
+        got.append(s.forward([int(t)]))
+    for step, (a, b) in enumerate(zip(got, g["logits"])):
+        err = float(np.abs(a - b).max())
+        assert err <= MAX_ABS, (step, err)
+        assert kl(b, a) < MAX_KL, step
+        if top2_margin(b) > 4 * err:
+            assert int(np.argmax(a)) == int(np.argmax(b)), step
+
+
+def test_free_running_greedy_matches_oracle(small):
+    w, model = small
+    o = oracle.Oracle(w.weights, 512, threads=4)
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, w.config.vocab, 70).astype(np.uint32)
+    s = model.session(512)
+    ours = s.forward(prompt)
+    ref = o.run(prompt)[len(prompt) - 1]
+    for step in range(24):
+        assert float(np.abs(ours - ref).max()) <= MAX_ABS
+        assert kl(ref, ours) < MAX_KL
+        tok = int(np.argmax(ref))
+        assert int(np.argmax(ours)) == tok or top2_margin(ref) < 1e-3, step
+        ours = s.forward([tok])
+        ref = o.step(tok, True)
+
+
+def test_chunked_matches_serial(small):
+    """513 tokens in one Forward (512 + 1 rows) vs one token at a time
+    (tests/session_test.cpp:117-144)."""
+    w, model = small
+    rng = np.random.default_rng(5)
+    tokens = rng.integers(0, w.config.vocab, 513).astype(np.uint32)
+    a, b = model.session(1024), model.session(1024)
+    batched = a.forward(tokens)
+    serial = None
+    for i, t in enumerate(tokens):
+        serial = b.forward([int(t)], logits=i + 1 == len(tokens))
+    err = float(np.abs(serial - batched).max())
+    assert kl(serial, batched) < 1e-5 and err < 0.02, (kl(serial, batched), err)
+    assert int(np.argmax(serial)) == int(np.argmax(batched))
+    # reset reproduces exact logits
+    a.reset()
+    again = a.forward(tokens)
+    np.testing.assert_array_equal(again, batched)
+
+
+@pytest.mark.parametrize("width", [2, 3, 4, 8])
+def test_batched_matches_serial_at_ragged_depths(small, width):
+    """C2/C3/C4/C8 rounds vs serial decode at depths 1/33/257/513
+    (tests/session_test.cpp:224-283)."""
+    w, model = small
+    rng = np.random.default_rng(9)
+    tokens = rng.integers(0, w.config.vocab, 600).astype(np.uint32)
+    lanes, controls = [], []
+    for row in range(width):
+        count = [1, 33, 257, 513][row % 4]
+        lanes.append(model.session(1024))
+        controls.append(model.session(1024))
+        lanes[-1].forward(tokens[:count], logits=False)
+        controls[-1].forward(tokens[:count], logits=False)
+    worst = 0.0
+    for step in range(3):
+        inputs = [int(tokens[(row + step) % len(tokens)]) for row in range(width)]
+        actual = lfm3.Session.forward_batch(lanes, inputs)
+        for row in range(width):
+            expected = controls[row].forward([inputs[row]])
+            assert lanes[row].position == controls[row].position
+            assert np.isfinite(actual[row]).all()
+            worst = max(worst, float(np.abs(actual[row] - expected).max()))
+            assert int(np.argmax(actual[row])) == int(np.argmax(expected))
+    assert worst < 0.002, worst
+    # a duplicate session is refused without mutating anything
+    boundary = lanes[0].position
+    with pytest.raises(lfm3.Lfm3Error):
+        lfm3.Session.forward_batch([lanes[0], lanes[0]], [1, 2])
+    assert lanes[0].position == boundary and lanes[0].coherent
+
+
+def test_invalid_input_refused_without_mutation(small):
+    w, model = small
+    s = model.session(64)
+    s.forward(list(range(10)), logits=False)
+    with pytest.raises(lfm3.Lfm3Error):
+        s.forward([w.config.vocab])
+    assert s.position == 10
+    with pytest.raises(lfm3.Lfm3Error):
+        s.forward(list(range(60)))  # context overflow
+    assert s.position == 10 and s.coherent
+    with pytest.raises(lfm3.Lfm3Error):
+        model.session(w.config.context + 1)
+
+
+def test_snapshot_round_trip_and_fork(small):
+    w, model = small
+    rng = np.random.default_rng(2)
+    tokens = rng.integers(0, w.config.vocab, 300).astype(np.uint32)
+    a, b = model.session(512), model.session(512)
+    a.forward(tokens[:290])  # sliding rings (32) wrapped
+    snap = a.save_snapshot()
+    before = a.read_logits()
+    a.forward(tokens[290:297], logits=False)
+    a.restore_snapshot(snap)
+    b.restore_snapshot(snap)
+    assert a.position == b.position == 290
+    np.testing.assert_array_equal(a.read_logits(), before)
+    np.testing.assert_array_equal(a.forward(tokens[297:300]),
+                                  b.forward(tokens[297:300]))
+    bad = snap.copy()
+    bad[0] ^= 0x80
+    with pytest.raises(lfm3.Lfm3Error):
+        a.restore_snapshot(bad)
+    with pytest.raises(lfm3.Lfm3Error):
+        a.restore_snapshot(snap[:-1])
+    assert a.position == 293
+
+
+def test_device_failure_poisons_until_reset(small):
+    """A failing CUDA call mid-pass (injected on the host) poisons the
+    session; it refuses work until Reset (engine.cpp:905-927, 1300-1332)."""
+    w, model = small
+    s = model.session(128)
+    s.forward([1, 2, 3], logits=False)
+    s.inject_failure(5)
+    with pytest.raises(lfm3.Lfm3Error):
+        s.forward([4, 5, 6, 7])
+    assert not s.coherent
+    with pytest.raises(lfm3.Lfm3Error):
+        s.forward([4])
+    s.reset()
+    assert s.coherent and s.position == 0
+    fresh = model.session(128)
+    np.testing.assert_array_equal(s.forward([1, 2, 3]), fresh.forward([1, 2, 3]))
+    assert lfm3.library().lfm3_cuda_take_device_error() == 0
