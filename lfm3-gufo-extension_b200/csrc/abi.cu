@@ -71,6 +71,8 @@ int GemvRows(lfm3::GemvParams p, const float* x, int n, int K,
     return Fail(LFM3_ERR_UNSUPPORTED, "projection too tall for the tickets");
   p.partials = ws.partial;
   p.tickets = ws.tickets;
+  if (int e = Cuda(lfm3::fill_gemv_maps(p)))
+    return e;
   const int grid = lfm3::gemv_grid(p.tiles * p.chunks, Sms());
   for (int r0 = 0; r0 < n; r0 += lfm3::kMaxBatch) {
     lfm3::GemvParams q = p;
@@ -376,6 +378,7 @@ int lfm3_cuda_attention(const float* q, const uint16_t* k, const uint16_t* v,
     p.heads = heads;
     p.kv_heads = kv_heads;
     p.window = window;
+    p.max_splits = lfm3::kMaxDecodeSplits;
     p.out_f32 = out;
     p.partials = scratch;
     // tickets live after the partials, zeroed here (they return to zero)

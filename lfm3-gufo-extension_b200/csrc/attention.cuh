@@ -27,6 +27,7 @@ struct DecodeAttentionParams {
   int layer;
   int heads, kv_heads;
   int window;  // 0: full attention
+  int max_splits;  // key spans per (row, KV group), <= kMaxDecodeSplits
   float eps;
   void* out_split;   // [rows][heads * 128] split records
   float* out_f32;    // optional [rows][heads * 128]

@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(kThreads)
   const int capacity = state.capacity;
   const int first = p.window > 0 ? max(0, position + 1 - p.window) : 0;
   const int tiles = (position + 1 - first + kDecodeTile - 1) / kDecodeTile;
-  const int per = (tiles + kMaxDecodeSplits - 1) / kMaxDecodeSplits;
+  const int max_splits = max(1, min(p.max_splits, kMaxDecodeSplits));
+  const int per = (tiles + max_splits - 1) / max_splits;
   const int used = (tiles + per - 1) / per;
   if (split >= used)
     return;

@@ -103,6 +103,19 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src,
       : "memory");
 }
 
+// One tiled TMA copy of a 3-D box at coordinates (x0, x1, x2) of `map` (a
+// __grid_constant__ kernel parameter) completing on bar. x0 * element size
+// must be a multiple of 16 bytes; the weight maps always start x0 at 0.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int x0,
+                                            int x1, int x2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(x1), "r"(x2),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
 // ---- programmatic dependent launch ------------------------------------------
 // Work before grid_dependency_wait() may only touch data that no earlier
 // kernel in the stream writes (weights); everything else comes after it.

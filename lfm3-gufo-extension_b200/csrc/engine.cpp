@@ -15,6 +15,7 @@
 #include <unordered_set>
 
 #include "kernels.cuh"
+#include "tensor_map.hpp"
 
 namespace lfm3 {
 namespace {
@@ -171,6 +172,19 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
       *error = e.what();
     return nullptr;
   }
+}
+
+const CUtensorMap& Model::RowMap(const lfm3_tensor& t, int box_rows) {
+  std::lock_guard<std::mutex> lock(maps_mutex_);
+  const auto key = std::make_pair(t.data, box_rows);
+  auto it = maps_.find(key);
+  if (it == maps_.end()) {
+    CUtensorMap map;
+    Throw(encode_row_map(&map, t.data, size_t(t.cols) / 32 * 34, int(t.rows),
+                         kGemvChunk, box_rows));
+    it = maps_.emplace(key, map).first;
+  }
+  return it->second;
 }
 
 std::unique_ptr<Session> Model::CreateSession(uint32_t context,
@@ -332,9 +346,15 @@ void Session::TakeProfile(double* ms, long long* launches) {
 // ---- decode round -------------------------------------------------------------
 
 // Launches one projection of the round's rows (split input x).
-static cudaError_t RunGemv(GemvParams p, int sms, float* partials,
+static cudaError_t RunGemv(GemvParams p, Model& model, float* partials,
                            unsigned* tickets, cudaStream_t stream) {
+  const int sms = model.sms();
   p.chunks = p.K / 256;
+  const int maps = p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
+  for (int j = 0; j < maps; ++j) {
+    lfm3_tensor t{p.o[j].w, LFM3_Q8_0, uint32_t(p.K), uint32_t(p.o[j].rows), 0};
+    p.maps[j] = model.RowMap(t, gemv_box_rows(p.kind));
+  }
   if (p.kind == kGemvPlain) {
     int tiles = 0;
     for (int j = 0; j < p.n_out; ++j) {
@@ -368,7 +388,7 @@ void Session::LaunchLmHead(const void* split_rows, int rows, float* out) {
   p.n_out = 1;
   p.o[0] = Out(w.output, out, c.vocab);
   p.x = split_rows;
-  Check(RunGemv(p, model_->sms(), gemv_partials_.as<float>(),
+  Check(RunGemv(p, *model_, gemv_partials_.as<float>(),
                 gemv_tickets_.as<unsigned>(), stream_));
 }
 
@@ -384,7 +404,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
   unsigned* tickets = gemv_tickets_.as<unsigned>();
   const auto gemv = [&](GemvParams p) {
     Timed(kDecodeProjection,
-          [&] { Check(RunGemv(p, sms, partials, tickets, s)); });
+          [&] { Check(RunGemv(p, *model_, partials, tickets, s)); });
   };
   // the rows of this round
   Check(cudaStreamSynchronize(s));  // host_rows_ is reused between rounds
@@ -467,6 +487,8 @@ void Session::DecodeRound(std::span<Session* const> batch,
       ap.heads = c.heads;
       ap.kv_heads = int(c.kv_heads[i]);
       ap.window = swa ? int(c.window) : 0;
+      // about two CTAs per SM over the round's (row, group) pairs
+      ap.max_splits = std::max(1, 2 * model_->sms() / (B * int(c.kv_heads[i])));
       ap.eps = c.eps;
       ap.out_split = a_split_.data();
       ap.partials = attn_partials_.as<float>();

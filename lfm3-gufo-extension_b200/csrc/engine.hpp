@@ -5,8 +5,12 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cuda.h>
+
 #include <cstdint>
+#include <map>
 #include <memory>
+#include <mutex>
 #include <span>
 #include <string>
 #include <vector>
@@ -63,6 +67,9 @@ public:
   int sms() const { return sms_; }
   // Device bytes of the weight segments.
   size_t weight_bytes() const { return weight_bytes_; }
+  // The TMA map over a Q8_0 matrix's rows in 272-byte chunks with boxes of
+  // box_rows rows (encoded once, cached).
+  const CUtensorMap& RowMap(const lfm3_tensor& t, int box_rows);
 
 private:
   Model() = default;
@@ -71,6 +78,8 @@ private:
   DeviceBuffer freq_;  // [2][64]: global then sliding theta
   int sms_ = 148;
   size_t weight_bytes_ = 0;
+  std::mutex maps_mutex_;
+  std::map<std::pair<const void*, int>, CUtensorMap> maps_;
   friend class Session;
 };
 

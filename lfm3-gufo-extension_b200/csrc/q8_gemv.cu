@@ -20,8 +20,9 @@
 // between CTAs merges its parts in CTA order in whichever CTA finishes it
 // last (a ticket, not a wait), so results never depend on timing.
 #include "common.cuh"
-#include "q8_gemv.cuh"
 #include "kernels.cuh"
+#include "q8_gemv.cuh"
+#include "tensor_map.hpp"
 
 namespace lfm3 {
 
@@ -36,30 +37,33 @@ struct GemvSmem {
   int last;
 };
 
-// Source row of tile row i, or nullptr past the weights.
-__device__ __forceinline__ const uint8_t* tile_source(const GemvParams& p,
-                                                      int t, int i,
-                                                      size_t row_bytes) {
+// Issues the tiled copies of unit (tile t, chunk c) into `dst`; returns the
+// bytes they deliver (boxes past the matrix are zero-filled and still count).
+__device__ __forceinline__ uint32_t load_unit(const GemvParams& p, int t,
+                                              int c, uint8_t* dst,
+                                              uint64_t* bar) {
+  const int x1 = c * (kGemvChunk / 16);
   if (p.kind == kGemvPlain) {
     int j = 0;
 #pragma unroll
     for (int q = 1; q < 4; ++q)
       if (q < p.n_out && t >= p.first_tile[q])
         j = q;
-    const int row = (t - p.first_tile[j]) * kGemvRows + i;
-    return row < p.o[j].rows ? p.o[j].w + size_t(row) * row_bytes : nullptr;
+    tma_load_3d(dst, &p.maps[j], 0, x1, (t - p.first_tile[j]) * kGemvRows,
+                bar);
+    return kGemvRows * kGemvChunk;
   }
   if (p.kind == kGemvSwiGLU) {
-    const int row = t * 32 + (i & 31);
-    if (row >= p.o[0].rows)
-      return nullptr;
-    return p.o[i < 32 ? 0 : 1].w + size_t(row) * row_bytes;
+    tma_load_3d(dst, &p.maps[0], 0, x1, t * 32, bar);
+    tma_load_3d(dst + 32 * kGemvChunk, &p.maps[1], 0, x1, t * 32, bar);
+    return kGemvRows * kGemvChunk;
   }
   // Conv: rows 0-15 B, 16-31 C, 32-47 x of channels 16t..16t+15
-  const int ch = t * 16 + (i & 15);
-  if (i >= 48 || ch >= p.H)
-    return nullptr;
-  return p.o[0].w + (size_t(i / 16) * p.H + ch) * row_bytes;
+#pragma unroll
+  for (int part = 0; part < 3; ++part)
+    tma_load_3d(dst + part * 16 * kGemvChunk, &p.maps[0], 0, x1,
+                part * p.H + t * 16, bar);
+  return 48 * kGemvChunk;
 }
 
 __device__ __forceinline__ long long unit_begin(long long c, long long units,
@@ -131,62 +135,46 @@ __device__ void gemv_epilogue(const GemvParams& p, const float* tile, int t,
   }
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 1)
-    q8_gemv_kernel(const __grid_constant__ GemvParams p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  GemvSmem& s = *reinterpret_cast<GemvSmem*>(smem_raw);
-  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const long long units = (long long)p.tiles * p.chunks;
-  const long long grid = gridDim.x;
-  const long long u0 = unit_begin(blockIdx.x, units, grid);
-  const long long u1 = unit_begin(blockIdx.x + 1, units, grid);
-  const size_t row_bytes = size_t(p.K / 32) * 34;
-
-  if (tid == 0) {
-    for (int i = 0; i < kGemvStages; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], kGemvWarps);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-  allow_dependents();
-
-  if (warp == kGemvWarps) {
-    // ---- producer: weights only, so it may run ahead of the previous
-    // kernel in the stream
-    int stage = 0;
-    uint32_t phase = 0;
-    for (long long u = u0; u < u1; ++u) {
-      const int t = int(u / p.chunks), c = int(u % p.chunks);
-      if (!mbar_wait(&s.empty[stage], phase ^ 1, kErrGemvEmptyWait))
-        return;
-      const uint8_t* src0 = tile_source(p, t, lane, row_bytes);
-      const uint8_t* src1 = tile_source(p, t, lane + 32, row_bytes);
-      const unsigned n0 = __popc(__ballot_sync(0xffffffffu, src0 != nullptr));
-      const unsigned n1 = __popc(__ballot_sync(0xffffffffu, src1 != nullptr));
-      if (lane == 0)
-        mbar_arrive_expect_tx(&s.full[stage], (n0 + n1) * kGemvChunk);
-      __syncwarp();
-      uint8_t* dst = s.stage[stage];
-      if (src0)
-        bulk_load(dst + lane * kGemvChunk, src0 + size_t(c) * kGemvChunk,
-                  kGemvChunk, &s.full[stage]);
-      if (src1)
-        bulk_load(dst + (lane + 32) * kGemvChunk,
-                  src1 + size_t(c) * kGemvChunk, kGemvChunk, &s.full[stage]);
-      if (++stage == kGemvStages) {
-        stage = 0;
-        phase ^= 1;
+// The block of this warp (codes of rows m * 16 + g and + 8, 8 codes per
+// thread) as MMA A fragments for the chunk's two k16 halves.
+template <bool kAligned, int kMTiles>
+__device__ __forceinline__ void load_block(const uint8_t* base, int g, int cq,
+                                           uint32_t (&a1)[kMTiles][4],
+                                           uint32_t (&a2)[kMTiles][4],
+                                           float (&d)[kMTiles][2]) {
+  uint32_t w[kMTiles][2][2];
+#pragma unroll
+  for (int m = 0; m < kMTiles; ++m)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint8_t* row = base + (m * 16 + g + h * 8) * kGemvChunk;
+      d[m][h] = __half2float(*reinterpret_cast<const __half*>(row));
+      if (kAligned) {
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(row + 2 + 8 * cq);
+        w[m][h][0] = pw[0];
+        w[m][h][1] = pw[1];
+      } else {
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(row + 8 * cq);
+        const uint32_t v0 = pw[0], v1 = pw[1], v2 = pw[2];
+        w[m][h][0] = __funnelshift_r(v0, v1, 16);
+        w[m][h][1] = __funnelshift_r(v1, v2, 16);
       }
     }
-    return;
+#pragma unroll
+  for (int m = 0; m < kMTiles; ++m) {
+    codes_to_half2(w[m][0][0], a1[m][0], a1[m][2]);
+    codes_to_half2(w[m][1][0], a1[m][1], a1[m][3]);
+    codes_to_half2(w[m][0][1], a2[m][0], a2[m][2]);
+    codes_to_half2(w[m][1][1], a2[m][1], a2[m][3]);
   }
+}
 
-  // ---- consumers
-  grid_dependency_wait();
+template <bool kAligned, int kMTiles>
+__device__ __forceinline__ void consume(const GemvParams& p, GemvSmem& s,
+                                        long long u0, long long u1,
+                                        long long units, long long grid,
+                                        int tid, int warp, int lane) {
   const int g = lane / 4, cq = lane % 4;
-  const int mtiles = p.kind == kGemvConv ? 3 : 4;
   const uint4* x = static_cast<const uint4*>(p.x);
   const int records = p.K / 8;
   int stage = 0;
@@ -212,59 +200,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     }
     if (!mbar_wait(&s.full[stage], phase, kErrGemvFullWait))
       return;
-    const uint8_t* base = s.stage[stage] + warp * 34;
+    {
+      uint32_t a1[kMTiles][4], a2[kMTiles][4];
+      float d[kMTiles][2];
+      load_block<kAligned, kMTiles>(s.stage[stage] + warp * 34, g, cq, a1, a2,
+                                    d);
+      __syncwarp();
+      if (lane == 0)
+        mbar_arrive(&s.empty[stage]);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      if (m >= mtiles)
-        break;
-      uint32_t w[2][2];  // [row g / g + 8][codes 0-3 / 4-7]
-      float d[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint8_t* row = base + (m * 16 + g + h * 8) * kGemvChunk;
-        d[h] = __half2float(*reinterpret_cast<const __half*>(row));
-        const uint8_t* q = row + 2 + 8 * cq;
-        // Odd g reads its words in the other order, so a warp's 32 lanes
-        // cover 32 banks (the row pitch is 4 words modulo 32).
-        if (warp & 1) {  // codes start on a word
-          const uint32_t* pw = reinterpret_cast<const uint32_t*>(q);
-          const uint32_t a = pw[g & 1], b = pw[(g & 1) ^ 1];
-          w[h][0] = (g & 1) ? b : a;
-          w[h][1] = (g & 1) ? a : b;
-        } else {  // codes start two bytes into a word
-          const uint32_t* pw = reinterpret_cast<const uint32_t*>(q - 2);
-          uint32_t v0, v1, v2;
-          if (g & 1) {
-            v1 = pw[1];
-            v2 = pw[2];
-            v0 = pw[0];
-          } else {
-            v0 = pw[0];
-            v1 = pw[1];
-            v2 = pw[2];
-          }
-          w[h][0] = __funnelshift_r(v0, v1, 16);
-          w[h][1] = __funnelshift_r(v1, v2, 16);
-        }
+      for (int m = 0; m < kMTiles; ++m) {
+        float cc[4] = {0, 0, 0, 0};
+        mma_f16(cc, a1[m], xh.x, xh.y);
+        mma_f16(cc, a1[m], xl.x, xl.y);
+        mma_f16(cc, a2[m], xh.z, xh.w);
+        mma_f16(cc, a2[m], xl.z, xl.w);
+        acc[m][0] = fmaf(d[m][0], cc[0], acc[m][0]);
+        acc[m][1] = fmaf(d[m][0], cc[1], acc[m][1]);
+        acc[m][2] = fmaf(d[m][1], cc[2], acc[m][2]);
+        acc[m][3] = fmaf(d[m][1], cc[3], acc[m][3]);
       }
-      uint32_t a1[4], a2[4];
-      codes_to_half2(w[0][0], a1[0], a1[2]);
-      codes_to_half2(w[1][0], a1[1], a1[3]);
-      codes_to_half2(w[0][1], a2[0], a2[2]);
-      codes_to_half2(w[1][1], a2[1], a2[3]);
-      float cc[4] = {0, 0, 0, 0};
-      mma_f16(cc, a1, xh.x, xh.y);
-      mma_f16(cc, a1, xl.x, xl.y);
-      mma_f16(cc, a2, xh.z, xh.w);
-      mma_f16(cc, a2, xl.z, xl.w);
-      acc[m][0] = fmaf(d[0], cc[0], acc[m][0]);
-      acc[m][1] = fmaf(d[0], cc[1], acc[m][1]);
-      acc[m][2] = fmaf(d[1], cc[2], acc[m][2]);
-      acc[m][3] = fmaf(d[1], cc[3], acc[m][3]);
     }
-    __syncwarp();
-    if (lane == 0)
-      mbar_arrive(&s.empty[stage]);
     if (++stage == kGemvStages) {
       stage = 0;
       phase ^= 1;
@@ -329,11 +285,85 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   }
 }
 
+
+__global__ void __launch_bounds__(kGemvThreads, 2)
+    q8_gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  GemvSmem& s = *reinterpret_cast<GemvSmem*>(smem_raw);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const long long units = (long long)p.tiles * p.chunks;
+  const long long grid = gridDim.x;
+  const long long u0 = unit_begin(blockIdx.x, units, grid);
+  const long long u1 = unit_begin(blockIdx.x + 1, units, grid);
+  if (tid == 0) {
+    for (int i = 0; i < kGemvStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], kGemvWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  allow_dependents();
+
+  if (warp == kGemvWarps) {
+    // ---- producer: weights only, so it may run ahead of the previous
+    // kernel in the stream
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long u = u0; u < u1; ++u) {
+      const int t = int(u / p.chunks), c = int(u % p.chunks);
+      if (!mbar_wait(&s.empty[stage], phase ^ 1, kErrGemvEmptyWait))
+        return;
+      if (lane == 0) {
+        const uint32_t bytes =
+            p.kind == kGemvConv ? 48 * kGemvChunk : kGemvRows * kGemvChunk;
+        mbar_arrive_expect_tx(&s.full[stage], bytes);
+        load_unit(p, t, c, s.stage[stage], &s.full[stage]);
+      }
+      __syncwarp();
+      if (++stage == kGemvStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    return;
+  }
+
+  // ---- consumers
+  grid_dependency_wait();
+  // Odd warps' blocks start on a word boundary, even warps' two bytes past
+  // one; each variant is straight-line code over the tile's m-tiles.
+  if (warp & 1) {
+    if (p.kind == kGemvConv)
+      consume<true, 3>(p, s, u0, u1, units, grid, tid, warp, lane);
+    else
+      consume<true, 4>(p, s, u0, u1, units, grid, tid, warp, lane);
+  } else {
+    if (p.kind == kGemvConv)
+      consume<false, 3>(p, s, u0, u1, units, grid, tid, warp, lane);
+    else
+      consume<false, 4>(p, s, u0, u1, units, grid, tid, warp, lane);
+  }
+}
+
 }  // namespace
 
 int gemv_grid(int units, int sms) { return units < sms ? units : sms; }
 
 size_t gemv_partial_floats(int grid) { return size_t(grid) * 2 * kGemvTile; }
+
+cudaError_t fill_gemv_maps(GemvParams& p) {
+  const size_t row_bytes = size_t(p.K / 32) * 34;
+  const int outputs = p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
+  for (int j = 0; j < outputs; ++j) {
+    const cudaError_t e =
+        encode_row_map(&p.maps[j], p.o[j].w, row_bytes, p.o[j].rows,
+                       kGemvChunk, gemv_box_rows(p.kind));
+    if (e != cudaSuccess)
+      return e;
+  }
+  return cudaSuccess;
+}
 
 cudaError_t launch_q8_gemv(const GemvParams& p, int grid, cudaStream_t stream,
                            bool pdl) {

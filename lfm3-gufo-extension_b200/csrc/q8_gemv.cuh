@@ -4,6 +4,7 @@
 // convolution-step kernels that follow them (hip/ops.hip:165-182,
 // 1135-1151).
 #pragma once
+#include <cuda.h>
 #include <stdint.h>
 
 #include "decode_types.cuh"
@@ -13,7 +14,7 @@ namespace lfm3 {
 constexpr int kGemvRows = 64;     // weight rows per tile
 constexpr int kGemvBlocks = 8;    // Q8 blocks per stage (256 columns)
 constexpr int kGemvChunk = kGemvBlocks * 34;  // bytes per row per stage
-constexpr int kGemvStages = 6;
+constexpr int kGemvStages = 4;
 constexpr int kGemvWarps = 8;     // consumer warps, one Q8 block each
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
 constexpr int kGemvTile = kGemvRows * kMaxBatch;  // fp32 values per tile
@@ -38,6 +39,10 @@ struct GemvOutput {
 };
 
 struct GemvParams {
+  // TMA maps over the weight rows (tensor_map.hpp), 272-byte chunks: Plain
+  // one per output with 64-row boxes; SwiGLU gate and up with 32-row boxes;
+  // Conv in_proj with 16-row boxes.
+  alignas(64) CUtensorMap maps[4];
   int kind;
   int K;        // columns (multiple of 256)
   int chunks;   // K / 256
@@ -63,5 +68,13 @@ struct GemvParams {
 // Grid size and scratch needs of one launch.
 int gemv_grid(int units, int sms);
 size_t gemv_partial_floats(int grid);
+
+// Box rows of the weight maps each kind reads (per output slot).
+inline int gemv_box_rows(int kind) {
+  return kind == kGemvPlain ? kGemvRows : kind == kGemvSwiGLU ? 32 : 16;
+}
+// Encodes p.maps from p.o[j].w / rows / K (host; for callers without a map
+// cache).
+cudaError_t fill_gemv_maps(GemvParams& p);
 
 }  // namespace lfm3

@@ -1,0 +1,56 @@
+// Host encoding of TMA tensor maps (driver entry point reached through the
+// runtime, so the library needs no direct libcuda link).
+#include "tensor_map.hpp"
+
+#include <mutex>
+
+namespace lfm3 {
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
+                                 void*, const cuuint64_t*, const cuuint64_t*,
+                                 const cuuint32_t*, const cuuint32_t*,
+                                 CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion,
+                                 CUtensorMapFloatOOBfill);
+
+EncodeTiled Encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p,
+                                cudaEnableDefault, &status) == cudaSuccess &&
+        status == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+cudaError_t encode_row_map(CUtensorMap* map, const void* base,
+                           size_t row_bytes, int rows, int chunk_bytes,
+                           int box_rows) {
+  const EncodeTiled encode = Encoder();
+  if (!encode)
+    return cudaErrorNotSupported;
+  if (row_bytes % 16 || chunk_bytes % 16 || chunk_bytes / 16 > 256 ||
+      box_rows < 1 || box_rows > 256 || rows < 1 ||
+      reinterpret_cast<uintptr_t>(base) % 16)
+    return cudaErrorInvalidValue;
+  const cuuint64_t dims[3] = {16, row_bytes / 16, cuuint64_t(rows)};
+  const cuuint64_t strides[2] = {16, row_bytes};
+  const cuuint32_t box[3] = {16, cuuint32_t(chunk_bytes / 16),
+                             cuuint32_t(box_rows)};
+  const cuuint32_t element_strides[3] = {1, 1, 1};
+  const CUresult r = encode(
+      map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims,
+      strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace lfm3
