@@ -123,7 +123,7 @@ def default_config():
     return cfg
 
 
-def small_config(hidden=256, intermediate=512, vocab=1024, heads=4, kv_heads=2,
+def small_config(hidden=512, intermediate=1024, vocab=1024, heads=4, kv_heads=2,
                  window=32, context=4096, pattern="CSGCSG"):
     """A small geometry of the same architecture, for fast tests."""
     cfg = default_config()

@@ -42,7 +42,7 @@ constexpr int kPromptRows = 16;  // hip/ops.hpp:33
 constexpr size_t kTicketWords = 8192;
 
 bool Q8Matrix(const lfm3_tensor* t) {
-  return t && t->data && t->type == LFM3_Q8_0 && t->cols % 256 == 0;
+  return t && t->data && t->type == LFM3_Q8_0 && t->cols % 512 == 0;
 }
 
 // Decode projections of n < 16 FP32 rows: split once, then <= 8 rows per
@@ -50,30 +50,16 @@ bool Q8Matrix(const lfm3_tensor* t) {
 int GemvRows(lfm3::GemvParams p, const float* x, int n, int K,
              const lfm3_dense_workspace& ws, cudaStream_t s,
              std::vector<size_t> out_row_stride) {
-  if (!ws.quantized || !ws.partial || !ws.tickets)
-    return Fail(LFM3_ERR_INVALID, "workspace needs quantized, partial, tickets");
+  if (!ws.quantized)
+    return Fail(LFM3_ERR_INVALID, "workspace needs quantized");
+  p.K = K;
+  if (!lfm3::gemv_plan(p))
+    return Fail(LFM3_ERR_UNSUPPORTED, "projection width not tiled");
   if (int e = Cuda(lfm3::launch_split_rows(x, ws.quantized, n, K, s)))
     return e;
-  p.K = K;
-  p.chunks = K / 256;
-  if (p.kind == lfm3::kGemvPlain) {
-    int tiles = 0;
-    for (int j = 0; j < p.n_out; ++j) {
-      p.first_tile[j] = tiles;
-      tiles += (p.o[j].rows + lfm3::kGemvRows - 1) / lfm3::kGemvRows;
-    }
-    p.first_tile[p.n_out] = tiles;
-    p.tiles = tiles;
-  } else {
-    p.tiles = (p.o[0].rows + 31) / 32;
-  }
-  if (size_t(p.tiles) > kTicketWords)
-    return Fail(LFM3_ERR_UNSUPPORTED, "projection too tall for the tickets");
-  p.partials = ws.partial;
-  p.tickets = ws.tickets;
   if (int e = Cuda(lfm3::fill_gemv_maps(p)))
     return e;
-  const int grid = lfm3::gemv_grid(p.tiles * p.chunks, Sms());
+  const int grid = lfm3::gemv_grid(p.tiles, Sms());
   for (int r0 = 0; r0 < n; r0 += lfm3::kMaxBatch) {
     lfm3::GemvParams q = p;
     q.tokens = std::min(lfm3::kMaxBatch, n - r0);
@@ -129,7 +115,7 @@ int ProjectImpl(const lfm3_output* outputs, int count, const float* x, int n,
         !outputs[j].out)
       return Fail(LFM3_ERR_UNSUPPORTED,
                   "projections need Q8_0 weights with equal widths, "
-                  "multiples of 256");
+                  "multiples of 512");
   if (n < kPromptRows) {
     lfm3::GemvParams p{};
     p.kind = lfm3::kGemvPlain;
@@ -204,7 +190,8 @@ size_t lfm3_cuda_dense_workspace_bytes(size_t rows, size_t K) {
   return std::max(rows * K * 2 + rows * 4, rows * K * 4);
 }
 size_t lfm3_cuda_split_partial_bytes(void) {
-  return lfm3::gemv_partial_floats(Sms()) * 4;
+  // decode projections finish every tile in one CTA: no split-K partials
+  return 0;
 }
 size_t lfm3_cuda_split_ticket_words(void) { return kTicketWords; }
 int lfm3_cuda_prompt_rows(void) { return kPromptRows; }

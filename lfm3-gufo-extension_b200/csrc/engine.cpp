@@ -32,8 +32,8 @@ std::string Validate(const lfm3_weights& w) {
       !c.heads || !c.hidden || !c.intermediate || !c.vocab || !c.context ||
       c.conv_width < 2 || c.conv_width > 32 || !c.window)
     return "unsupported LFM3 dimensions";
-  if (c.hidden % 256 || c.intermediate % 256 || (c.heads * 128) % 256)
-    return "LFM3 widths must be multiples of 256";
+  if (c.hidden % 512 || c.intermediate % 512 || (c.heads * 128) % 512)
+    return "LFM3 widths must be multiples of 512";
   if (c.hidden > 8192)
     return "LFM3 hidden width above 8192";
   for (uint32_t i = 0; i < c.n_layers; ++i) {
@@ -174,14 +174,15 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
   }
 }
 
-const CUtensorMap& Model::RowMap(const lfm3_tensor& t, int box_rows) {
+const CUtensorMap& Model::RowMap(const lfm3_tensor& t, int chunk_bytes,
+                                 int box_rows) {
   std::lock_guard<std::mutex> lock(maps_mutex_);
-  const auto key = std::make_pair(t.data, box_rows);
+  const auto key = std::make_pair(t.data, chunk_bytes * 1024 + box_rows);
   auto it = maps_.find(key);
   if (it == maps_.end()) {
     CUtensorMap map;
     Throw(encode_row_map(&map, t.data, size_t(t.cols) / 32 * 34, int(t.rows),
-                         kGemvChunk, box_rows));
+                         chunk_bytes, box_rows));
     it = maps_.emplace(key, map).first;
   }
   return it->second;
@@ -260,13 +261,6 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     batch_logits_ = DeviceBuffer(kMaxBatch * size_t(c.vocab) * 4);
     chunk_k_ = DeviceBuffer(R * KV * 2);
     chunk_v_ = DeviceBuffer(R * KV * 2);
-    const int sms = model_->sms();
-    gemv_partials_ = DeviceBuffer(gemv_partial_floats(sms) * 4);
-    const size_t max_tiles = std::max<size_t>(
-        {size_t(c.vocab) / kGemvRows + 4, F / 32 + 4, H / 16 + 4,
-         (3 * H + A + 2 * KV) / kGemvRows + 8});
-    gemv_tickets_ = DeviceBuffer(max_tiles * 4);
-    Throw(cudaMemset(gemv_tickets_.data(), 0, gemv_tickets_.bytes()));
     attn_partials_ =
         DeviceBuffer(decode_attention_partial_floats(c.heads) * 4);
     attn_tickets_ = DeviceBuffer(kMaxBatch * std::max(kv_max, 1u) * 4);
@@ -346,32 +340,15 @@ void Session::TakeProfile(double* ms, long long* launches) {
 // ---- decode round -------------------------------------------------------------
 
 // Launches one projection of the round's rows (split input x).
-static cudaError_t RunGemv(GemvParams p, Model& model, float* partials,
-                           unsigned* tickets, cudaStream_t stream) {
-  const int sms = model.sms();
-  p.chunks = p.K / 256;
+static cudaError_t RunGemv(GemvParams p, Model& model, cudaStream_t stream) {
+  if (!gemv_plan(p))
+    return cudaErrorInvalidValue;
   const int maps = p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
   for (int j = 0; j < maps; ++j) {
     lfm3_tensor t{p.o[j].w, LFM3_Q8_0, uint32_t(p.K), uint32_t(p.o[j].rows), 0};
-    p.maps[j] = model.RowMap(t, gemv_box_rows(p.kind));
+    p.maps[j] = model.RowMap(t, gemv_pitch_units(p.chunk_blocks) * 16, 16);
   }
-  if (p.kind == kGemvPlain) {
-    int tiles = 0;
-    for (int j = 0; j < p.n_out; ++j) {
-      p.first_tile[j] = tiles;
-      tiles += CeilDiv(p.o[j].rows, kGemvRows);
-    }
-    p.first_tile[p.n_out] = tiles;
-    p.tiles = tiles;
-  } else if (p.kind == kGemvSwiGLU) {
-    p.tiles = CeilDiv(p.o[0].rows, 32);
-  } else {
-    p.tiles = CeilDiv(p.H, 16);
-  }
-  p.partials = partials;
-  p.tickets = tickets;
-  const int units = p.tiles * p.chunks;
-  return launch_q8_gemv(p, gemv_grid(units, sms), stream, true);
+  return launch_q8_gemv(p, gemv_grid(p.tiles, model.sms()), stream, true);
 }
 
 static GemvOutput Out(const lfm3_tensor& w, float* out, int ld) {
@@ -388,8 +365,7 @@ void Session::LaunchLmHead(const void* split_rows, int rows, float* out) {
   p.n_out = 1;
   p.o[0] = Out(w.output, out, c.vocab);
   p.x = split_rows;
-  Check(RunGemv(p, *model_, gemv_partials_.as<float>(),
-                gemv_tickets_.as<unsigned>(), stream_));
+  Check(RunGemv(p, *model_, stream_));
 }
 
 void Session::DecodeRound(std::span<Session* const> batch,
@@ -399,12 +375,9 @@ void Session::DecodeRound(std::span<Session* const> batch,
   const int B = int(batch.size());
   const int H = c.hidden, F = c.intermediate, A = c.heads * 128;
   cudaStream_t s = stream_;
-  const int sms = model_->sms();
-  float* partials = gemv_partials_.as<float>();
-  unsigned* tickets = gemv_tickets_.as<unsigned>();
   const auto gemv = [&](GemvParams p) {
     Timed(kDecodeProjection,
-          [&] { Check(RunGemv(p, *model_, partials, tickets, s)); });
+          [&] { Check(RunGemv(p, *model_, s)); });
   };
   // the rows of this round
   Check(cudaStreamSynchronize(s));  // host_rows_ is reused between rounds

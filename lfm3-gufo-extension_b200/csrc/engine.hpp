@@ -67,9 +67,10 @@ public:
   int sms() const { return sms_; }
   // Device bytes of the weight segments.
   size_t weight_bytes() const { return weight_bytes_; }
-  // The TMA map over a Q8_0 matrix's rows in 272-byte chunks with boxes of
-  // box_rows rows (encoded once, cached).
-  const CUtensorMap& RowMap(const lfm3_tensor& t, int box_rows);
+  // The TMA map over a Q8_0 matrix's rows with boxes of box_rows rows x
+  // chunk_bytes (encoded once, cached).
+  const CUtensorMap& RowMap(const lfm3_tensor& t, int chunk_bytes,
+                            int box_rows);
 
 private:
   Model() = default;
@@ -175,7 +176,7 @@ private:
   // workspace (this session's passes, and rounds it leads)
   DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_, row_max_,
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
-      chunk_k_, chunk_v_, gemv_partials_, gemv_tickets_, attn_partials_,
+      chunk_k_, chunk_v_, attn_partials_,
       attn_tickets_, prompt_scratch_;
   DecodeRows* host_rows_ = nullptr;  // pinned
   bool profiling_ = false;

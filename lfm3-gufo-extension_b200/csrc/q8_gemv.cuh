@@ -11,25 +11,33 @@
 
 namespace lfm3 {
 
-constexpr int kGemvRows = 64;     // weight rows per tile
-constexpr int kGemvBlocks = 8;    // Q8 blocks per stage (256 columns)
-constexpr int kGemvChunk = kGemvBlocks * 34;  // bytes per row per stage
-constexpr int kGemvStages = 4;
-constexpr int kGemvWarps = 8;     // consumer warps, one Q8 block each
-constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
-constexpr int kGemvTile = kGemvRows * kMaxBatch;  // fp32 values per tile
-
 enum GemvKind : int {
-  // out[token * ld + row] for up to four weights sharing the input
+  // out[token * ld + row] for up to four weights sharing the input;
+  // tile = 16 rows of one weight, chunks of 64 Q8 blocks (2048 columns)
   kGemvPlain = 0,
-  // tile = 32 gate rows + the same 32 up rows; writes silu(g) * u as split
-  // activations of width F
+  // tile = 16 gate rows + the same 16 up rows, chunks of 32 blocks; writes
+  // silu(g) * u as split activations of width F (and/or FP32)
   kGemvSwiGLU = 1,
-  // tile = 16 channels: rows ch, H + ch, 2H + ch of in_proj (B, C, x);
-  // runs the width-L convolution step against each row's session history
-  // and writes the gated output as split activations of width H
+  // tile = 16 channels: rows ch, H + ch, 2H + ch of in_proj (B, C, x),
+  // chunks of 16 blocks; runs the width-L convolution step against each
+  // row's session history and writes the gated output as split activations
   kGemvConv = 2,
 };
+
+// m-tiles (16 rows each) of a tile; the 16-byte units a row occupies in
+// shared memory for chunks of `blocks` Q8 blocks (the chunk plus padding
+// that spreads the rows of a warp's fragment loads over the banks).
+constexpr __host__ __device__ int gemv_mtiles(int kind) {
+  return kind == kGemvPlain ? 1 : kind == kGemvSwiGLU ? 2 : 3;
+}
+constexpr __host__ __device__ int gemv_pitch_units(int blocks) {
+  return blocks * 34 / 16 + ((blocks * 34 / 16) % 4 == 0 ? 2 : 0);
+}
+
+constexpr int kGemvStageBytes = 35840;  // max over kinds of rows x pitch
+constexpr int kGemvStages = 2;
+constexpr int kGemvWarps = 8;  // consumer warps
+constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
 
 struct GemvOutput {
   const uint8_t* w;  // Q8_0 rows of K / 32 blocks
@@ -39,13 +47,14 @@ struct GemvOutput {
 };
 
 struct GemvParams {
-  // TMA maps over the weight rows (tensor_map.hpp), 272-byte chunks: Plain
-  // one per output with 64-row boxes; SwiGLU gate and up with 32-row boxes;
-  // Conv in_proj with 16-row boxes.
+  // TMA maps over the weight rows (tensor_map.hpp), 16-row boxes of
+  // gemv_pitch_units(chunk_blocks) 16-byte units: Plain one per output,
+  // SwiGLU gate and up, Conv in_proj.
   alignas(64) CUtensorMap maps[4];
   int kind;
-  int K;        // columns (multiple of 256)
-  int chunks;   // K / 256
+  int K;             // columns
+  int chunk_blocks;  // Q8 blocks per chunk (64, 32 or 16; gemv_plan)
+  int chunks;        // K / (32 * chunk_blocks)
   int tiles;
   int tokens;   // 1..8
   int n_out;
@@ -60,19 +69,13 @@ struct GemvParams {
   int layer;
   int H;
   int L;
-  // stream-K fix-up scratch
-  float* partials;    // [grid][2][kGemvTile]
-  unsigned* tickets;  // [tiles], zero between launches
 };
 
-// Grid size and scratch needs of one launch.
-int gemv_grid(int units, int sms);
-size_t gemv_partial_floats(int grid);
-
-// Box rows of the weight maps each kind reads (per output slot).
-inline int gemv_box_rows(int kind) {
-  return kind == kGemvPlain ? kGemvRows : kind == kGemvSwiGLU ? 32 : 16;
-}
+// Fills p.chunk_blocks, p.chunks, p.tiles and p.first_tile from the kind,
+// K and outputs (Plain chunks of 64 blocks when K allows, else 16; SwiGLU 32
+// or 16; Conv 16); returns false for widths that are not multiples of 512.
+bool gemv_plan(GemvParams& p);
+int gemv_grid(int tiles, int sms);
 // Encodes p.maps from p.o[j].w / rows / K (host; for callers without a map
 // cache).
 cudaError_t fill_gemv_maps(GemvParams& p);
