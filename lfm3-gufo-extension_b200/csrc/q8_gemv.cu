@@ -347,7 +347,14 @@ bool gemv_plan(GemvParams& p) {
   return p.tiles > 0;
 }
 
-int gemv_grid(int tiles, int sms) { return tiles < sms ? tiles : sms; }
+int gemv_grid(int tiles, int sms) {
+  // Projections with tiles for two CTAs per SM take them (twice the warps to
+  // hide latency); smaller ones keep one per SM so the next kernel's CTA can
+  // be resident and start its copies early.
+  if (tiles >= 2 * sms)
+    return 2 * sms;
+  return tiles < sms ? tiles : sms;
+}
 
 cudaError_t fill_gemv_maps(GemvParams& p) {
   const size_t row_bytes = size_t(p.K / 32) * 34;
