@@ -137,6 +137,23 @@ int lfm3_cuda_attention(const float* q, const uint16_t* k, const uint16_t* v,
                         const uint16_t* cache_v, float* out, int n, int heads,
                         int kv_heads, int dim, int position, int capacity,
                         int window, void* stream, float* scratch);
+/* No counterpart in the reference. The n == 1 case of lfm3_cuda_attention
+ * for callers that cannot allocate device memory (a serving loop whose
+ * memory is a fixed arena sized at start-up, or a latency-critical thread
+ * that must not call cudaMalloc between steps): same arguments minus n and
+ * scratch; its scratch is a static device array of about 1 MiB per GPU that
+ * loads the library, kept until the process exits, so heads must be <= 32
+ * (LFM3_ERR_UNSUPPORTED with a message beyond that). It allocates nothing.
+ * The first call on each device looks up that array's device address; make
+ * it before any stream capture. Calls share the array: calls that overlap
+ * on the GPU race and must be serialised by the caller. */
+int lfm3_cuda_attention_decode_noalloc(const float* q, const uint16_t* k,
+                                       const uint16_t* v, const float* gate,
+                                       const uint16_t* cache_k,
+                                       const uint16_t* cache_v, float* out,
+                                       int heads, int kv_heads, int dim,
+                                       int position, int capacity, int window,
+                                       void* stream);
 /* AttentionScratchBytes (hip/ops.hpp:99). */
 size_t lfm3_cuda_attention_scratch_bytes(int heads, int dim, int context,
                                          int rows);

@@ -179,6 +179,10 @@ __global__ void copy_rows_kernel(const unsigned char* source,
 
 }  // namespace
 
+int lfm3::set_last_error(int code, const char* message) {
+  return Fail(code, message);
+}
+
 extern "C" {
 
 const char* lfm3_last_error(void) { return g_last_error.c_str(); }

@@ -17,6 +17,9 @@ cudaError_t launch_q8_gemv(const GemvParams& p, int grid, cudaStream_t stream,
 // Reads and clears the device error word (bounded waits that gave up).
 unsigned take_device_error();
 
+// Records the message lfm3_last_error() returns on this thread; returns code.
+int set_last_error(int code, const char* message);
+
 // Process-wide count of kernels this library has launched.
 void note_launch(int kernels = 1);
 unsigned long long launch_count();
