@@ -86,7 +86,7 @@ int PrefillRows(lfm3::PrefillParams p, const float* x, int n, int K,
       return e;
   p.K = K;
   p.tokens = n;
-  p.x = values;
+  p.x_row0 = 0;
   p.scale = scale;
   if (p.kind == lfm3::kPrefillPlain) {
     int tiles = 0;
@@ -99,7 +99,7 @@ int PrefillRows(lfm3::PrefillParams p, const float* x, int n, int K,
   } else {
     p.row_tiles = (p.o[0].rows + 63) / 64;
   }
-  return Cuda(lfm3::launch_q8_prefill(p, s));
+  return Cuda(lfm3::launch_q8_prefill(p, values, n, s));
 }
 
 int ProjectImpl(const lfm3_output* outputs, int count, const float* x, int n,

@@ -116,6 +116,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int x0,
       : "memory");
 }
 
+// One tiled TMA copy of a 2-D box at (x0, x1) of `map`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x0,
+                                            int x1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(x1),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
 // ---- programmatic dependent launch ------------------------------------------
 // Work before grid_dependency_wait() may only touch data that no earlier
 // kernel in the stream writes (weights); everything else comes after it.

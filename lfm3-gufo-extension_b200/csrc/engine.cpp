@@ -556,8 +556,14 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
   __half* half = half_.as<__half>();
   float* scale = scale_.as<float>();
   const auto half_at = [&](int row, int width) { return half + size_t(row) * width; };
-  const auto prefill = [&](PrefillParams p) {
-    Timed(kPromptProjection, [&] { Check(launch_q8_prefill(p, s)); });
+  // prompt projections read FP16 rows of the workspace (viewed as
+  // [rows][K]) starting at row `first`
+  const size_t half_elems = half_.bytes() / 2;
+  const auto prefill = [&](PrefillParams p, int first) {
+    p.x_row0 = first;
+    Timed(kPromptProjection, [&] {
+      Check(launch_q8_prefill(p, half, int(half_elems / size_t(p.K)), s));
+    });
   };
   const auto other = [&](auto launch) { Timed(kPromptOther, launch); };
   const auto rows = [&](auto launch) { Timed(kRowKernels, launch); };
@@ -577,9 +583,8 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     }
     p.first_tile[j] = tiles;
     p.row_tiles = tiles;
-    p.x = half_at(first_row, K);
     p.scale = scale + first_row;
-    prefill(p);
+    prefill(p, first_row);
   };
   const auto pout = [](const lfm3_tensor& t, float* o, int ld) {
     return PrefillOutput{static_cast<const uint8_t*>(t.data), o, int(t.rows),
@@ -683,10 +688,9 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       p.o[0] = pout(l.gate, ff + size_t(o) * F, F);
       p.o[1] = pout(l.up, nullptr, F);
       p.row_tiles = CeilDiv(F, 64);
-      p.x = half_at(o, H);
       p.scale = scale + o;
       p.row_max = row_max + o;
-      prefill(p);
+      prefill(p, o);
       other([&] {
         Check(launch_half_rows(ff + size_t(o) * F, row_max + o,
                                half_at(o, F), scale + o, rows_out, F, s));

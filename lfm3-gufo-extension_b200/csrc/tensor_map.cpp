@@ -53,4 +53,24 @@ cudaError_t encode_row_map(CUtensorMap* map, const void* base,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t encode_activation_map(CUtensorMap* map, const void* base, int rows,
+                                  int cols, int box_rows, int box_cols) {
+  const EncodeTiled encode = Encoder();
+  if (!encode)
+    return cudaErrorNotSupported;
+  if (rows < 1 || cols % 8 || box_cols * 2 != 64 || box_rows < 1 ||
+      box_rows > 256 || reinterpret_cast<uintptr_t>(base) % 16)
+    return cudaErrorInvalidValue;
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+  const cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  const cuuint32_t element_strides[2] = {1, 1};
+  const CUresult r = encode(
+      map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+      strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace lfm3

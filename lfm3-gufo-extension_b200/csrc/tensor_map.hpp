@@ -19,4 +19,10 @@ cudaError_t encode_row_map(CUtensorMap* map, const void* base,
                            size_t row_bytes, int rows, int chunk_bytes,
                            int box_rows);
 
+// Encodes a map over fp16 activations [rows][cols] (row pitch cols * 2
+// bytes) with boxes of box_rows x box_cols (box_cols * 2 == 64) and the
+// 64-byte swizzle the tcgen05 K-major operand layout expects.
+cudaError_t encode_activation_map(CUtensorMap* map, const void* base, int rows,
+                                  int cols, int box_rows, int box_cols);
+
 }  // namespace lfm3
