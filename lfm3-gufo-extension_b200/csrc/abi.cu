@@ -88,17 +88,8 @@ int PrefillRows(lfm3::PrefillParams p, const float* x, int n, int K,
   p.tokens = n;
   p.x_row0 = 0;
   p.scale = scale;
-  if (p.kind == lfm3::kPrefillPlain) {
-    int tiles = 0;
-    for (int j = 0; j < p.n_out; ++j) {
-      p.first_tile[j] = tiles;
-      tiles += (p.o[j].rows + 127) / 128;
-    }
-    p.first_tile[p.n_out] = tiles;
-    p.row_tiles = tiles;
-  } else {
-    p.row_tiles = (p.o[0].rows + 63) / 64;
-  }
+  // split-K partial sums when the caller passed the split workspace
+  p.partial = ws.partial;
   return Cuda(lfm3::launch_q8_prefill(p, values, n, s));
 }
 
@@ -194,8 +185,8 @@ size_t lfm3_cuda_dense_workspace_bytes(size_t rows, size_t K) {
   return std::max(rows * K * 2 + rows * 4, rows * K * 4);
 }
 size_t lfm3_cuda_split_partial_bytes(void) {
-  // decode projections finish every tile in one CTA: no split-K partials
-  return 0;
+  // prompt projections with few tiles split K (decode projections never do)
+  return lfm3::kPrefillPartialFloats * sizeof(float);
 }
 size_t lfm3_cuda_split_ticket_words(void) { return kTicketWords; }
 int lfm3_cuda_prompt_rows(void) { return kPromptRows; }

@@ -252,6 +252,7 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     a_ = DeviceBuffer(R * std::max(A, H) * 4);
     ff_ = DeviceBuffer(R * F * 4);
     row_max_ = DeviceBuffer(R * 4);
+    split_partial_ = DeviceBuffer(kPrefillPartialFloats * 4);
     half_ = DeviceBuffer(R * width * 2);
     scale_ = DeviceBuffer(R * 4);
     z_split_ = DeviceBuffer(kMaxBatch * H * 4);
@@ -561,6 +562,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
   const size_t half_elems = half_.bytes() / 2;
   const auto prefill = [&](PrefillParams p, int first) {
     p.x_row0 = first;
+    p.partial = split_partial_.as<float>();
     Timed(kPromptProjection, [&] {
       Check(launch_q8_prefill(p, half, int(half_elems / size_t(p.K)), s));
     });
@@ -574,15 +576,9 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     p.K = K;
     p.tokens = rows;
     p.n_out = int(outs.size());
-    int tiles = 0, j = 0;
-    for (const auto& o : outs) {
-      p.o[j] = o;
-      p.first_tile[j] = tiles;
-      tiles += CeilDiv(o.rows, 128);
-      ++j;
-    }
-    p.first_tile[j] = tiles;
-    p.row_tiles = tiles;
+    int j = 0;
+    for (const auto& o : outs)
+      p.o[j++] = o;
     p.scale = scale + first_row;
     prefill(p, first_row);
   };
@@ -687,7 +683,6 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       p.n_out = 2;
       p.o[0] = pout(l.gate, ff + size_t(o) * F, F);
       p.o[1] = pout(l.up, nullptr, F);
-      p.row_tiles = CeilDiv(F, 64);
       p.scale = scale + o;
       p.row_max = row_max + o;
       prefill(p, o);

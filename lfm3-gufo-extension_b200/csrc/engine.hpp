@@ -177,7 +177,7 @@ private:
   DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_, row_max_,
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
-      attn_tickets_, prompt_scratch_;
+      attn_tickets_, prompt_scratch_, split_partial_;
   DecodeRows* host_rows_ = nullptr;  // pinned
   bool profiling_ = false;
   std::vector<cudaEvent_t> events_;

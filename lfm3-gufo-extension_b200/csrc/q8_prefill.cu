@@ -1,26 +1,44 @@
 // Prompt-pass Q8_0 projections on the fifth-generation tensor cores
-// (tcgen05, accumulators in tensor memory).
+// (tcgen05 MMA, accumulators in tensor memory).
 //
-// A work unit is 128 weight rows x 128 tokens over all K; CTAs (one per SM)
-// take units round-robin, token tile fastest, so the CTAs sharing a weight
-// tile run together and read it once from HBM. Warp roles:
-//   warp 0     TMA producer: raw Q8 rows (272-byte chunks = 8 blocks) and
-//              the fp16 activation tile of every block (128 tokens x 32,
-//              64-byte swizzle)
-//   warps 1-4  converters: each thread owns one weight row, decodes its
-//              codes exactly to fp16 into the 64-byte-swizzled K-major A
-//              tile of one block and records the block scale d
-//   warp 5     one thread issues tcgen05.mma (M128 N128 K16, twice per
-//              block) into one of four TMEM buffers and commits
-//   warps 6-13 epilogue: each thread owns one weight row (TMEM lane) and
-//              one half of the 128 token columns, loads the block's 64 sums
-//              and accumulates acc += d * C in FP32
-// so every K32 block is scaled as in the reference (acc = fma(d, c, acc),
-// hip/q8_prefill.hpp:563-569), with the row scale of the FP16 activations
-// applied after K. Stages hand over through mbarriers; every wait is
-// bounded. SwiGLU units hold 64 gate rows and the same 64 up rows and
-// write silu(g) * u with per-token maxima (atomicMax) for the down
-// projection's FP16 conversion.
+// Exact split of the block scales. The reference sums each K32 block in FP32
+// and scales it (acc = fma(d, c, acc), hip/q8_prefill.hpp:563-569). Here each
+// weight w = q * d (q the integer code, d the block's fp16 scale) is written
+// as w = hi + lo with hi = fp16(q * d) and lo = fp16(q * d - hi) (one rounded
+// multiply and one fused multiply-add in fp16). q * d has at most 18
+// significant bits and its last bit is a multiple of 2^-24, so the rounding
+// residual is itself an fp16 number and hi + lo == q * d exactly (true for
+// every code and every fp16 scale below 516; larger scales, weights beyond
+// 65504, would overflow hi). The tensor cores multiply hi and lo by the FP16
+// activations exactly (11 x 11 significant bits) and accumulate in FP32, so
+// each output is the reference's real-valued sum up to FP32 rounding order,
+// with twice the MMA work and no per-block epilogue: the K loop stays in the
+// tensor pipe.
+//
+// A tile is 256 weight rows x 128 prompt rows over a K range (split-K for
+// matrices with few tiles: FP32 partial sums per split, then a bandwidth-
+// bound pass adds them in split order, hip/ops.hip:2039-2119). Persistent
+// CTAs (one per SM) take units round-robin, split and prompt tile fastest,
+// so the CTAs sharing a weight tile run together and read it once from HBM.
+// Warp roles:
+//   warp 0      TMA producer: the fp16 activation tile of every K32 block
+//               (128 rows x 32, 64-byte swizzle)
+//   warp 1      one thread issues tcgen05.mma: per block, two accumulators
+//               (rows 0-127, 128-255) x {hi, lo} x two K16 steps, M128 N128,
+//               into one of two accumulator pairs; commits every stage and
+//               every finished tile
+//   warps 2-9   converters: thread r owns weight row r of the tile. Raw Q8
+//               rows arrive by TMA 8 blocks (272 bytes per row) at a time,
+//               issued by warp 2's lane 0 as soon as the previous chunk is in
+//               registers; per block each thread writes its row of the hi and
+//               lo A tiles (fp16, K-major, 64-byte swizzle)
+//   warps 10-13 epilogue: thread owns one TMEM lane (weight row) of both
+//               accumulators; applies the prompt-row scales and writes the
+//               outputs (SwiGLU: silu(g) * u and per-row maxima; split tiles:
+//               the FP32 partial sums)
+// Stages hand over through mbarriers and every wait is bounded: a pipeline
+// that stops making progress reports kErrPrefillWait and the CTA returns.
+// When that happens every copy and MMA it issued is seconds old and complete.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8_prefill.cuh"
@@ -29,25 +47,24 @@
 namespace lfm3 {
 namespace {
 
-constexpr int kTM = 128, kTN = 128;
-constexpr int kWStages = 2, kASlots = 4, kBSlots = 6, kTBufs = 4;
-constexpr int kWRowBytes = 272;                    // 8 blocks
-constexpr int kWStageBytes = kTM * kWRowBytes;     // 34,816
-constexpr int kABytes = kTM * 64, kBBytes = kTN * 64;
-constexpr int kThreads = 448;  // 14 warps: <= 128 registers each
-constexpr int kXchPitch = kTN + 1;
+constexpr int kTM = 128;                      // rows per accumulator
+constexpr int kRows = kPrefillTileRows;       // 256
+constexpr int kTN = kPrefillTileTokens;       // 128
+constexpr int kStages = 3;
+constexpr int kWRowBytes = 272;               // 8 blocks of 34 bytes
+constexpr int kWBytes = kRows * kWRowBytes;   // 69,632
+constexpr int kAPartBytes = kRows * 64;       // 256 rows x 32 fp16
+constexpr int kBBytes = kTN * 64;             // 128 rows x 32 fp16
+constexpr int kThreads = 14 * 32;
 
 struct __align__(1024) PrefillSmem {
-  uint8_t a[kASlots][kABytes];
-  uint8_t b[kBSlots][kBBytes];
-  uint8_t w[kWStages][kWStageBytes];
-  float d[kASlots][kTM];
-  float xch[64 * kXchPitch];
-  uint64_t w_full[kWStages], w_empty[kWStages];
-  uint64_t b_full[kBSlots], b_empty[kBSlots];
-  uint64_t a_full[kASlots], a_empty[kASlots];
-  uint64_t d_full[kASlots], d_empty[kASlots];
-  uint64_t t_full[kTBufs], t_empty[kTBufs];
+  uint8_t a_hi[kStages][kAPartBytes];
+  uint8_t a_lo[kStages][kAPartBytes];
+  uint8_t b[kStages][kBBytes];
+  uint8_t w[kWBytes];
+  uint64_t w_full, w_empty;
+  uint64_t full[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t tmem_base;
 };
 
@@ -57,7 +74,8 @@ constexpr uint32_t kInstrDesc =
     (1u << 4) | (uint32_t(kTN >> 3) << 17) | (uint32_t(kTM >> 4) << 24);
 
 // Shared-memory matrix descriptor of a K-major operand with 64-byte rows and
-// the 64-byte swizzle: 8-row groups 512 bytes apart.
+// the 64-byte swizzle: 8-row groups 512 bytes apart. Adding 2 advances K by
+// 16 elements (32 bytes), adding 512 advances 128 rows.
 __device__ __forceinline__ uint64_t sw64_desc(const void* p) {
   const uint32_t addr = smem_addr(p);
   return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) |
@@ -104,19 +122,6 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 __device__ __forceinline__ void tc_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-// acc (two lanes) += d * v (two lanes), FP32, one packed instruction.
-__device__ __forceinline__ void fma2(float2& acc, float d, uint32_t v0,
-                                     uint32_t v1) {
-  unsigned long long a = (unsigned long long)__float_as_uint(acc.x) |
-                         ((unsigned long long)__float_as_uint(acc.y) << 32);
-  const unsigned long long dd = (unsigned long long)__float_as_uint(d) |
-                                ((unsigned long long)__float_as_uint(d) << 32);
-  const unsigned long long vv =
-      (unsigned long long)v0 | ((unsigned long long)v1 << 32);
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(dd), "l"(vv));
-  acc.x = __uint_as_float(uint32_t(a));
-  acc.y = __uint_as_float(uint32_t(a >> 32));
-}
 
 struct Ring {
   int slot = 0;
@@ -129,13 +134,46 @@ struct Ring {
   }
 };
 
-__device__ __forceinline__ int output_of(const PrefillParams& p, int t) {
+// Unit u: split fastest, then prompt tile, then row tile.
+struct Unit {
+  int rt, tt, tile, kb0, kb1;
+};
+__device__ __forceinline__ Unit unit_of(const PrefillParams& p, int u,
+                                        int token_tiles, int blocks_per_split) {
+  Unit x;
+  const int sp = u % p.splits;
+  x.tile = u / p.splits;
+  x.tt = x.tile % token_tiles;
+  x.rt = x.tile / token_tiles;
+  x.kb0 = sp * blocks_per_split;
+  x.kb1 = x.kb0 + blocks_per_split;
+  return x;
+}
+
+__device__ __forceinline__ int output_of(const PrefillParams& p, int rt) {
   int j = 0;
 #pragma unroll
   for (int q = 1; q < 4; ++q)
-    if (q < p.n_out && t >= p.first_tile[q])
+    if (q < p.n_out && rt >= p.first_tile[q])
       j = q;
   return j;
+}
+
+// One 8-block chunk of the tile's 256 raw weight rows into s.w.
+__device__ __forceinline__ void load_weights(const PrefillParams& p,
+                                             PrefillSmem& s, int rt,
+                                             int chunk) {
+  mbar_arrive_expect_tx(&s.w_full, kWBytes);
+  if (p.kind == kPrefillPlain) {
+    const int j = output_of(p, rt);
+    tma_load_2d(s.w, &p.w_maps[j], chunk * (kWRowBytes / 8),
+                (rt - p.first_tile[j]) * kRows, &s.w_full);
+  } else {
+    tma_load_2d(s.w, &p.w_maps[0], chunk * (kWRowBytes / 8), rt * kTM,
+                &s.w_full);
+    tma_load_2d(s.w + kTM * kWRowBytes, &p.w_maps[1],
+                chunk * (kWRowBytes / 8), rt * kTM, &s.w_full);
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -145,27 +183,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int token_tiles = (p.tokens + kTN - 1) / kTN;
-  const int units = p.row_tiles * token_tiles;
-  const int blocks = p.K / 32, stages = blocks / 8;
+  const int units = p.row_tiles * token_tiles * p.splits;
+  const int bps = p.K / 32 / p.splits;  // blocks per split, a multiple of 8
 
   if (tid == 0) {
-    for (int i = 0; i < kWStages; ++i) {
-      mbar_init(&s.w_full[i], 1);
-      mbar_init(&s.w_empty[i], 4);
+    mbar_init(&s.w_full, 1);
+    mbar_init(&s.w_empty, 8);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 9);  // 8 converter warps + the producer's bytes
+      mbar_init(&s.empty[i], 1);
     }
-    for (int i = 0; i < kBSlots; ++i) {
-      mbar_init(&s.b_full[i], 1);
-      mbar_init(&s.b_empty[i], 1);
-    }
-    for (int i = 0; i < kASlots; ++i) {
-      mbar_init(&s.a_full[i], 4);
-      mbar_init(&s.a_empty[i], 1);
-      mbar_init(&s.d_full[i], 4);
-      mbar_init(&s.d_empty[i], 8);
-    }
-    for (int i = 0; i < kTBufs; ++i) {
-      mbar_init(&s.t_full[i], 1);
-      mbar_init(&s.t_empty[i], 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);
     }
     fence_barrier_init();
   }
@@ -181,49 +211,77 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = s.tmem_base;
 
   if (warp == 0) {
-    // ---- producer
+    // ---- activation tiles
     if (lane == 0) {
-      Ring w, b;
+      Ring b;
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        const int rt = u / token_tiles, tok0 = (u % token_tiles) * kTN;
-        for (int st = 0; st < stages; ++st) {
-          if (!mbar_wait(&s.w_empty[w.slot], w.phase ^ 1, kErrPrefillWait))
+        const Unit x = unit_of(p, u, token_tiles, bps);
+        for (int kb = x.kb0; kb < x.kb1; ++kb) {
+          if (!mbar_wait(&s.empty[b.slot], b.phase ^ 1, kErrPrefillWait))
             goto done;
-          mbar_arrive_expect_tx(&s.w_full[w.slot], kWStageBytes);
-          if (p.kind == kPrefillPlain) {
-            const int j = output_of(p, rt);
-            tma_load_3d(s.w[w.slot], &p.w_maps[j], 0, st * 17,
-                        (rt - p.first_tile[j]) * kTM, &s.w_full[w.slot]);
-          } else {
-            tma_load_3d(s.w[w.slot], &p.w_maps[0], 0, st * 17, rt * 64,
-                        &s.w_full[w.slot]);
-            tma_load_3d(s.w[w.slot] + 64 * kWRowBytes, &p.w_maps[1], 0,
-                        st * 17, rt * 64, &s.w_full[w.slot]);
-          }
-          w.next(kWStages);
-          for (int kb = st * 8; kb < st * 8 + 8; ++kb) {
-            if (!mbar_wait(&s.b_empty[b.slot], b.phase ^ 1, kErrPrefillWait))
-              goto done;
-            mbar_arrive_expect_tx(&s.b_full[b.slot], kBBytes);
-            tma_load_2d(s.b[b.slot], &p.x_map, kb * 32, p.x_row0 + tok0,
-                        &s.b_full[b.slot]);
-            b.next(kBSlots);
-          }
+          mbar_arrive_expect_tx(&s.full[b.slot], kBBytes);
+          tma_load_2d(s.b[b.slot], &p.x_map, kb * 32,
+                      p.x_row0 + x.tt * kTN, &s.full[b.slot]);
+          b.next(kStages);
         }
       }
     }
-  } else if (warp <= 4) {
-    // ---- converters: thread owns weight row r of the unit
-    const int r = (warp - 1) * 32 + lane;
-    Ring w, a;
+  } else if (warp == 1) {
+    // ---- MMA issue
+    if (lane == 0) {
+      Ring st;
+      int j = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+        const Unit x = unit_of(p, u, token_tiles, bps);
+        const int buf = j & 1;
+        if (!mbar_wait(&s.acc_empty[buf], ((j >> 1) & 1) ^ 1,
+                       kErrPrefillWait))
+          goto done;
+        tc_fence_after();
+        const uint32_t d0 = tmem + uint32_t(buf * 2 * kTN);
+        const uint32_t d1 = d0 + kTN;
+        for (int kb = x.kb0; kb < x.kb1; ++kb) {
+          if (!mbar_wait(&s.full[st.slot], st.phase, kErrPrefillWait))
+            goto done;
+          tc_fence_after();
+          const uint64_t hi = sw64_desc(s.a_hi[st.slot]);
+          const uint64_t lo = sw64_desc(s.a_lo[st.slot]);
+          const uint64_t xb = sw64_desc(s.b[st.slot]);
+          const uint32_t acc = kb != x.kb0;
+          tc_mma(d0, hi, xb, acc);
+          tc_mma(d0, hi + 2, xb + 2, 1);
+          tc_mma(d0, lo, xb, 1);
+          tc_mma(d0, lo + 2, xb + 2, 1);
+          tc_mma(d1, hi + 512, xb, acc);
+          tc_mma(d1, hi + 514, xb + 2, 1);
+          tc_mma(d1, lo + 512, xb, 1);
+          tc_mma(d1, lo + 514, xb + 2, 1);
+          tc_commit(&s.empty[st.slot]);
+          st.next(kStages);
+        }
+        tc_commit(&s.acc_full[buf]);
+      }
+    }
+  } else if (warp < 10) {
+    // ---- converters: thread owns weight row r of the tile
+    const int r = (warp - 2) * 32 + lane;
+    const bool loader = warp == 2 && lane == 0;
+    const int swz = (r >> 1) & 3;  // 64-byte swizzle of row r
+    Ring a;
+    uint32_t w_phase = 0;
+    if (loader && int(blockIdx.x) < units) {
+      const Unit x = unit_of(p, blockIdx.x, token_tiles, bps);
+      load_weights(p, s, x.rt, x.kb0 / 8);
+    }
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      for (int st = 0; st < stages; ++st) {
-        if (!mbar_wait(&s.w_full[w.slot], w.phase, kErrPrefillWait))
+      const Unit x = unit_of(p, u, token_tiles, bps);
+      for (int chunk = x.kb0 / 8; chunk < x.kb1 / 8; ++chunk) {
+        if (!mbar_wait(&s.w_full, w_phase, kErrPrefillWait))
           goto done;
         uint32_t raw[68];
         {
           const uint4* row =
-              reinterpret_cast<const uint4*>(s.w[w.slot] + r * kWRowBytes);
+              reinterpret_cast<const uint4*>(s.w + r * kWRowBytes);
 #pragma unroll
           for (int i = 0; i < 17; ++i) {
             const uint4 v = row[i];
@@ -235,166 +293,176 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0)
-          mbar_arrive(&s.w_empty[w.slot]);
-        w.next(kWStages);
+          mbar_arrive(&s.w_empty);
+        if (loader) {
+          // the next chunk (of this tile, or of this CTA's next unit) once
+          // every converter warp holds this one in registers
+          int nu = u, next = chunk + 1;
+          if (next == x.kb1 / 8) {
+            nu = u + gridDim.x;
+            if (nu < units)
+              next = unit_of(p, nu, token_tiles, bps).kb0 / 8;
+          }
+          if (nu < units) {
+            if (!mbar_wait(&s.w_empty, w_phase, kErrPrefillWait))
+              goto done;
+            load_weights(p, s, unit_of(p, nu, token_tiles, bps).rt, next);
+          }
+        }
+        w_phase ^= 1;
 #pragma unroll
         for (int blk = 0; blk < 8; ++blk) {
           // block blk: d at byte 34 blk, codes at 34 blk + 2
           const int o = 34 * blk;
           const uint32_t dw = raw[o / 4];
           const uint16_t dbits = (o % 4) ? uint16_t(dw >> 16) : uint16_t(dw);
-          uint32_t codes[8];
+          const __half2 d2 = __half2half2(__ushort_as_half(dbits));
+          uint32_t hi[16], lo[16];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int c = o + 2 + 4 * i;
-            codes[i] = (c % 4) ? __funnelshift_r(raw[c / 4], raw[c / 4 + 1], 16)
-                               : raw[c / 4];
+            const uint32_t codes =
+                (c % 4) ? __funnelshift_r(raw[c / 4], raw[c / 4 + 1], 16)
+                        : raw[c / 4];
+            uint32_t q[2];
+            codes_to_half2(codes, q[0], q[1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const __half2 qv = *reinterpret_cast<const __half2*>(&q[h]);
+              const __half2 wh = __hmul2(qv, d2);
+              const __half2 wl = __hfma2(qv, d2, __hneg2(wh));
+              hi[2 * i + h] = *reinterpret_cast<const uint32_t*>(&wh);
+              lo[2 * i + h] = *reinterpret_cast<const uint32_t*>(&wl);
+            }
           }
-          uint32_t h[16];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            codes_to_half2(codes[i], h[2 * i], h[2 * i + 1]);
-          if (!mbar_wait(&s.a_empty[a.slot], a.phase ^ 1, kErrPrefillWait) ||
-              !mbar_wait(&s.d_empty[a.slot], a.phase ^ 1, kErrPrefillWait))
+          if (!mbar_wait(&s.empty[a.slot], a.phase ^ 1, kErrPrefillWait))
             goto done;
-          uint8_t* dst = s.a[a.slot] + r * 64;
+          uint8_t* dh = s.a_hi[a.slot] + r * 64;
+          uint8_t* dl = s.a_lo[a.slot] + r * 64;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(dst + ((c ^ ((r >> 1) & 3)) * 16)) =
-                make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
-          s.d[a.slot][r] = __half2float(__ushort_as_half(dbits));
+          for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(dh + ((c ^ swz) * 16)) =
+                make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2],
+                           hi[4 * c + 3]);
+            *reinterpret_cast<uint4*>(dl + ((c ^ swz) * 16)) =
+                make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2],
+                           lo[4 * c + 3]);
+          }
           fence_proxy_async();
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&s.a_full[a.slot]);
-            mbar_arrive(&s.d_full[a.slot]);
-          }
-          a.next(kASlots);
-        }
-      }
-    }
-  } else if (warp == 5) {
-    // ---- MMA issue
-    if (lane == 0) {
-      Ring a, b, t;
-      for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        for (int kb = 0; kb < blocks; ++kb) {
-          if (!mbar_wait(&s.a_full[a.slot], a.phase, kErrPrefillWait) ||
-              !mbar_wait(&s.b_full[b.slot], b.phase, kErrPrefillWait) ||
-              !mbar_wait(&s.t_empty[t.slot], t.phase ^ 1, kErrPrefillWait))
-            goto done;
-          tc_fence_after();
-          const uint32_t d_tmem = tmem + uint32_t(t.slot * kTN);
-          const uint64_t da = sw64_desc(s.a[a.slot]);
-          const uint64_t db = sw64_desc(s.b[b.slot]);
-          tc_mma(d_tmem, da, db, 0);
-          tc_mma(d_tmem, da + 2, db + 2, 1);  // second K16: +32 bytes
-          tc_commit(&s.a_empty[a.slot]);
-          tc_commit(&s.b_empty[b.slot]);
-          tc_commit(&s.t_full[t.slot]);
-          a.next(kASlots);
-          b.next(kBSlots);
-          t.next(kTBufs);
+          if (lane == 0)
+            mbar_arrive(&s.full[a.slot]);
+          a.next(kStages);
         }
       }
     }
   } else {
-    // ---- epilogue: thread owns weight row r = TMEM lane and token columns
-    // col0 .. col0 + 63
-    const int quarter = warp % 4, col0 = ((warp - 6) / 4) * 64;
+    // ---- epilogue: thread owns TMEM lane r of both accumulators
+    const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    Ring a, t;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const int rt = u / token_tiles, tok0 = (u % token_tiles) * kTN;
-      float2 acc[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        acc[j] = make_float2(0.f, 0.f);
-      for (int kb = 0; kb < blocks; ++kb) {
-        if (!mbar_wait(&s.t_full[t.slot], t.phase, kErrPrefillWait) ||
-            !mbar_wait(&s.d_full[a.slot], a.phase, kErrPrefillWait))
-          goto done;
-        tc_fence_after();
-        const float d = s.d[a.slot][r];
-        const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) +
-                              uint32_t(t.slot * kTN + col0);
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint32_t v[32];
-          tc_ld32(base + q * 32, v);
-          tc_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            fma2(acc[q * 16 + j], d, v[2 * j], v[2 * j + 1]);
-        }
+    int j = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+      const Unit x = unit_of(p, u, token_tiles, bps);
+      const int buf = j & 1;
+      if (!mbar_wait(&s.acc_full[buf], (j >> 1) & 1, kErrPrefillWait))
+        goto done;
+      tc_fence_after();
+      const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) +
+                            uint32_t(buf * 2 * kTN);
+      const int tok0 = x.tt * kTN;
+      const int ntok = min(kTN, p.tokens - tok0);
+      // releases the accumulator pair once its last columns are in registers
+      const auto release = [&] {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s.t_empty[t.slot]);
-          mbar_arrive(&s.d_empty[a.slot]);
-        }
-        a.next(kASlots);
-        t.next(kTBufs);
-      }
-      // ---- unit complete: row scales of the tokens, then the outputs
-      const int ntok = min(kTN, p.tokens - tok0);
-      if (p.kind == kPrefillPlain) {
-        const int j = output_of(p, rt);
-        const int row = (rt - p.first_tile[j]) * kTM + r;
-        if (row < p.o[j].rows) {
-          float* out = p.o[j].out + row;
+        if (lane == 0)
+          mbar_arrive(&s.acc_empty[buf]);
+      };
+      if (p.kind == kPrefillSwiGLU) {
+        const int row = x.rt * kTM + r;
+        const bool valid = row < p.o[0].rows;
+        float* out = p.o[0].out;
+        const int ld = p.o[0].ld;
+        for (int c = 0; c < kTN / 32; ++c) {
+          uint32_t g[32], v[32];
+          tc_ld32(base + c * 32, g);
+          tc_ld32(base + kTN + c * 32, v);
+          // lane i holds the row scale of prompt row c * 32 + i
+          const int tl = c * 32 + lane;
+          const float lane_scale = tl < ntok ? p.scale[tok0 + tl] : 0.f;
+          tc_wait_ld();
+          if (c == kTN / 32 - 1)
+            release();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int t0 = col0 + 2 * c;
-            if (t0 < ntok)
-              out[size_t(tok0 + t0) * p.o[j].ld] = acc[c].x * p.scale[tok0 + t0];
-            if (t0 + 1 < ntok)
-              out[size_t(tok0 + t0 + 1) * p.o[j].ld] =
-                  acc[c].y * p.scale[tok0 + t0 + 1];
-          }
-        }
-      } else {
-        // rows 0-63 gate, 64-127 up of the same 64 indices
-        float* x = s.xch;
-        if (r >= 64)
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            x[(r - 64) * kXchPitch + col0 + 2 * c] = acc[c].x;
-            x[(r - 64) * kXchPitch + col0 + 2 * c + 1] = acc[c].y;
-          }
-        named_barrier(2, 256);
-        const int row = rt * 64 + r;
-        if (r < 64) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const int c = col0 + i;
-            const float scale = c < ntok ? p.scale[tok0 + c] : 0.f;
-            const float gv = (i & 1 ? acc[i / 2].y : acc[i / 2].x) * scale;
-            const float uv = x[r * kXchPitch + c] * scale;
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            const float sc = __shfl_sync(0xffffffffu, lane_scale, i);
+            const float gv = __uint_as_float(g[i]) * sc;
+            const float uv = __uint_as_float(v[i]) * sc;
             // BatchedSwiGLUActivationKernel's formula (hip/ops.hip:175-177)
             const float sig = 1.0F / (1.0F + expf(-gv));
             const float h = (gv * sig) * uv;
-            if (c < ntok && row < p.o[0].rows)
-              p.o[0].out[size_t(tok0 + c) * p.o[0].ld + row] = h;
-            x[r * kXchPitch + c] = row < p.o[0].rows ? fabsf(h) : 0.f;
+            if (valid && t < ntok)
+              out[size_t(tok0 + t) * ld + row] = h;
+            // max |h| over the warp's 32 rows (non-negative floats order as
+            // their bit patterns)
+            const unsigned m = __reduce_max_sync(
+                0xffffffffu, valid ? __float_as_uint(fabsf(h)) : 0u);
+            if (lane == i && t < ntok && p.row_max)
+              atomicMax(p.row_max + tok0 + t, m);
           }
         }
-        named_barrier(2, 256);
-        if (p.row_max) {
-          // two threads per token column, 32 rows each
-          const int e = (warp - 6) * 32 + lane, c = e & 127, r0 = (e >> 7) * 32;
-          if (c < ntok) {
-            float m = 0.f;
-            for (int i = r0; i < r0 + 32; ++i)
-              m = fmaxf(m, x[i * kXchPitch + c]);
-            atomicMax(p.row_max + tok0 + c, __float_as_uint(m));
+        continue;
+      }
+      if (p.splits > 1) {
+        // FP32 partial [prompt row][256 rows] of unit u
+        float* part = p.partial + size_t(u) * (kRows * kTN);
+#pragma unroll 1
+        for (int acc = 0; acc < 2; ++acc) {
+          for (int c = 0; c < kTN / 32; ++c) {
+            uint32_t v[32];
+            tc_ld32(base + acc * kTN + c * 32, v);
+            tc_wait_ld();
+            if (acc == 1 && c == kTN / 32 - 1)
+              release();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              __stcg(part + (c * 32 + i) * kRows + acc * kTM + r,
+                     __uint_as_float(v[i]));
           }
         }
-        named_barrier(2, 256);
+        continue;
+      }
+      const int jo = output_of(p, x.rt);
+      float* out = p.o[jo].out;
+      const int ld = p.o[jo].ld, rows = p.o[jo].rows;
+      const int row0 = (x.rt - p.first_tile[jo]) * kRows;
+#pragma unroll 1
+      for (int acc = 0; acc < 2; ++acc) {
+        const int row = row0 + acc * kTM + r;
+        for (int c = 0; c < kTN / 32; ++c) {
+          uint32_t v[32];
+          tc_ld32(base + acc * kTN + c * 32, v);
+          const int tl = c * 32 + lane;
+          const float lane_scale = tl < ntok ? p.scale[tok0 + tl] : 0.f;
+          tc_wait_ld();
+          if (acc == 1 && c == kTN / 32 - 1)
+            release();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            const float sc = __shfl_sync(0xffffffffu, lane_scale, i);
+            if (row < rows && t < ntok)
+              out[size_t(tok0 + t) * ld + row] = __uint_as_float(v[i]) * sc;
+          }
+        }
       }
     }
   }
 done:
+  // lanes of the producer and MMA warps arrive here at different times: the
+  // warp converges before the CTA barrier, which must count every warp once
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -404,41 +472,151 @@ done:
   }
 }
 
+// Split tiles: out[t][row] = scale[t] * sum over splits, in split order, of
+// the FP32 partials (four rows per thread).
+struct ReduceParams {
+  const float* partial;
+  const float* scale;
+  int splits, token_tiles, tokens, n_out;
+  int first_tile[5];
+  float* out[4];
+  int rows[4];
+  int ld[4];
+};
+
+__global__ void __launch_bounds__(256)
+    prefill_split_reduce_kernel(const __grid_constant__ ReduceParams p) {
+  const int quads = kRows / 4;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;  // tile, t, row quad
+  const int tile = e / (kTN * quads);
+  const int t = (e / quads) % kTN, q = e % quads;
+  const int tt = tile % p.token_tiles, rt = tile / p.token_tiles;
+  const int tok = tt * kTN + t;
+  if (rt >= p.first_tile[p.n_out] || tok >= p.tokens)
+    return;
+  int j = 0;
+#pragma unroll
+  for (int o = 1; o < 4; ++o)
+    if (o < p.n_out && rt >= p.first_tile[o])
+      j = o;
+  const float4* src = reinterpret_cast<const float4*>(
+      p.partial + size_t(tile) * p.splits * (kRows * kTN) + t * kRows) + q;
+  float4 sum = __ldcg(src);
+  for (int sp = 1; sp < p.splits; ++sp) {
+    const float4 v = __ldcg(src + size_t(sp) * (kRows * kTN / 4));
+    sum.x += v.x;
+    sum.y += v.y;
+    sum.z += v.z;
+    sum.w += v.w;
+  }
+  const float sc = p.scale[tok];
+  const int row = (rt - p.first_tile[j]) * kRows + 4 * q;
+  float* out = p.out[j] + size_t(tok) * p.ld[j];
+  const float v[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (row + i < p.rows[j])
+      out[row + i] = v[i] * sc;
+}
+
 }  // namespace
 
 cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
                               cudaStream_t stream) {
-  static bool configured = false;
-  const int smem = int(sizeof(PrefillSmem)) + 1024;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        q8_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        smem);
-    if (e != cudaSuccess)
-      return e;
-    configured = true;
-  }
-  if (p.K % 256 || p.tokens <= 0)
-    return cudaErrorInvalidValue;
-  const size_t row_bytes = size_t(p.K / 32) * 34;
-  const int outputs = p.kind == kPrefillPlain ? p.n_out : 2;
-  for (int j = 0; j < outputs; ++j) {
-    const cudaError_t e =
-        encode_row_map(&p.w_maps[j], p.o[j].w, row_bytes, p.o[j].rows,
-                       kWRowBytes, p.kind == kPrefillPlain ? kTM : 64);
-    if (e != cudaSuccess)
-      return e;
-  }
-  cudaError_t e = encode_activation_map(&p.x_map, x, x_rows, p.K, kTN, 32);
+  int device = 0, sms = 148;
+  cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess)
     return e;
-  int device = 0, sms = 148;
-  cudaGetDevice(&device);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  const int units = p.row_tiles * ((p.tokens + kTN - 1) / kTN);
+  const int smem = int(sizeof(PrefillSmem)) + 1024;
+  static bool configured[64] = {};
+  if (device < 0 || device >= 64)
+    return cudaErrorInvalidDevice;
+  if (!configured[device]) {
+    e = cudaFuncSetAttribute(q8_prefill_tc_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+      return e;
+    configured[device] = true;
+  }
+  if (p.K <= 0 || p.K % 256 || p.tokens <= 0 || !x || !p.scale ||
+      x_rows < p.x_row0 + p.tokens)
+    return cudaErrorInvalidValue;
+  const size_t row_bytes = size_t(p.K / 32) * 34;
+  const int token_tiles = (p.tokens + kTN - 1) / kTN;
+  p.splits = 1;
+  if (p.kind == kPrefillPlain) {
+    if (p.n_out < 1 || p.n_out > 4)
+      return cudaErrorInvalidValue;
+    int tiles = 0;
+    for (int j = 0; j < p.n_out; ++j) {
+      if (!p.o[j].w || !p.o[j].out || p.o[j].rows <= 0)
+        return cudaErrorInvalidValue;
+      p.first_tile[j] = tiles;
+      tiles += (p.o[j].rows + kRows - 1) / kRows;
+      e = cached_q8_rows(&p.w_maps[j], p.o[j].w, row_bytes, p.o[j].rows,
+                         kWRowBytes, kRows);
+      if (e != cudaSuccess)
+        return e;
+    }
+    for (int j = p.n_out; j < 5; ++j)
+      p.first_tile[j] = tiles;
+    p.row_tiles = tiles;
+    // split K when the tiles leave SMs idle: fewest waves x K range
+    if (p.partial) {
+      const int stages = p.K / 256, all = tiles * token_tiles;
+      long best = long((all + sms - 1) / sms) * stages;
+      for (int sp = 2; sp <= 8; sp *= 2) {
+        if (stages % sp || all * sp > kPrefillMaxSplitUnits)
+          continue;
+        const long cost = long((all * sp + sms - 1) / sms) * (stages / sp);
+        if (cost < best) {
+          best = cost;
+          p.splits = sp;
+        }
+      }
+    }
+  } else {
+    if (!p.o[0].w || !p.o[1].w || !p.o[0].out ||
+        p.o[0].rows != p.o[1].rows || p.o[0].rows <= 0)
+      return cudaErrorInvalidValue;
+    p.n_out = 2;
+    p.row_tiles = (p.o[0].rows + kTM - 1) / kTM;
+    for (int j = 0; j < 2; ++j) {
+      e = cached_q8_rows(&p.w_maps[j], p.o[j].w, row_bytes, p.o[j].rows,
+                         kWRowBytes, kTM);
+      if (e != cudaSuccess)
+        return e;
+    }
+  }
+  e = cached_activation_map(&p.x_map, x, x_rows, p.K, kTN, 32);
+  if (e != cudaSuccess)
+    return e;
+  const int units = p.row_tiles * token_tiles * p.splits;
   note_launch();
   q8_prefill_tc_kernel<<<units < sms ? units : sms, kThreads, smem, stream>>>(
       p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.splits == 1)
+    return e;
+  ReduceParams r{};
+  r.partial = p.partial;
+  r.scale = p.scale;
+  r.splits = p.splits;
+  r.token_tiles = token_tiles;
+  r.tokens = p.tokens;
+  r.n_out = p.n_out;
+  for (int j = 0; j < 5; ++j)
+    r.first_tile[j] = p.first_tile[j];
+  for (int j = 0; j < p.n_out; ++j) {
+    r.out[j] = p.o[j].out;
+    r.rows[j] = p.o[j].rows;
+    r.ld[j] = p.o[j].ld;
+  }
+  const long threads = long(p.row_tiles) * token_tiles * kTN * (kRows / 4);
+  note_launch();
+  prefill_split_reduce_kernel<<<unsigned((threads + 255) / 256), 256, 0,
+                                stream>>>(r);
   return cudaGetLastError();
 }
 

@@ -1,11 +1,12 @@
 // Q8_0 projections of prompt rows (16..512 per pass) with FP16 row-scaled
 // activations: y[t][m] = scale[t] * sum_b d[m][b] * (sum_{k in b} q[m][k] *
-// x16[t][k]), FP32 accumulation per K32 block (hip/q8_prefill.hpp:94-645,
-// RegQ8Gemm / TiledQ8Gemm, and LaunchSplit, hip/ops.hip:2039-2119).
+// x16[t][k]), FP32 accumulation (hip/q8_prefill.hpp:94-645, RegQ8Gemm /
+// TiledQ8Gemm, and LaunchSplit, hip/ops.hip:2039-2119).
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace lfm3 {
@@ -15,6 +16,17 @@ enum PrefillKind : int {
   kPrefillSwiGLU = 1,  // o[0] gate, o[1] up: out = silu(g) * u, row maxima
 };
 
+// A work tile is 256 weight rows (two tensor-memory accumulators of 128)
+// by 128 prompt rows; SwiGLU tiles pair 128 gate rows with the same 128 up
+// rows.
+constexpr int kPrefillTileRows = 256;
+constexpr int kPrefillTileTokens = 128;
+// Split-K: at most this many (tile, K range) units keep FP32 partial sums
+// (hip/ops.hpp:17-21, kMaxSplitUnits).
+constexpr int kPrefillMaxSplitUnits = 192;
+constexpr size_t kPrefillPartialFloats =
+    size_t(kPrefillMaxSplitUnits) * kPrefillTileRows * kPrefillTileTokens;
+
 struct PrefillOutput {
   const uint8_t* w;
   float* out;  // [tokens][ld]
@@ -23,10 +35,10 @@ struct PrefillOutput {
 };
 
 struct PrefillParams {
-  // TMA maps: weights as [rows][row_bytes / 16][16] with boxes of 272-byte
-  // chunks (128 rows for Plain, 64 rows for SwiGLU gate and up), and the
-  // activations as [rows of the buffer][K] fp16 with 128 x 32 boxes,
-  // 64-byte swizzle.
+  // TMA maps (filled by launch_q8_prefill): weights as [rows][row_bytes / 8]
+  // 8-byte elements with boxes of 34 elements (8 blocks) x 256 rows (128
+  // for SwiGLU gate and up), and the activations as [rows of the buffer][K]
+  // fp16 with 128 x 32 boxes, 64-byte swizzle.
   alignas(64) CUtensorMap w_maps[4];
   alignas(64) CUtensorMap x_map;
   int kind;
@@ -35,14 +47,20 @@ struct PrefillParams {
   int x_row0;   // first activation row of this pass in x_map
   int n_out;
   PrefillOutput o[4];
-  int first_tile[5];  // row tiles (128 rows) of each output
+  // filled by launch_q8_prefill
+  int first_tile[5];  // 256-row tiles of each output (Plain)
   int row_tiles;
+  int splits;         // K ranges per tile
   const float* scale;   // [tokens]
   unsigned* row_max;    // SwiGLU: FP32 bits of each row's max |out|
+  // Optional split-K workspace of kPrefillPartialFloats floats (16-byte
+  // aligned); without it no projection splits K.
+  float* partial;
 };
 
-// Fills p.w_maps and p.x_map (x is [x_rows][K] fp16; the pass reads rows
-// x_row0 .. x_row0 + tokens - 1) and launches.
+// Fills the maps and the tiling of p (x is [x_rows][K] fp16; the pass reads
+// rows x_row0 .. x_row0 + tokens - 1) and launches. K must be a multiple of
+// 256.
 cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
                               cudaStream_t stream);
 

