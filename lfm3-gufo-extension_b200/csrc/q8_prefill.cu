@@ -393,24 +393,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_wait_ld();
           if (c == kTN / 32 - 1)
             release();
+          // independent per prompt row: activation, store, |h| bits
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int t = c * 32 + i;
             const float sc = __shfl_sync(0xffffffffu, lane_scale, i);
             const float gv = __uint_as_float(g[i]) * sc;
             const float uv = __uint_as_float(v[i]) * sc;
-            // BatchedSwiGLUActivationKernel's formula (hip/ops.hip:175-177)
-            const float sig = 1.0F / (1.0F + expf(-gv));
+            // BatchedSwiGLUActivationKernel's formula (hip/ops.hip:175-177);
+            // __frcp_rn is the correctly rounded 1 / x
+            const float sig = __frcp_rn(1.0F + expf(-gv));
             const float h = (gv * sig) * uv;
-            if (valid && t < ntok)
-              out[size_t(tok0 + t) * ld + row] = h;
-            // max |h| over the warp's 32 rows (non-negative floats order as
-            // their bit patterns)
-            const unsigned m = __reduce_max_sync(
-                0xffffffffu, valid ? __float_as_uint(fabsf(h)) : 0u);
-            if (lane == i && t < ntok && p.row_max)
-              atomicMax(p.row_max + tok0 + t, m);
+            if (valid && c * 32 + i < ntok)
+              out[size_t(tok0 + c * 32 + i) * ld + row] = h;
+            g[i] = valid ? __float_as_uint(fabsf(h)) : 0u;
           }
+          // max |h| over the warp's 32 rows per prompt row (non-negative
+          // floats order as their bit patterns); lane i keeps row i's
+          unsigned mine = 0;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const unsigned m = __reduce_max_sync(0xffffffffu, g[i]);
+            mine = lane == i ? m : mine;
+          }
+          if (tl < ntok && p.row_max)
+            atomicMax(p.row_max + tok0 + tl, mine);
         }
         continue;
       }
