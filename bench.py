@@ -278,6 +278,66 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# ---- ranks (one process per GPU under torchrun) ------------------------------------------------
+class Ranks:
+    """Rank plumbing of a replicas-only job: RANK / WORLD_SIZE / LOCAL_RANK from
+    the torchrun environment, a MAX over ranks and a barrier. Only timings
+    cross ranks: each rank runs its own model replica and sessions."""
+
+    def __init__(self, backend="nccl"):
+        import torch
+        import torch.distributed as dist
+        self.dist, self.torch = dist, torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.device = torch.device("cuda", self.local) if backend == "nccl" else torch.device("cpu")
+        if backend == "nccl":
+            torch.cuda.set_device(self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            extra = {"device_id": self.device} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=timedelta(seconds=300), **extra)
+
+    def sync_max(self, value):
+        if self.world == 1:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sync_sum(self, value):
+        if self.world == 1:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def barrier(self):
+        if self.device.type == "cuda":
+            self.torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier()
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+def rank_workload(rank, prompt_max, vocab):
+    """This rank's 8 sessions: prompt lengths U[64, prompt_max] and tokens, from
+    seed (1, rank), so ranks hold different sessions."""
+    rng = np.random.default_rng([1, rank])
+    lengths = rng.integers(PROMPT_RANGE[0], prompt_max + 1, SESSIONS)
+    prompts = [rng.integers(0, vocab, int(n)).astype(np.uint32) for n in lengths]
+    return lengths, prompts
+
+
+def job_rate(tokens_per_rank, world, max_ms):
+    """Whole-job throughput: every rank's tokens over the slowest rank's time."""
+    return tokens_per_rank * world / (max_ms / 1e3)
+
+
 # ---- our arm ---------------------------------------------------------------------------------
 def main():
     args = parse()
@@ -285,38 +345,18 @@ def main():
         reference_arm(args)
         return
     import torch
-    import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-
-    def sync_max(value):
-        if world == 1:
-            return value
-        t = torch.tensor([value], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+    ranks = Ranks("nccl")
+    world, rank, local = ranks.world, ranks.rank, ranks.local
+    sync_max, barrier = ranks.sync_max, ranks.barrier
 
     lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
     weights = lfm3.SyntheticWeights(seed=0)
     cfg = weights.config
     model = lfm3.Model(weights.weights)
-    rng = np.random.default_rng([1, rank])
-    lengths = rng.integers(PROMPT_RANGE[0], args.prompt_max + 1, SESSIONS)
+    lengths, prompts = rank_workload(rank, args.prompt_max, cfg.vocab)
     total_steps = args.warmup * 2 + args.steps * 3 + 8
     sessions = [model.session(int(n) + total_steps + 16) for n in lengths]
-    prompts = [rng.integers(0, cfg.vocab, int(n)).astype(np.uint32) for n in lengths]
 
     def stream_of(s):
         return torch.cuda.ExternalStream(s.stream)
@@ -429,13 +469,11 @@ def main():
                "sample": f"{threads} sessions x 2 decode tokens at depth 3, one session "
                          f"per host thread ({elapsed:.1f} s)"}
 
-    tokens_all = SESSIONS * world * args.steps
-    value = tokens_all / (decode_ms_max / 1e3)
-    e2e = tokens_all / (e2e_ms_max / 1e3)
-    prefill_rate = prefill_tokens * world / (sync_max(prefill_ms) / 1e3)
+    value = job_rate(SESSIONS * args.steps, world, decode_ms_max)
+    e2e = job_rate(SESSIONS * args.steps, world, e2e_ms_max)
+    prefill_rate = ranks.sync_sum(prefill_tokens) / (sync_max(prefill_ms) / 1e3)
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
+        ranks.close()
         return
     clocks = sampler.summary()
     line = {
@@ -493,8 +531,7 @@ def main():
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    ranks.close()
 
 
 if __name__ == "__main__":

@@ -53,7 +53,7 @@ int GemvRows(lfm3::GemvParams p, const float* x, int n, int K,
   if (!ws.quantized)
     return Fail(LFM3_ERR_INVALID, "workspace needs quantized");
   p.K = K;
-  if (!lfm3::gemv_plan(p))
+  if (!lfm3::gemv_plan(p, Sms()))
     return Fail(LFM3_ERR_UNSUPPORTED, "projection width not tiled");
   if (int e = Cuda(lfm3::launch_split_rows(x, ws.quantized, n, K, s)))
     return e;

@@ -181,7 +181,7 @@ const CUtensorMap& Model::RowMap(const lfm3_tensor& t, int chunk_bytes,
   auto it = maps_.find(key);
   if (it == maps_.end()) {
     CUtensorMap map;
-    Throw(encode_row_map(&map, t.data, size_t(t.cols) / 32 * 34, int(t.rows),
+    Throw(encode_q8_rows(&map, t.data, size_t(t.cols) / 32 * 34, int(t.rows),
                          chunk_bytes, box_rows));
     it = maps_.emplace(key, map).first;
   }
@@ -342,12 +342,13 @@ void Session::TakeProfile(double* ms, long long* launches) {
 
 // Launches one projection of the round's rows (split input x).
 static cudaError_t RunGemv(GemvParams p, Model& model, cudaStream_t stream) {
-  if (!gemv_plan(p))
+  if (!gemv_plan(p, model.sms()))
     return cudaErrorInvalidValue;
   const int maps = p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
   for (int j = 0; j < maps; ++j) {
     lfm3_tensor t{p.o[j].w, LFM3_Q8_0, uint32_t(p.K), uint32_t(p.o[j].rows), 0};
-    p.maps[j] = model.RowMap(t, gemv_pitch_units(p.chunk_blocks) * 16, 16);
+    p.maps[j] = model.RowMap(t, gemv_pitch_units(p.chunk_blocks) * 16,
+                             gemv_box_rows(p));
   }
   return launch_q8_gemv(p, gemv_grid(p.tiles, model.sms()), stream, true);
 }

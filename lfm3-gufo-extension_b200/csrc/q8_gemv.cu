@@ -28,7 +28,7 @@ namespace lfm3 {
 
 namespace {
 
-constexpr int kMaxTileRows = 48;
+constexpr int kMaxTileRows = 64;
 
 struct GemvSmem {
   uint8_t stage[kGemvStages][kGemvStageBytes];
@@ -38,32 +38,37 @@ struct GemvSmem {
   uint64_t empty[kGemvStages];
 };
 
-template <int kKind, int kBlocks>
+template <int kMT, int kBlocks>
 __device__ __forceinline__ uint32_t stage_bytes() {
-  return gemv_mtiles(kKind) * 16 * gemv_pitch_units(kBlocks) * 16;
+  return kMT * 16 * gemv_pitch_units(kBlocks) * 16;
 }
 
-// Issues the tiled copies of (tile t, chunk c) into dst (one 16-row box per
-// m-tile; boxes past the matrix are zero-filled and still count).
-template <int kKind, int kBlocks>
+// Issues the tiled copies of (tile t, chunk c) into dst (Plain: one box of
+// the tile's 16 x kMT rows; otherwise one 16-row box per m-tile; boxes past
+// the matrix are zero-filled and still count). The maps view each weight as
+// [rows][row_bytes / 8] 8-byte elements, so a box row is one contiguous run
+// of the chunk (plus its padding) and lands as one shared-memory row.
+template <int kKind, int kBlocks, int kMT>
 __device__ __forceinline__ void load_unit(const GemvParams& p, int t, int c,
                                           uint8_t* dst, uint64_t* bar) {
   constexpr int kBox = 16 * gemv_pitch_units(kBlocks) * 16;
-  const int x1 = c * (kBlocks * 34 / 16);
+  // chunk c starts at byte 34 * kBlocks * c of each row: in 8-byte
+  // elements an even coordinate, so the copy starts 16-byte aligned
+  const int x8 = c * (kBlocks * 34 / 8);
   if (kKind == kGemvPlain) {
     int j = 0;
 #pragma unroll
     for (int q = 1; q < 4; ++q)
       if (q < p.n_out && t >= p.first_tile[q])
         j = q;
-    tma_load_3d(dst, &p.maps[j], 0, x1, (t - p.first_tile[j]) * 16, bar);
+    tma_load_2d(dst, &p.maps[j], x8, (t - p.first_tile[j]) * 16 * kMT, bar);
   } else if (kKind == kGemvSwiGLU) {
-    tma_load_3d(dst, &p.maps[0], 0, x1, t * 16, bar);
-    tma_load_3d(dst + kBox, &p.maps[1], 0, x1, t * 16, bar);
+    tma_load_2d(dst, &p.maps[0], x8, t * 16, bar);
+    tma_load_2d(dst + kBox, &p.maps[1], x8, t * 16, bar);
   } else {
 #pragma unroll
     for (int part = 0; part < 3; ++part)
-      tma_load_3d(dst + part * kBox, &p.maps[0], 0, x1, part * p.H + t * 16,
+      tma_load_2d(dst + part * kBox, &p.maps[0], x8, part * p.H + t * 16,
                   bar);
   }
 }
@@ -121,23 +126,26 @@ __device__ __forceinline__ void run_block(const uint8_t* block, int pitch,
   }
 }
 
-template <int kKind>
+template <int kKind, int kMT>
 __device__ void gemv_epilogue(const GemvParams& p, const float* tile, int t,
                               int tid) {
-  const int i = tid / kMaxBatch, tok = tid % kMaxBatch;  // 16 rows x 8
-  if (i >= 16 || tok >= p.tokens)
-    return;
   if (kKind == kGemvPlain) {
     int j = 0;
 #pragma unroll
     for (int q = 1; q < 4; ++q)
       if (q < p.n_out && t >= p.first_tile[q])
         j = q;
-    const int row = (t - p.first_tile[j]) * 16 + i;
-    if (row < p.o[j].rows)
-      p.o[j].out[size_t(tok) * p.o[j].ld + row] = tile[i * kMaxBatch + tok];
+    for (int e = tid; e < kMT * 16 * kMaxBatch; e += kGemvWarps * 32) {
+      const int i = e / kMaxBatch, tok = e % kMaxBatch;
+      const int row = (t - p.first_tile[j]) * 16 * kMT + i;
+      if (tok < p.tokens && row < p.o[j].rows)
+        p.o[j].out[size_t(tok) * p.o[j].ld + row] = tile[e];
+    }
     return;
   }
+  const int i = tid / kMaxBatch, tok = tid % kMaxBatch;  // 16 rows x 8
+  if (i >= 16 || tok >= p.tokens)
+    return;
   if (kKind == kGemvSwiGLU) {
     const int row = t * 16 + i;
     if (row >= p.o[0].rows)
@@ -176,9 +184,8 @@ __device__ void gemv_epilogue(const GemvParams& p, const float* tile, int t,
   store_split(p.split_out, tok, p.split_width, ch, sum * c);
 }
 
-template <int kKind, int kBlocks>
+template <int kKind, int kBlocks, int kMT>
 __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
-  constexpr int kMT = gemv_mtiles(kKind);
   constexpr int kPitch = gemv_pitch_units(kBlocks) * 16;
   static_assert(kMT * 16 * kPitch <= kGemvStageBytes, "stage overflow");
   constexpr int kPerWarp = kBlocks / kGemvWarps;  // even: 8, 4 or 2
@@ -196,8 +203,9 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
       for (int c = 0; c < chunks; ++c) {
         if (!mbar_wait(&s.empty[stage], phase ^ 1, kErrGemvEmptyWait))
           return;
-        mbar_arrive_expect_tx(&s.full[stage], stage_bytes<kKind, kBlocks>());
-        load_unit<kKind, kBlocks>(p, t, c, s.stage[stage], &s.full[stage]);
+        mbar_arrive_expect_tx(&s.full[stage], stage_bytes<kMT, kBlocks>());
+        load_unit<kKind, kBlocks, kMT>(p, t, c, s.stage[stage],
+                                       &s.full[stage]);
         if (++stage == kGemvStages) {
           stage = 0;
           phase ^= 1;
@@ -285,7 +293,7 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
       s.tile[e] = v;
     }
     named_barrier(1, kGemvWarps * 32);
-    gemv_epilogue<kKind>(p, s.tile, t, tid);
+    gemv_epilogue<kKind, kMT>(p, s.tile, t, tid);
   }
 }
 
@@ -303,37 +311,47 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   __syncthreads();
   allow_dependents();
   if (p.kind == kGemvPlain) {
-    if (p.chunk_blocks == 64)
-      gemv_body<kGemvPlain, 64>(p, s);
+    if (p.wide)
+      gemv_body<kGemvPlain, 16, 4>(p, s);
+    else if (p.chunk_blocks == 32)
+      gemv_body<kGemvPlain, 32, 1>(p, s);
     else
-      gemv_body<kGemvPlain, 16>(p, s);
+      gemv_body<kGemvPlain, 16, 1>(p, s);
   } else if (p.kind == kGemvSwiGLU) {
     if (p.chunk_blocks == 32)
-      gemv_body<kGemvSwiGLU, 32>(p, s);
+      gemv_body<kGemvSwiGLU, 32, 2>(p, s);
     else
-      gemv_body<kGemvSwiGLU, 16>(p, s);
+      gemv_body<kGemvSwiGLU, 16, 2>(p, s);
   } else {
-    gemv_body<kGemvConv, 16>(p, s);
+    gemv_body<kGemvConv, 16, 3>(p, s);
   }
 }
 
 }  // namespace
 
-bool gemv_plan(GemvParams& p) {
+bool gemv_plan(GemvParams& p, int sms) {
   if (p.K <= 0 || p.K % 512)
     return false;
-  if (p.kind == kGemvPlain)
-    p.chunk_blocks = p.K % 2048 == 0 ? 64 : 16;
-  else if (p.kind == kGemvSwiGLU)
+  p.wide = 0;
+  if (p.kind == kGemvPlain) {
+    int wide_tiles = 0;
+    for (int j = 0; j < p.n_out; ++j)
+      wide_tiles += (p.o[j].rows + 63) / 64;
+    // two or more 64-row tiles for each of the 2 x sms CTA slots
+    p.wide = wide_tiles >= 4 * sms;
+    p.chunk_blocks = p.wide ? 16 : p.K % 1024 == 0 ? 32 : 16;
+  } else if (p.kind == kGemvSwiGLU) {
     p.chunk_blocks = p.K % 1024 == 0 ? 32 : 16;
-  else
+  } else {
     p.chunk_blocks = 16;
+  }
   p.chunks = p.K / (32 * p.chunk_blocks);
   if (p.kind == kGemvPlain) {
     int tiles = 0;
+    const int rows = p.wide ? 64 : 16;
     for (int j = 0; j < p.n_out; ++j) {
       p.first_tile[j] = tiles;
-      tiles += (p.o[j].rows + 15) / 16;
+      tiles += (p.o[j].rows + rows - 1) / rows;
     }
     p.first_tile[p.n_out] = tiles;
     p.tiles = tiles;
@@ -356,14 +374,19 @@ int gemv_grid(int tiles, int sms) {
   return tiles < sms ? tiles : sms;
 }
 
+int gemv_box_rows(const GemvParams& p) {
+  return p.kind == kGemvPlain && p.wide ? 64 : 16;
+}
+
 cudaError_t fill_gemv_maps(GemvParams& p) {
   const size_t row_bytes = size_t(p.K / 32) * 34;
   const int outputs =
       p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
   for (int j = 0; j < outputs; ++j) {
     const cudaError_t e =
-        encode_row_map(&p.maps[j], p.o[j].w, row_bytes, p.o[j].rows,
-                       gemv_pitch_units(p.chunk_blocks) * 16, 16);
+        encode_q8_rows(&p.maps[j], p.o[j].w, row_bytes, p.o[j].rows,
+                       gemv_pitch_units(p.chunk_blocks) * 16,
+                       gemv_box_rows(p));
     if (e != cudaSuccess)
       return e;
   }

@@ -13,7 +13,8 @@ namespace lfm3 {
 
 enum GemvKind : int {
   // out[token * ld + row] for up to four weights sharing the input;
-  // tile = 16 rows of one weight, chunks of 64 Q8 blocks (2048 columns)
+  // tile = 16 rows of one weight (64 for tall projections), chunks of 32 Q8
+  // blocks (1024 columns) or 16
   kGemvPlain = 0,
   // tile = 16 gate rows + the same 16 up rows, chunks of 32 blocks; writes
   // silu(g) * u as split activations of width F (and/or FP32)
@@ -24,17 +25,19 @@ enum GemvKind : int {
   kGemvConv = 2,
 };
 
-// m-tiles (16 rows each) of a tile; the 16-byte units a row occupies in
+// m-tiles (16 rows each) of a tile: Plain 1, or 4 for projections with at
+// least two 64-row tiles per CTA slot (the input fragments of a block then
+// serve four m-tiles); SwiGLU 2; Conv 3. The 16-byte units a row occupies in
 // shared memory for chunks of `blocks` Q8 blocks (the chunk plus padding
 // that spreads the rows of a warp's fragment loads over the banks).
-constexpr __host__ __device__ int gemv_mtiles(int kind) {
-  return kind == kGemvPlain ? 1 : kind == kGemvSwiGLU ? 2 : 3;
+constexpr __host__ __device__ int gemv_mtiles(int kind, int wide = 0) {
+  return kind == kGemvPlain ? (wide ? 4 : 1) : kind == kGemvSwiGLU ? 2 : 3;
 }
 constexpr __host__ __device__ int gemv_pitch_units(int blocks) {
   return blocks * 34 / 16 + ((blocks * 34 / 16) % 4 == 0 ? 2 : 0);
 }
 
-constexpr int kGemvStageBytes = 35840;  // max over kinds of rows x pitch
+constexpr int kGemvStageBytes = 36864;  // max over kinds of rows x pitch
 constexpr int kGemvStages = 2;
 constexpr int kGemvWarps = 8;  // consumer warps
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
@@ -47,14 +50,15 @@ struct GemvOutput {
 };
 
 struct GemvParams {
-  // TMA maps over the weight rows (tensor_map.hpp), 16-row boxes of
-  // gemv_pitch_units(chunk_blocks) 16-byte units: Plain one per output,
-  // SwiGLU gate and up, Conv in_proj.
+  // TMA maps over the weight rows (encode_q8_rows, tensor_map.hpp): boxes of
+  // gemv_box_rows(p) rows x gemv_pitch_units(chunk_blocks) * 16 bytes: Plain
+  // one per output, SwiGLU gate and up, Conv in_proj.
   alignas(64) CUtensorMap maps[4];
   int kind;
   int K;             // columns
   int chunk_blocks;  // Q8 blocks per chunk (64, 32 or 16; gemv_plan)
   int chunks;        // K / (32 * chunk_blocks)
+  int wide;          // Plain: 64-row tiles (chunks of 16 blocks)
   int tiles;
   int tokens;   // 1..8
   int n_out;
@@ -71,10 +75,14 @@ struct GemvParams {
   int L;
 };
 
-// Fills p.chunk_blocks, p.chunks, p.tiles and p.first_tile from the kind,
-// K and outputs (Plain chunks of 64 blocks when K allows, else 16; SwiGLU 32
-// or 16; Conv 16); returns false for widths that are not multiples of 512.
-bool gemv_plan(GemvParams& p);
+// Fills p.chunk_blocks, p.chunks, p.wide, p.tiles and p.first_tile from the
+// kind, K, outputs and the SM count (Plain: 64-row tiles in chunks of 16
+// blocks when there are at least two per CTA slot, else 16-row tiles in
+// chunks of 32 blocks when K allows, else 16; SwiGLU 32 or 16; Conv 16);
+// returns false for widths that are not multiples of 512.
+bool gemv_plan(GemvParams& p, int sms);
+// Rows of one TMA box (16 x m-tiles of a Plain tile, 16 otherwise).
+int gemv_box_rows(const GemvParams& p);
 int gemv_grid(int tiles, int sms);
 // Encodes p.maps from p.o[j].w / rows / K (host; for callers without a map
 // cache).

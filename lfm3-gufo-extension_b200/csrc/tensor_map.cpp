@@ -32,29 +32,6 @@ EncodeTiled Encoder() {
 
 }  // namespace
 
-cudaError_t encode_row_map(CUtensorMap* map, const void* base,
-                           size_t row_bytes, int rows, int chunk_bytes,
-                           int box_rows) {
-  const EncodeTiled encode = Encoder();
-  if (!encode)
-    return cudaErrorNotSupported;
-  if (row_bytes % 16 || chunk_bytes % 16 || chunk_bytes / 16 > 256 ||
-      box_rows < 1 || box_rows > 256 || rows < 1 ||
-      reinterpret_cast<uintptr_t>(base) % 16)
-    return cudaErrorInvalidValue;
-  const cuuint64_t dims[3] = {16, row_bytes / 16, cuuint64_t(rows)};
-  const cuuint64_t strides[2] = {16, row_bytes};
-  const cuuint32_t box[3] = {16, cuuint32_t(chunk_bytes / 16),
-                             cuuint32_t(box_rows)};
-  const cuuint32_t element_strides[3] = {1, 1, 1};
-  const CUresult r = encode(
-      map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims,
-      strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
 cudaError_t encode_q8_rows(CUtensorMap* map, const void* base, size_t row_bytes,
                            int rows, int box_bytes, int box_rows) {
   const EncodeTiled encode = Encoder();

@@ -1,7 +1,7 @@
-// TMA tensor maps over Q8_0 weight rows: the bytes of a matrix viewed as a
-// 3-D tensor [rows][row_bytes / 16][16], so one tiled copy moves a box of
-// up to 256 rows x (17 x 16) bytes (one 256-column chunk of each row) into
-// shared memory as dense 272-byte rows. Rows past the matrix read as zeros.
+// TMA tensor maps: Q8_0 weight rows viewed as [rows][row_bytes / 8] 8-byte
+// elements (one copy lands a box of rows as dense shared-memory rows of the
+// box width; rows and columns past the matrix read as zeros), and fp16
+// activation rows with the 64-byte swizzle of the tcgen05 operand layout.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -10,14 +10,6 @@
 #include <cstdint>
 
 namespace lfm3 {
-
-// Encodes a map over `rows` rows of `row_bytes` bytes (a multiple of 16)
-// starting at base (16-byte aligned), with boxes of box_rows rows and
-// chunk_bytes (a multiple of 16, <= 4096) per row. Returns cudaSuccess or the
-// error of the driver call.
-cudaError_t encode_row_map(CUtensorMap* map, const void* base,
-                           size_t row_bytes, int rows, int chunk_bytes,
-                           int box_rows);
 
 // Encodes a map over Q8_0 rows viewed as [rows][row_bytes / 8] 8-byte
 // elements (row_bytes a multiple of 16), boxes of box_bytes (a multiple of

@@ -107,6 +107,30 @@ def test_projection(n):
     near(host(out).reshape(n, M), expected, 1e-4)
 
 
+@pytest.mark.parametrize("n", [1, 5, 8])
+def test_projection_tall(n):
+    """Decode projections of matrices tall enough for 64-row tiles (more than
+    four per SM), with a ragged last tile."""
+    M, K = 4 * 148 * 64 + 37, 512
+    nb = M * K // 32
+    i = np.arange(nb)
+    d = (0x2400 + 32 * (i % 10)).astype(np.uint16)
+    j = np.arange(32)
+    qs = ((i[:, None] * 17 + j[None, :] * 37) % 255 - 127).astype(np.int8)
+    blocks = np.zeros((nb, 34), np.uint8)
+    blocks[:, :2] = d.view(np.uint8).reshape(nb, 2)
+    blocks[:, 2:] = qs.view(np.uint8)
+    x = data(n * K, 0.07).reshape(n, K)
+    w = (d.view(np.float16).astype(np.float64)[:, None] * qs).reshape(M, K)
+    expected = x.astype(np.float64) @ w.T
+    t, keep = q8_tensor(blocks.tobytes(), K, M)
+    dx, out = dev(x), torch.empty(n * M, dtype=torch.float32, device="cuda")
+    ws, keep2 = workspace(n, K)
+    lfm3.check(lib.lfm3_cuda_dense(ctypes.byref(t), ptr(dx), ptr(out), n, None,
+                                   ctypes.byref(ws)))
+    near(host(out).reshape(n, M), expected, 1e-4)
+
+
 # ---- ShortConv (tests/ops_test.cpp:90-116) ------------------------------------
 @pytest.mark.parametrize("n", [1, 8, 9, 15, 16, 29, 32, 33, 128, 512])
 def test_conv(n):
