@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt-max", type=int, default=PROMPT_RANGE[1])
+    ap.add_argument("--profile", action="store_true",
+                    help="no timing: a fixed launch sequence for ncu captures "
+                         "(see profile_sequence)")
     return ap.parse_args()
 
 
@@ -338,11 +341,45 @@ def job_rate(tokens_per_rank, world, max_ms):
     return tokens_per_rank * world / (max_ms / 1e3)
 
 
+# ---- profiling sequence ----------------------------------------------------------------------
+PROFILE_PROMPT = 64
+PROFILE_WARM_ROUNDS = 3
+
+
+def profile_sequence():
+    """A fixed, untimed launch sequence for ncu: 8 sessions prefilled with
+    64-token prompts (one prompt pass each, whose last row's logits take one
+    LM-head q8_gemv launch), 3 warm decode rounds, then the captured work: one
+    decode round of the 8 rows, then one 512-row prompt pass on session 0.
+    Before the captured round: 8 + 3 x 97 = 299 q8_gemv launches and
+    8 x 96 = 768 q8_prefill_tc_kernel launches (24 layers: 4 projection
+    launches per layer)."""
+    import torch
+    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
+    weights = lfm3.SyntheticWeights(seed=0)
+    cfg = weights.config
+    model = lfm3.Model(weights.weights)
+    rng = np.random.default_rng([1, 0])
+    sessions = [model.session(1024) for _ in range(SESSIONS)]
+    for s in sessions:
+        s.forward(rng.integers(0, cfg.vocab, PROFILE_PROMPT).astype(np.uint32))
+    tokens = [int(t) for t in rng.integers(0, cfg.vocab, SESSIONS)]
+    for _ in range(PROFILE_WARM_ROUNDS + 1):
+        lfm3.Session.forward_batch_inputs(sessions, tokens, logits=True)
+    sessions[0].forward(rng.integers(0, cfg.vocab, 512).astype(np.uint32))
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_sequence": "done", "sessions": SESSIONS,
+                      "prompt": PROFILE_PROMPT, "warm_rounds": PROFILE_WARM_ROUNDS}))
+
+
 # ---- our arm ---------------------------------------------------------------------------------
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.profile:
+        profile_sequence()
         return
     import torch
 
