@@ -44,6 +44,19 @@ constexpr size_t kTicketWords = 8192;
 bool Q8Matrix(const lfm3_tensor* t) {
   return t && t->data && t->type == LFM3_Q8_0 && t->cols % 512 == 0;
 }
+bool Bf16Matrix(const lfm3_tensor* t) {
+  return t && t->data && t->type == LFM3_BF16 && t->cols % 256 == 0;
+}
+
+// BF16 projections of any number of FP32 rows (exact BF16 x FP32 on the
+// CUDA cores; hip/ops.hip:1917-2005).
+int Bf16Rows(lfm3::GemvParams p, const float* x, int n, int K,
+             cudaStream_t s) {
+  p.K = K;
+  if (!lfm3::bf16_plan(p))
+    return Fail(LFM3_ERR_UNSUPPORTED, "BF16 projection width not tiled");
+  return Cuda(lfm3::launch_bf16_gemv(p, x, K, n, s));
+}
 
 // Decode projections of n < 16 FP32 rows: split once, then <= 8 rows per
 // launch.
@@ -101,12 +114,24 @@ int ProjectImpl(const lfm3_output* outputs, int count, const float* x, int n,
   if (n == 0)
     return LFM3_OK;
   const uint32_t K = outputs[0].weight ? outputs[0].weight->cols : 0;
+  const bool bf16 = Bf16Matrix(outputs[0].weight);
   for (int j = 0; j < count; ++j)
-    if (!Q8Matrix(outputs[j].weight) || outputs[j].weight->cols != K ||
-        !outputs[j].out)
+    if (!(bf16 ? Bf16Matrix(outputs[j].weight) : Q8Matrix(outputs[j].weight)) ||
+        outputs[j].weight->cols != K || !outputs[j].out)
       return Fail(LFM3_ERR_UNSUPPORTED,
-                  "projections need Q8_0 weights with equal widths, "
-                  "multiples of 512");
+                  "projections need Q8_0 (widths multiples of 512) or BF16 "
+                  "(multiples of 256) weights of one type and width");
+  if (bf16) {
+    lfm3::GemvParams p{};
+    p.kind = lfm3::kGemvPlain;
+    p.n_out = count;
+    for (int j = 0; j < count; ++j) {
+      const auto* w = outputs[j].weight;
+      p.o[j] = {static_cast<const uint8_t*>(w->data), outputs[j].out,
+                int(w->rows), int(w->rows)};
+    }
+    return Bf16Rows(p, x, n, int(K), s);
+  }
   if (n < kPromptRows) {
     lfm3::GemvParams p{};
     p.kind = lfm3::kGemvPlain;
@@ -218,13 +243,24 @@ int lfm3_cuda_project_swiglu(const lfm3_tensor* gate, const lfm3_tensor* up,
                              int n, void* stream,
                              const lfm3_dense_workspace* ws) {
   (void)up_scratch;  // the fused kernels keep up x in registers
-  if (!Q8Matrix(gate) || !Q8Matrix(up) || gate->rows != up->rows ||
+  const bool bf16 = Bf16Matrix(gate) && Bf16Matrix(up);
+  if (!(bf16 || (Q8Matrix(gate) && Q8Matrix(up))) || gate->rows != up->rows ||
       gate->cols != up->cols || !out || !ws || n < 0)
     return Fail(LFM3_ERR_UNSUPPORTED, "invalid SwiGLU projection");
   if (n == 0)
     return LFM3_OK;
   const cudaStream_t s = Stream(stream);
   const int K = int(gate->cols);
+  if (bf16) {
+    lfm3::GemvParams p{};
+    p.kind = lfm3::kGemvSwiGLU;
+    p.n_out = 2;
+    p.o[0] = {static_cast<const uint8_t*>(gate->data), out, int(gate->rows),
+              int(gate->rows)};
+    p.o[1] = {static_cast<const uint8_t*>(up->data), nullptr, int(up->rows),
+              0};
+    return Bf16Rows(p, x, n, K, s);
+  }
   if (n < kPromptRows) {
     lfm3::GemvParams p{};
     p.kind = lfm3::kGemvSwiGLU;
@@ -252,12 +288,13 @@ int lfm3_cuda_project_ffn(const lfm3_tensor* gate, const lfm3_tensor* up,
                           const lfm3_tensor* down, const float* x,
                           float* hidden, float* up_scratch, float* out, int n,
                           void* stream, const lfm3_dense_workspace* ws) {
-  if (!Q8Matrix(down) || !gate || down->cols != gate->rows)
+  if (!(Q8Matrix(down) || Bf16Matrix(down)) || !gate ||
+      down->cols != gate->rows || down->type != gate->type)
     return Fail(LFM3_ERR_UNSUPPORTED, "invalid FFN down projection");
   if (int e = lfm3_cuda_project_swiglu(gate, up, x, hidden, up_scratch, n,
                                        stream, ws))
     return e;
-  if (n >= kPromptRows && ws->row_max) {
+  if (n >= kPromptRows && ws->row_max && down->type == LFM3_Q8_0) {
     // down input from the SwiGLU row maxima (HalfRowsFromMax)
     auto* values = static_cast<__half*>(ws->quantized);
     auto* scale = reinterpret_cast<float*>(values + size_t(n) * down->cols);

@@ -44,15 +44,20 @@ std::string Validate(const lfm3_weights& w) {
                               c.heads / h != 8)))
       return "LFM3 GQA group must be 2, 4 or 8";
   }
-  const auto matrix = [](const lfm3_tensor& t) {
-    return t.data && t.type == LFM3_Q8_0;
+  // every matrix Q8_0, or every matrix BF16 (the numerical-reference
+  // weights)
+  const uint32_t type = w.output.type;
+  if (type != LFM3_Q8_0 && type != LFM3_BF16)
+    return "this build needs Q8_0 or BF16 matrices";
+  const auto matrix = [type](const lfm3_tensor& t) {
+    return t.data && t.type == type;
   };
   if (!matrix(w.embedding) || !matrix(w.output))
-    return "this build needs Q8_0 embedding and output matrices";
+    return "the embedding and output matrices must share one type";
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     const auto& l = w.layers[i];
     if (!matrix(l.gate) || !matrix(l.up) || !matrix(l.down))
-      return "this build needs Q8_0 FFN matrices";
+      return "the FFN matrices must share the model's matrix type";
     if (c.layer_type[i] == LFM3_CONV) {
       if (!matrix(l.in_proj) || !matrix(l.out_proj) || !l.conv.data ||
           l.conv.type != LFM3_F32)
@@ -252,6 +257,7 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     a_ = DeviceBuffer(R * std::max(A, H) * 4);
     ff_ = DeviceBuffer(R * F * 4);
     row_max_ = DeviceBuffer(R * 4);
+    zf_ = DeviceBuffer(R * H * 4);
     split_partial_ = DeviceBuffer(kPrefillPartialFloats * 4);
     half_ = DeviceBuffer(R * width * 2);
     scale_ = DeviceBuffer(R * 4);
@@ -342,6 +348,11 @@ void Session::TakeProfile(double* ms, long long* launches) {
 
 // Launches one projection of the round's rows (split input x).
 static cudaError_t RunGemv(GemvParams p, Model& model, cudaStream_t stream) {
+  if (model.bf16()) {
+    if (!bf16_plan(p))
+      return cudaErrorInvalidValue;
+    return launch_bf16_gemv(p, nullptr, 0, 0, stream);
+  }
   if (!gemv_plan(p, model.sms()))
     return cudaErrorInvalidValue;
   const int maps = p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
@@ -570,8 +581,37 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
   };
   const auto other = [&](auto launch) { Timed(kPromptOther, launch); };
   const auto rows = [&](auto launch) { Timed(kRowKernels, launch); };
-  const auto plain = [&](int K, int rows, int first_row,
+  // BF16 models project FP32 rows (in32) on the CUDA cores; Q8_0 models the
+  // FP16 row-scaled copies on the tensor cores
+  const bool bf16 = model_->bf16();
+  float* zf = zf_.as<float>();
+  const auto norm_out = [&](int row) {
+    return bf16 ? NormOut{zf + size_t(row) * H, nullptr, nullptr, nullptr}
+                : NormOut{nullptr, nullptr, half_at(row, H), scale + row};
+  };
+  const auto to_half = [&](const float* src, int row, int n_rows, int width) {
+    if (!bf16)
+      Timed(kPromptOther, [&] {
+        Check(launch_half_rows(src, nullptr, half_at(row, width), scale + row,
+                               n_rows, width, s));
+      });
+  };
+  const auto plain = [&](int K, int rows, int first_row, const float* in32,
                          std::initializer_list<PrefillOutput> outs) {
+    if (bf16) {
+      GemvParams g{};
+      g.kind = kGemvPlain;
+      g.K = K;
+      g.n_out = int(outs.size());
+      int j = 0;
+      for (const auto& o : outs)
+        g.o[j++] = GemvOutput{o.w, o.out, o.rows, o.ld};
+      if (!bf16_plan(g))
+        Throw(cudaErrorInvalidValue);
+      Timed(kPromptProjection,
+            [&] { Check(launch_bf16_gemv(g, in32, K, rows, s)); });
+      return;
+    }
     PrefillParams p{};
     p.kind = kPrefillPlain;
     p.K = K;
@@ -599,8 +639,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       Check(launch_residual_norm(
           nullptr, nullptr, x + size_t(o_in) * H,
           static_cast<const float*>(w.layers[0].norm.data),
-          NormOut{nullptr, nullptr, half_at(o_in, H), scale + o_in},
-          live_in[0], H, c.eps, s, false));
+          norm_out(o_in), live_in[0], H, c.eps, s, false));
     });
   }
   for (int i = 0; i < L; ++i) {
@@ -609,7 +648,8 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     const int o_in = n - rows_in, o = n - rows_out;
     if (c.layer_type[i] == LFM3_CONV) {
       float* p = p_.as<float>();
-      plain(H, rows_in, o_in, {pout(l.in_proj, p + size_t(o_in) * 3 * H, 3 * H)});
+      plain(H, rows_in, o_in, zf + size_t(o_in) * H,
+            {pout(l.in_proj, p + size_t(o_in) * 3 * H, 3 * H)});
       float* a = a_.as<float>();
       other([&] {
         Check(launch_short_conv(p + size_t(o_in) * 3 * H,
@@ -618,18 +658,16 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
                                 a + size_t(o_in) * H, rows_in, H,
                                 int(c.conv_width), true, s));
       });
-      other([&] {
-        Check(launch_half_rows(a + size_t(o) * H, nullptr, half_at(o, H),
-                               scale + o, rows_out, H, s));
-      });
-      plain(H, rows_out, o, {pout(l.out_proj, out + size_t(o) * H, H)});
+      to_half(a + size_t(o) * H, o, rows_out, H);
+      plain(H, rows_out, o, a + size_t(o) * H,
+            {pout(l.out_proj, out + size_t(o) * H, H)});
     } else {
       const int kvh = int(c.kv_heads[i]), kv = kvh * 128;
       const size_t stride = size_t(kv);
       const bool swa = c.layer_type[i] == LFM3_SLIDING_ATTENTION;
       float *q = q_.as<float>(), *k = k_.as<float>(), *v = v_.as<float>(),
             *g = gate_.as<float>();
-      plain(H, n, 0,
+      plain(H, n, 0, zf,
             {pout(l.q, q, A), pout(l.k, k, kv), pout(l.v, v, kv),
              pout(l.attn_gate, g, c.heads)});
       auto& st = states_[i];
@@ -660,20 +698,34 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
           Check(launch_store_kv(kc, vc, st.k.as<__half>(), st.v.as<__half>(),
                                 n, kv, int(position_), int(st.capacity), s));
         });
-      other([&] {
-        Check(launch_half_rows(a + size_t(o) * A, nullptr, half_at(o, A),
-                               scale + o, rows_out, A, s));
-      });
-      plain(A, rows_out, o, {pout(l.attn_out, out + size_t(o) * H, H)});
+      to_half(a + size_t(o) * A, o, rows_out, A);
+      plain(A, rows_out, o, a + size_t(o) * A,
+            {pout(l.attn_out, out + size_t(o) * H, H)});
     }
     rows([&] {
       Check(launch_residual_norm(
           out + size_t(o) * H, static_cast<const float*>(l.post_norm.data),
           x + size_t(o) * H, static_cast<const float*>(l.ffn_norm.data),
-          NormOut{nullptr, nullptr, half_at(o, H), scale + o}, rows_out, H,
-          c.eps, s, false));
+          norm_out(o), rows_out, H, c.eps, s, false));
     });
-    {
+    if (bf16) {
+      float* ff = ff_.as<float>();
+      GemvParams g{};
+      g.kind = kGemvSwiGLU;
+      g.K = H;
+      g.n_out = 2;
+      g.o[0] = GemvOutput{static_cast<const uint8_t*>(l.gate.data),
+                          ff + size_t(o) * F, int(l.gate.rows), F};
+      g.o[1] = GemvOutput{static_cast<const uint8_t*>(l.up.data), nullptr,
+                          int(l.up.rows), 0};
+      if (!bf16_plan(g))
+        Throw(cudaErrorInvalidValue);
+      Timed(kPromptProjection, [&] {
+        Check(launch_bf16_gemv(g, zf + size_t(o) * H, H, rows_out, s));
+      });
+      plain(F, rows_out, o, ff + size_t(o) * F,
+            {pout(l.down, out + size_t(o) * H, H)});
+    } else {
       float* ff = ff_.as<float>();
       unsigned* row_max = row_max_.as<unsigned>();
       Check(cudaMemsetAsync(row_max + o, 0, size_t(rows_out) * 4, s));
@@ -691,7 +743,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
         Check(launch_half_rows(ff + size_t(o) * F, row_max + o,
                                half_at(o, F), scale + o, rows_out, F, s));
       });
-      plain(F, rows_out, o, {pout(l.down, out + size_t(o) * H, H)});
+      plain(F, rows_out, o, nullptr, {pout(l.down, out + size_t(o) * H, H)});
     }
     const bool last = i + 1 == L;
     rows([&] {
@@ -700,9 +752,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
           static_cast<const float*>(l.post_ffn_norm.data), x + size_t(o) * H,
           last ? nullptr
                : static_cast<const float*>(w.layers[i + 1].norm.data),
-          NormOut{nullptr, nullptr, last ? nullptr : half_at(o, H),
-                  last ? nullptr : scale + o},
-          rows_out, H, c.eps, s, false));
+          last ? NormOut{} : norm_out(o), rows_out, H, c.eps, s, false));
     });
   }
   // frontier = output_norm(last row); logits from it when asked

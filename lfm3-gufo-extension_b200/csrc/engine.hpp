@@ -65,6 +65,8 @@ public:
     return freq_.as<float>() + (sliding ? 64 : 0);
   }
   int sms() const { return sms_; }
+  // BF16 numerical-reference matrices (else Q8_0)
+  bool bf16() const { return device_.output.type == LFM3_BF16; }
   // Device bytes of the weight segments.
   size_t weight_bytes() const { return weight_bytes_; }
   // The TMA map over a Q8_0 matrix's rows with boxes of box_rows rows x
@@ -177,7 +179,7 @@ private:
   DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_, row_max_,
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
-      attn_tickets_, prompt_scratch_, split_partial_;
+      attn_tickets_, prompt_scratch_, split_partial_, zf_;
   DecodeRows* host_rows_ = nullptr;  // pinned
   bool profiling_ = false;
   std::vector<cudaEvent_t> events_;

@@ -327,6 +327,171 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   }
 }
 
+// ---- BF16 projections -------------------------------------------------------
+constexpr int kBf16Chunk = 1024;  // K columns of the input staged per pass
+constexpr int kBf16Threads = 256;
+
+struct Bf16Smem {
+  float x[kMaxBatch][kBf16Chunk + 4];
+  float tile[kMaxTileRows * kMaxBatch];
+};
+
+// Weight row of tile row r of tile t (BF16, K elements), or null past the
+// matrix.
+template <int kKind, int kMT>
+__device__ __forceinline__ const uint16_t* bf16_row(const GemvParams& p, int t,
+                                                    int r) {
+  int matrix = 0, row = 0;
+  if (kKind == kGemvPlain) {
+#pragma unroll
+    for (int q = 1; q < 4; ++q)
+      if (q < p.n_out && t >= p.first_tile[q])
+        matrix = q;
+    row = (t - p.first_tile[matrix]) * 16 * kMT + r;
+  } else if (kKind == kGemvSwiGLU) {
+    matrix = r / 16;
+    row = t * 16 + r % 16;
+  } else {
+    row = (r / 16) * p.H + t * 16 + r % 16;
+    if (t * 16 + r % 16 >= p.H)
+      return nullptr;
+  }
+  if (row >= p.o[matrix].rows)
+    return nullptr;
+  return reinterpret_cast<const uint16_t*>(p.o[matrix].w) + size_t(row) * p.K;
+}
+
+__device__ __forceinline__ void bf16x8(const uint4& w, float (&f)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+  }
+}
+
+template <int kKind, int kMT>
+__global__ void __launch_bounds__(kBf16Threads)
+    bf16_gemv_kernel(const __grid_constant__ GemvParams p, const float* x32,
+                     int x_ld, int rows) {
+  constexpr int kRows = 16 * kMT, kR = kRows / 8;  // tile rows, rows per warp
+  __shared__ Bf16Smem s;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int t = blockIdx.x;
+  const int t0 = blockIdx.y * kMaxBatch;  // first input row of this group
+  const int nt = x32 ? min(kMaxBatch, rows - t0) : p.tokens;
+  grid_dependency_wait();
+  const uint16_t* w[kR];
+#pragma unroll
+  for (int r = 0; r < kR; ++r)
+    w[r] = bf16_row<kKind, kMT>(p, t, warp * kR + r);
+  float acc[kR][kMaxBatch];
+#pragma unroll
+  for (int r = 0; r < kR; ++r)
+#pragma unroll
+    for (int j = 0; j < kMaxBatch; ++j)
+      acc[r][j] = 0;
+  // columns per staging pass: the largest of 1024, 512, 256 dividing K
+  const int chunk = p.K % 1024 == 0 ? 1024 : p.K % 512 == 0 ? 512 : 256;
+  for (int c0 = 0; c0 < p.K; c0 += chunk) {
+    __syncthreads();
+    // stage the input rows' columns c0 .. c0 + chunk - 1 as FP32 (8 per
+    // thread-step: one split record, or two float4)
+    for (int e = tid; e < kMaxBatch * chunk / 8; e += kBf16Threads) {
+      const int tok = e / (chunk / 8), k = (e % (chunk / 8)) * 8;
+      float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (tok < nt) {
+        if (x32) {
+          const float* src = x32 + size_t(t0 + tok) * x_ld + c0 + k;
+          const float4 a = *reinterpret_cast<const float4*>(src);
+          const float4 b = *reinterpret_cast<const float4*>(src + 4);
+          v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+          v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+          const uint4* rec = static_cast<const uint4*>(p.x) +
+                             (size_t(tok) * (p.K / 8) + (c0 + k) / 8) * 2;
+          const uint4 hi = rec[0], lo = rec[1];
+          const uint32_t h[4] = {hi.x, hi.y, hi.z, hi.w};
+          const uint32_t l[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&l[i]));
+            v[2 * i] = a.x + b.x;
+            v[2 * i + 1] = a.y + b.y;
+          }
+        }
+      }
+      float* dst = &s.x[tok][k];
+      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    __syncthreads();
+    for (int k = lane * 8; k < chunk; k += 256) {
+      float wf[kR][8];
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (w[r])
+          raw = __ldg(reinterpret_cast<const uint4*>(w[r] + c0 + k));
+        bf16x8(raw, wf[r]);
+      }
+#pragma unroll
+      for (int tok = 0; tok < kMaxBatch; ++tok) {
+        const float4 a = *reinterpret_cast<const float4*>(&s.x[tok][k]);
+        const float4 b = *reinterpret_cast<const float4*>(&s.x[tok][k + 4]);
+        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int r = 0; r < kR; ++r)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            acc[r][tok] = fmaf(wf[r][i], xv[i], acc[r][tok]);
+      }
+    }
+  }
+  allow_dependents();
+  // lanes' partial sums in a fixed butterfly order
+#pragma unroll
+  for (int r = 0; r < kR; ++r)
+#pragma unroll
+    for (int tok = 0; tok < kMaxBatch; ++tok) {
+      const float v = warp_sum(acc[r][tok]);
+      if (lane == 0)
+        s.tile[(warp * kR + r) * kMaxBatch + tok] = v;
+    }
+  __syncthreads();
+  if (!x32) {
+    gemv_epilogue<kKind, kMT>(p, s.tile, t, tid);
+    return;
+  }
+  // prompt rows t0 .. t0 + nt - 1
+  for (int e = tid; e < 16 * kMaxBatch * (kKind == kGemvPlain ? kMT : 1);
+       e += kBf16Threads) {
+    const int i = e / kMaxBatch, tok = e % kMaxBatch;
+    if (tok >= nt)
+      continue;
+    if (kKind == kGemvPlain) {
+      int j = 0;
+#pragma unroll
+      for (int q = 1; q < 4; ++q)
+        if (q < p.n_out && t >= p.first_tile[q])
+          j = q;
+      const int row = (t - p.first_tile[j]) * 16 * kMT + i;
+      if (row < p.o[j].rows)
+        p.o[j].out[size_t(t0 + tok) * p.o[j].ld + row] = s.tile[e];
+    } else {
+      const int row = t * 16 + i;
+      if (row >= p.o[0].rows)
+        continue;
+      const float g = s.tile[i * kMaxBatch + tok];
+      const float u = s.tile[(16 + i) * kMaxBatch + tok];
+      // BatchedSwiGLUActivationKernel's formula (hip/ops.hip:175-177)
+      const float sig = 1.0F / (1.0F + expf(-g));
+      p.o[0].out[size_t(t0 + tok) * p.o[0].ld + row] = (g * sig) * u;
+    }
+  }
+}
+
 }  // namespace
 
 bool gemv_plan(GemvParams& p, int sms) {
@@ -391,6 +556,50 @@ cudaError_t fill_gemv_maps(GemvParams& p) {
       return e;
   }
   return cudaSuccess;
+}
+
+bool bf16_plan(GemvParams& p) {
+  if (p.K <= 0 || p.K % 256)
+    return false;
+  p.wide = 0;
+  p.chunk_blocks = 0;
+  p.chunks = 0;
+  if (p.kind == kGemvPlain) {
+    int tiles = 0;
+    for (int j = 0; j < p.n_out; ++j) {
+      p.first_tile[j] = tiles;
+      tiles += (p.o[j].rows + 15) / 16;
+    }
+    p.first_tile[p.n_out] = tiles;
+    p.tiles = tiles;
+  } else if (p.kind == kGemvSwiGLU) {
+    p.tiles = (p.o[0].rows + 15) / 16;
+  } else {
+    if (p.H % 16)
+      return false;
+    p.tiles = p.H / 16;
+  }
+  return p.tiles > 0;
+}
+
+cudaError_t launch_bf16_gemv(const GemvParams& p, const float* x32, int x_ld,
+                             int rows, cudaStream_t stream) {
+  if (p.tiles <= 0 || (x32 && (rows <= 0 || p.kind == kGemvConv ||
+                               x_ld % 4 || x_ld < p.K)) ||
+      (!x32 && (!p.x || p.tokens < 1 || p.tokens > kMaxBatch)))
+    return cudaErrorInvalidValue;
+  const dim3 grid(p.tiles, x32 ? (rows + kMaxBatch - 1) / kMaxBatch : 1);
+  note_launch();
+  if (p.kind == kGemvPlain)
+    bf16_gemv_kernel<kGemvPlain, 1>
+        <<<grid, kBf16Threads, 0, stream>>>(p, x32, x_ld, rows);
+  else if (p.kind == kGemvSwiGLU)
+    bf16_gemv_kernel<kGemvSwiGLU, 2>
+        <<<grid, kBf16Threads, 0, stream>>>(p, x32, x_ld, rows);
+  else
+    bf16_gemv_kernel<kGemvConv, 3>
+        <<<grid, kBf16Threads, 0, stream>>>(p, x32, x_ld, rows);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_q8_gemv(const GemvParams& p, int grid, cudaStream_t stream,

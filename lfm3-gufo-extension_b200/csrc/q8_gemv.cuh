@@ -88,4 +88,21 @@ int gemv_grid(int tiles, int sms);
 // cache).
 cudaError_t fill_gemv_maps(GemvParams& p);
 
+// ---- BF16 projections ----------------------------------------------------------
+// Exact BF16 x FP32 on the CUDA cores with FP32 accumulation, for the BF16
+// numerical-reference weights (Wave32GEMVKernel_1Row, FastGEMVBlockKernel,
+// BatchedExactBf16GEMMFp32VecKernel, hip/ops.hip:184-302, 452-591,
+// 1917-2005). Same GemvParams as the Q8_0 kernel (o[j].w are BF16 rows of K
+// elements; maps unused) with tiles of 16 x m-tiles rows: Plain 16, SwiGLU
+// 16 gate + 16 up, Conv 16 channels x (B, C, x).
+//   x32 == nullptr: decode rows, p.x split records of p.tokens <= 8 rows
+//     (hi + lo, 22 significant bits of each FP32 input), and the kind's
+//     epilogue exactly as q8_gemv_kernel's;
+//   otherwise FP32 prompt rows x32[t * x_ld + k], t < rows, in groups of 8:
+//     Plain, or SwiGLU writing FP32 silu(g) * u to o[0].out.
+// K must be a multiple of 256.
+bool bf16_plan(GemvParams& p);
+cudaError_t launch_bf16_gemv(const GemvParams& p, const float* x32, int x_ld,
+                             int rows, cudaStream_t stream);
+
 }  // namespace lfm3

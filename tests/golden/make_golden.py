@@ -10,9 +10,13 @@ oracle/Makefile) on the synthetic weights of lfm3_synth_generate.
   small.npz    small geometry of the same architecture (tests' small_config,
                norm jitter 0.1): 40-token prompt (default_rng(7)), 20 greedy
                tokens, logits after the prompt and after every greedy step.
+  config1_bf16.npz, small_bf16.npz
+               the same with BF16 matrices (the numerical-reference weights,
+               N(0, 0.02) rounded to BF16 instead of quantised to Q8_0).
 
-Run from the repository root:  python tests/golden/make_golden.py [small|config1]
-(config1 takes about ten minutes of one core).
+Run from the repository root:
+  python tests/golden/make_golden.py [small|config1|small_bf16|config1_bf16]
+(each config1 fixture takes about ten minutes of one core).
 """
 import importlib
 import os
@@ -33,8 +37,9 @@ SMALL = dict(norm_jitter=0.1, prompt=40, steps=20, seed=7)
 CONFIG1 = dict(prompt=128, steps=64, seed=0)
 
 
-def small():
-    w = lfm3.SyntheticWeights(lfm3.small_config(), seed=0, norm_jitter=SMALL["norm_jitter"])
+def small(matrix_type=lfm3.abi.Q8_0, name="small.npz"):
+    w = lfm3.SyntheticWeights(lfm3.small_config(), seed=0, matrix_type=matrix_type,
+                              norm_jitter=SMALL["norm_jitter"])
     ref = oracle.ReferenceOracle(w.weights, 256)
     rng = np.random.default_rng(SMALL["seed"])
     prompt = rng.integers(0, w.config.vocab, SMALL["prompt"]).astype(np.uint32)
@@ -45,13 +50,13 @@ def small():
         tok = int(np.argmax(logits[-1]))
         generated.append(tok)
         logits.append(ref.step(tok, True))
-    np.savez_compressed(os.path.join(HERE, "small.npz"), prompt=prompt,
+    np.savez_compressed(os.path.join(HERE, name), prompt=prompt,
                         generated=np.array(generated, np.uint32),
                         logits=np.stack(logits).astype(np.float32))
 
 
-def config1():
-    w = lfm3.SyntheticWeights(seed=0)
+def config1(matrix_type=lfm3.abi.Q8_0, name="config1.npz"):
+    w = lfm3.SyntheticWeights(seed=0, matrix_type=matrix_type)
     ref = oracle.ReferenceOracle(w.weights, 1024)
     rng = np.random.default_rng(CONFIG1["seed"])
     prompt = rng.integers(0, w.config.vocab, CONFIG1["prompt"]).astype(np.uint32)
@@ -68,7 +73,7 @@ def config1():
         argmax.append(tok)
         margin.append(float(top2.max() - top2.min()))
         logits = ref.step(tok, True)
-    np.savez_compressed(os.path.join(HERE, "config1.npz"), prompt=prompt,
+    np.savez_compressed(os.path.join(HERE, name), prompt=prompt,
                         generated=np.array(generated, np.uint32),
                         after_prompt=after_prompt.astype(np.float32),
                         final=logits.astype(np.float32),
@@ -82,3 +87,7 @@ if __name__ == "__main__":
         small()
     if "config1" in which:
         config1()
+    if "small_bf16" in which:
+        small(lfm3.abi.BF16, "small_bf16.npz")
+    if "config1_bf16" in which:
+        config1(lfm3.abi.BF16, "config1_bf16.npz")

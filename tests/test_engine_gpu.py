@@ -172,3 +172,54 @@ def test_device_failure_poisons_until_reset(small):
     fresh = model.session(128)
     np.testing.assert_array_equal(s.forward([1, 2, 3]), fresh.forward([1, 2, 3]))
     assert lfm3.library().lfm3_cuda_take_device_error() == 0
+
+
+# ---- BF16 numerical-reference weights (north-star logits tolerance 2e-2) ------
+BF16_MAX_ABS = 2e-2
+
+
+@pytest.fixture(scope="module")
+def small_bf16():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    w = lfm3.SyntheticWeights(lfm3.small_config(), seed=0, matrix_type=lfm3.abi.BF16,
+                              norm_jitter=0.1)
+    model = lfm3.Model(w.weights)
+    return w, model
+
+
+def test_bf16_prompt_and_greedy_match_golden(small_bf16):
+    """BF16 matrices: prompt pass (CUDA-core exact BF16 x FP32 projections)
+    and 20 greedy decode steps against the compiled reference's fixture."""
+    w, model = small_bf16
+    g = np.load(os.path.join(GOLDEN, "small_bf16.npz"))
+    s = model.session(256)
+    logits = s.forward(g["prompt"])
+    got = [logits]
+    for t in g["generated"]:
+        got.append(s.forward([int(t)]))
+    for step, (a, b) in enumerate(zip(got, g["logits"])):
+        err = float(np.abs(a - b).max())
+        assert err <= BF16_MAX_ABS, (step, err)
+        assert kl(b, a) < MAX_KL, step
+        if top2_margin(b) > 4 * err:
+            assert int(np.argmax(a)) == int(np.argmax(b)), step
+
+
+def test_bf16_batched_matches_serial(small_bf16):
+    """A batched BF16 decode round equals each session's own serial step."""
+    w, model = small_bf16
+    rng = np.random.default_rng(23)
+    lengths = [5, 33, 70]
+    prompts = [rng.integers(0, w.config.vocab, n).astype(np.uint32) for n in lengths]
+    batch = [model.session(256) for _ in lengths]
+    serial = [model.session(256) for _ in lengths]
+    for a, b, p in zip(batch, serial, prompts):
+        a.forward(p)
+        b.forward(p)
+    nxt = [int(t) for t in rng.integers(0, w.config.vocab, len(lengths))]
+    outs = lfm3.Session.forward_batch(batch, nxt)
+    for o, s, t in zip(outs, serial, nxt):
+        ref = s.forward([t])
+        assert float(np.abs(o - ref).max()) <= 2e-3
+        assert int(np.argmax(o)) == int(np.argmax(ref))

@@ -131,6 +131,53 @@ def test_projection_tall(n):
     near(host(out).reshape(n, M), expected, 1e-4)
 
 
+# ---- BF16 projections (exact BF16 x FP32, hip/ops.hip:1917-2005) ---------------
+def bf16_tensor(w32, cols, rows):
+    """BF16 matrix [rows][cols] from FP32 values (round to nearest even)."""
+    bits = w32.astype(np.float32).view(np.uint32)
+    bf = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16).astype(np.uint16)
+    buf = dev(bf.copy())
+    t = abi.Tensor(buf.data_ptr(), abi.BF16, cols, rows, bf.nbytes)
+    exact = (bf.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return t, buf, exact.reshape(rows, cols)
+
+
+@pytest.mark.parametrize("n", [1, 8, 9, 16, 37, 512])
+def test_projection_bf16(n):
+    M, K = 70, 512 + 256
+    w32 = data(M * K, 0.05).reshape(M, K)
+    t, keep, w = bf16_tensor(w32, K, M)
+    x = data(n * K, 0.3).reshape(n, K) + np.float32(0.01)
+    expected = x.astype(np.float64) @ w.T
+    dx, out = dev(x), torch.empty(n * M, dtype=torch.float32, device="cuda")
+    ws, keep2 = workspace(n, K)
+    lfm3.check(lib.lfm3_cuda_dense(ctypes.byref(t), ptr(dx), ptr(out), n, None,
+                                   ctypes.byref(ws)))
+    near(host(out).reshape(n, M), expected, 2e-5)
+
+
+@pytest.mark.parametrize("n", [1, 8, 20])
+def test_ffn_bf16(n):
+    H, F = 256, 512
+    gw, keep_g, g64 = bf16_tensor(data(F * H, 0.06).reshape(F, H), H, F)
+    uw, keep_u, u64 = bf16_tensor(data(F * H, 0.05).reshape(F, H) * -1, H, F)
+    dw, keep_d, d64 = bf16_tensor(data(H * F, 0.04).reshape(H, F), F, H)
+    x = data(n * H, 0.5).reshape(n, H)
+    g = x.astype(np.float64) @ g64.T
+    u = x.astype(np.float64) @ u64.T
+    hidden = g / (1 + np.exp(-g)) * u
+    expected = hidden @ d64.T
+    dx = dev(x)
+    h = torch.empty(n * F, dtype=torch.float32, device="cuda")
+    out = torch.empty(n * H, dtype=torch.float32, device="cuda")
+    ws, keep2 = workspace(n, F)
+    lfm3.check(lib.lfm3_cuda_project_ffn(ctypes.byref(gw), ctypes.byref(uw),
+                                         ctypes.byref(dw), ptr(dx), ptr(h), None,
+                                         ptr(out), n, None, ctypes.byref(ws)))
+    near(host(h).reshape(n, F), hidden, 2e-5)
+    near(host(out).reshape(n, H), expected, 5e-5)
+
+
 # ---- ShortConv (tests/ops_test.cpp:90-116) ------------------------------------
 @pytest.mark.parametrize("n", [1, 8, 9, 15, 16, 29, 32, 33, 128, 512])
 def test_conv(n):
