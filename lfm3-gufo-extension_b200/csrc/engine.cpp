@@ -474,7 +474,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       ap.kv_heads = int(c.kv_heads[i]);
       ap.window = swa ? int(c.window) : 0;
       // about two CTAs per SM over the round's (row, group) pairs
-      ap.max_splits = std::max(1, 2 * model_->sms() / (B * int(c.kv_heads[i])));
+      ap.max_splits = std::max(1, 4 * model_->sms() / (B * int(c.kv_heads[i])));
       ap.eps = c.eps;
       ap.out_split = a_split_.data();
       ap.partials = attn_partials_.as<float>();

@@ -531,10 +531,12 @@ bool gemv_plan(GemvParams& p, int sms) {
 }
 
 int gemv_grid(int tiles, int sms) {
-  // Projections with tiles for two CTAs per SM take them (twice the warps to
-  // hide latency); smaller ones keep one per SM so the next kernel's CTA can
-  // be resident and start its copies early.
-  if (tiles >= 2 * sms)
+  // One CTA per SM leaves room for the next kernel's CTA, whose producer then
+  // streams that projection's weights while this one finishes (programmatic
+  // dependent launch): across a round that overlap is worth more than a
+  // second CTA's warps. Only the tallest projections (the LM head, last in
+  // the round) take two per SM.
+  if (tiles >= 4 * sms)
     return 2 * sms;
   return tiles < sms ? tiles : sms;
 }
