@@ -167,14 +167,55 @@ def committed_traffic():
 
 # ---- clocks ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clocks and clock-event reasons sampled during a timed region (read
+    only): NVML every 5 ms when the bindings load, else nvidia-smi every
+    200 ms."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index):
         self.index, self.lines, self.proc = index, [], None
+        self.samples, self.max_mhz, self.reasons = [], None, set()
+        self.stop, self.thread, self.nvml = None, None, None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            props = torch.cuda.get_device_properties(self.index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        return pynvml, handle
+
+    def _poll(self):
+        nv, h = self.nvml
+        self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        reasons_of = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+            bits = reasons_of(h)
+            for name, bit in self.REASONS.items():
+                if bits & bit:
+                    self.reasons.add(name)
+            self.stop.wait(0.005)
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -191,6 +232,10 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.nvml:
+            self.stop.set()
+            self.thread.join(5)
+            return
         if self.proc:
             self.proc.terminate()
             try:
@@ -199,6 +244,12 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.nvml:
+            if not self.samples:
+                return None
+            return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(self.reasons), "samples": len(self.samples),
+                    "source": "nvml 5 ms"}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
@@ -216,7 +267,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 # ---- CPU baseline ------------------------------------------------------------------------
