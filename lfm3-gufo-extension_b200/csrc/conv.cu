@@ -18,28 +18,41 @@ __device__ __forceinline__ float product(const float* p, const float* history,
                      : history[size_t(ch) * (L - 1) + (L - 1) + source];
 }
 
+// kL > 0: the width as a compile-time constant (window and taps stay in
+// registers); kL == 0: any width L <= kMaxWidth.
+template <int kL>
 __global__ void conv_window_kernel(const float* __restrict__ p,
                                    const float* __restrict__ w,
                                    const float* __restrict__ history,
                                    float* __restrict__ y, int n, int H,
-                                   int L) {
+                                   int L_runtime) {
+  constexpr int kCap = kL > 0 ? kL : kMaxWidth;
+  const int L = kL > 0 ? kL : L_runtime;
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
   const int first = blockIdx.y * kConvRows;
   if (ch >= H)
     return;
-  float taps[kMaxWidth], window[kMaxWidth];
-  for (int t = 0; t < L; ++t)
-    taps[t] = w[size_t(ch) * L + t];
-  for (int t = 0; t < L - 1; ++t)
-    window[t + 1] = product(p, history, first - (L - 1) + t, ch, H, L);
+  float taps[kCap], window[kCap];
+#pragma unroll
+  for (int t = 0; t < kCap; ++t)
+    if (t < L)
+      taps[t] = w[size_t(ch) * L + t];
+#pragma unroll
+  for (int t = 0; t < kCap - 1; ++t)
+    if (t < L - 1)
+      window[t + 1] = product(p, history, first - (L - 1) + t, ch, H, L);
   const int last = min(first + kConvRows, n);
   for (int row = first; row < last; ++row) {
-    for (int t = 0; t < L - 1; ++t)
-      window[t] = window[t + 1];
+#pragma unroll
+    for (int t = 0; t < kCap - 1; ++t)
+      if (t < L - 1)
+        window[t] = window[t + 1];
     window[L - 1] = product(p, history, row, ch, H, L);
     float sum = 0;
-    for (int t = 0; t < L; ++t)
-      sum = fmaf(taps[t], window[t], sum);
+#pragma unroll
+    for (int t = 0; t < kCap; ++t)
+      if (t < L)
+        sum = fmaf(taps[t], window[t], sum);
     y[size_t(row) * H + ch] = sum * p[size_t(row) * 3 * H + H + ch];
   }
 }
@@ -67,7 +80,10 @@ cudaError_t launch_short_conv(const float* p, const float* w, float* history,
     return cudaSuccess;
   const dim3 grid((H + 127) / 128, (n + kConvRows - 1) / kConvRows);
   note_launch(update ? 2 : 1);
-  conv_window_kernel<<<grid, 128, 0, stream>>>(p, w, history, y, n, H, L);
+  if (L == 7)  // the LFM3 width (l_cache)
+    conv_window_kernel<7><<<grid, 128, 0, stream>>>(p, w, history, y, n, H, L);
+  else
+    conv_window_kernel<0><<<grid, 128, 0, stream>>>(p, w, history, y, n, H, L);
   if (update)
     conv_history_kernel<<<(H + 127) / 128, 128, 0, stream>>>(p, history, n, H,
                                                              L);

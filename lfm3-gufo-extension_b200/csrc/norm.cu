@@ -42,11 +42,28 @@ __device__ __forceinline__ int row_exponent(float maximum) {
   return maximum > 0 ? 14 - ilogbf(maximum) : 0;
 }
 
-// Normalises v (this thread's groups of row `row`) and writes every
-// requested output.
-__device__ void finish_norm(float (&v)[kNormMaxGroups][8], int groups,
-                            const float* norm_w, NormOut out, int row, int H,
-                            float eps, float* scratch) {
+// This thread's groups of a weight vector (8 consecutive values each).
+template <int G>
+__device__ __forceinline__ void load_groups(const float* w, int H,
+                                            float (&dst)[G][8]) {
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    if (w && k0 < H) {
+      const float4 a = *reinterpret_cast<const float4*>(w + k0);
+      const float4 b = *reinterpret_cast<const float4*>(w + k0 + 4);
+      dst[j][0] = a.x, dst[j][1] = a.y, dst[j][2] = a.z, dst[j][3] = a.w;
+      dst[j][4] = b.x, dst[j][5] = b.y, dst[j][6] = b.z, dst[j][7] = b.w;
+    }
+  }
+}
+
+// Normalises v (this thread's groups of row `row`) with the norm weights nw
+// (this thread's groups) and writes every requested output.
+template <int G>
+__device__ void finish_norm(float (&v)[G][8], int groups,
+                            const float (&nw)[G][8], NormOut out, int row,
+                            int H, float eps, float* scratch) {
   float squares = 0;
   for (int j = 0; j < groups; ++j)
 #pragma unroll
@@ -55,13 +72,9 @@ __device__ void finish_norm(float (&v)[kNormMaxGroups][8], int groups,
   const float inv = 1.0F / sqrtf(block_sum(squares, scratch) / float(H) + eps);
   float maximum = 0;
   for (int j = 0; j < groups; ++j) {
-    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
-    const float4 w0 = *reinterpret_cast<const float4*>(norm_w + k0);
-    const float4 w1 = *reinterpret_cast<const float4*>(norm_w + k0 + 4);
-    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      v[j][i] = (v[j][i] * inv) * w[i];
+      v[j][i] = (v[j][i] * inv) * nw[j][i];
       maximum = fmaxf(maximum, fabsf(v[j][i]));
     }
   }
@@ -95,20 +108,28 @@ __device__ void finish_norm(float (&v)[kNormMaxGroups][8], int groups,
   }
 }
 
+// G: 8-element groups per thread (H <= 2048 G)
+template <int G>
 __global__ void __launch_bounds__(kNormThreads)
     residual_norm_kernel(const float* __restrict__ branch,
                          const float* __restrict__ post_w, float* x,
                          const float* __restrict__ norm_w, NormOut out, int H,
                          float eps) {
   __shared__ float scratch[kNormThreads / 32];
+  // the norm weights do not depend on the previous kernel: load them while
+  // it finishes
+  float pw[G][8], nw[G][8];
+  load_groups<G>(post_w, H, pw);
+  load_groups<G>(norm_w, H, nw);
   grid_dependency_wait();
   allow_dependents();
   const int row = blockIdx.x, groups = H / 8 / kNormThreads + 1;
-  float v[kNormMaxGroups][8];
-  float b[kNormMaxGroups][8];
+  float v[G][8];
+  float b[G][8];
   float* xr = x + size_t(row) * H;
   int live = 0;
-  for (int j = 0; j < kNormMaxGroups; ++j) {
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
     const int k0 = (threadIdx.x + j * kNormThreads) * 8;
     if (j >= groups || k0 >= H)
       break;
@@ -134,12 +155,10 @@ __global__ void __launch_bounds__(kNormThreads)
           squares = fmaf(b[j][i], b[j][i], squares);
       const float inv =
           1.0F / sqrtf(block_sum(squares, scratch) / float(H) + eps);
-      for (int j = 0; j < live; ++j) {
-        const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+      for (int j = 0; j < live; ++j)
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          b[j][i] = (b[j][i] * inv) * post_w[k0 + i];
-      }
+          b[j][i] = (b[j][i] * inv) * pw[j][i];
     }
     for (int j = 0; j < live; ++j) {
       const int k0 = (threadIdx.x + j * kNormThreads) * 8;
@@ -153,13 +172,14 @@ __global__ void __launch_bounds__(kNormThreads)
     }
   }
   if (norm_w)
-    finish_norm(v, live, norm_w, out, row, H, eps, scratch);
+    finish_norm(v, live, nw, out, row, H, eps, scratch);
 }
 
 __device__ __forceinline__ float half_bits(uint16_t h) {
   return __half2float(__ushort_as_half(h));
 }
 
+template <int G>
 __global__ void __launch_bounds__(kNormThreads)
     embed_norm_kernel(const uint8_t* __restrict__ table, uint32_t type,
                       const uint32_t* __restrict__ ids,
@@ -167,13 +187,16 @@ __global__ void __launch_bounds__(kNormThreads)
                       const float* __restrict__ norm_w, NormOut out, int H,
                       float eps) {
   __shared__ float scratch[kNormThreads / 32];
+  float nw[G][8];
+  load_groups<G>(norm_w, H, nw);
   grid_dependency_wait();
   allow_dependents();
   const int row = blockIdx.x, groups = H / 8 / kNormThreads + 1;
   const uint32_t token = ids ? ids[row] : tokens[row];
-  float v[kNormMaxGroups][8];
+  float v[G][8];
   int live = 0;
-  for (int j = 0; j < kNormMaxGroups; ++j) {
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
     const int k0 = (threadIdx.x + j * kNormThreads) * 8;
     if (j >= groups || k0 >= H)
       break;
@@ -206,7 +229,7 @@ __global__ void __launch_bounds__(kNormThreads)
         make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
   }
   if (norm_w)
-    finish_norm(v, live, norm_w, out, row, H, eps, scratch);
+    finish_norm(v, live, nw, out, row, H, eps, scratch);
 }
 
 __global__ void __launch_bounds__(kNormThreads)
@@ -272,8 +295,11 @@ cudaError_t launch_residual_norm(const float* branch, const float* post_w,
   if (!rows)
     return cudaSuccess;
   void* args[] = {&branch, &post_w, &x, &norm_w, &out, &H, &eps};
-  return launch_pdl(reinterpret_cast<const void*>(residual_norm_kernel),
-                    dim3(rows), dim3(kNormThreads), stream, pdl, args);
+  const void* kernel =
+      H <= 2048   ? reinterpret_cast<const void*>(residual_norm_kernel<1>)
+      : H <= 4096 ? reinterpret_cast<const void*>(residual_norm_kernel<2>)
+                  : reinterpret_cast<const void*>(residual_norm_kernel<4>);
+  return launch_pdl(kernel, dim3(rows), dim3(kNormThreads), stream, pdl, args);
 }
 
 cudaError_t launch_embed_norm(const void* table, uint32_t type,
@@ -287,8 +313,11 @@ cudaError_t launch_embed_norm(const void* table, uint32_t type,
     return cudaSuccess;
   const uint8_t* t = static_cast<const uint8_t*>(table);
   void* args[] = {&t, &type, &ids, &tokens, &x, &norm_w, &out, &H, &eps};
-  return launch_pdl(reinterpret_cast<const void*>(embed_norm_kernel),
-                    dim3(rows), dim3(kNormThreads), stream, pdl, args);
+  const void* kernel =
+      H <= 2048   ? reinterpret_cast<const void*>(embed_norm_kernel<1>)
+      : H <= 4096 ? reinterpret_cast<const void*>(embed_norm_kernel<2>)
+                  : reinterpret_cast<const void*>(embed_norm_kernel<4>);
+  return launch_pdl(kernel, dim3(rows), dim3(kNormThreads), stream, pdl, args);
 }
 
 cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
