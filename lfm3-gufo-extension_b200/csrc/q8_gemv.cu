@@ -232,6 +232,16 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
   };
   int stage = 0;
   uint32_t phase = 0;
+  const int b0 = warp * kPerWarp;  // this warp's first block in each chunk
+  // the input terms of this warp's blocks of one chunk
+  struct ChunkX {
+    uint4 h[kPerWarp], l[kPerWarp];
+  };
+  const auto fetch_chunk = [&](int c, ChunkX& x) {
+#pragma unroll
+    for (int i = 0; i < kPerWarp; ++i)
+      fetch_x(c * kBlocks + b0 + i, x.h[i], x.l[i]);
+  };
   for (int t = blockIdx.x; t < p.tiles; t += grid) {
     float acc[kMT][4];
 #pragma unroll
@@ -239,33 +249,26 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         acc[m][j] = 0;
+    // every input load of a chunk in flight at once, the next chunk's
+    // issued before this one's math
+    ChunkX cur, next;
+    fetch_chunk(0, cur);
     for (int c = 0; c < chunks; ++c) {
-      const int b0 = warp * kPerWarp;  // this warp's first block in the chunk
-      uint4 xh[2], xl[2];
-      fetch_x(c * kBlocks + b0, xh[0], xl[0]);
-      fetch_x(c * kBlocks + b0 + 1, xh[1], xl[1]);
+      if (c + 1 < chunks)
+        fetch_chunk(c + 1, next);
       if (!mbar_wait(&s.full[stage], phase, kErrGemvFullWait))
         return;
       const uint8_t* rows = s.stage[stage] + g * kPitch;
 #pragma unroll
       for (int pair = 0; pair < kPerWarp / 2; ++pair) {
         const int b = b0 + 2 * pair;
-        uint4 nh[2], nl[2];
-        if (pair + 1 < kPerWarp / 2) {
-          fetch_x(c * kBlocks + b + 2, nh[0], nl[0]);
-          fetch_x(c * kBlocks + b + 3, nh[1], nl[1]);
-        }
         // block b starts two bytes into a word (b even), b + 1 on a word
-        run_block<false, kMT>(rows + b * 34, kPitch, cq, xh[0], xl[0], acc);
-        run_block<true, kMT>(rows + (b + 1) * 34, kPitch, cq, xh[1], xl[1],
-                             acc);
-        if (pair + 1 < kPerWarp / 2) {
-          xh[0] = nh[0];
-          xl[0] = nl[0];
-          xh[1] = nh[1];
-          xl[1] = nl[1];
-        }
+        run_block<false, kMT>(rows + b * 34, kPitch, cq, cur.h[2 * pair],
+                              cur.l[2 * pair], acc);
+        run_block<true, kMT>(rows + (b + 1) * 34, kPitch, cq,
+                             cur.h[2 * pair + 1], cur.l[2 * pair + 1], acc);
       }
+      cur = next;
       __syncwarp();
       if (lane == 0)
         mbar_arrive(&s.empty[stage]);
@@ -297,7 +300,7 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
   }
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 2)
+__global__ void __launch_bounds__(kGemvThreads, 1)
     q8_gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GemvSmem& s = *reinterpret_cast<GemvSmem*>(smem_raw);
@@ -531,13 +534,10 @@ bool gemv_plan(GemvParams& p, int sms) {
 }
 
 int gemv_grid(int tiles, int sms) {
-  // One CTA per SM leaves room for the next kernel's CTA, whose producer then
-  // streams that projection's weights while this one finishes (programmatic
-  // dependent launch): across a round that overlap is worth more than a
-  // second CTA's warps. Only the tallest projections (the LM head, last in
-  // the round) take two per SM.
-  if (tiles >= 4 * sms)
-    return 2 * sms;
+  // One CTA per SM (registers for every input load of two chunks in flight)
+  // leaves room for the next kernel's CTA, whose producer then streams that
+  // projection's weights while this one finishes (programmatic dependent
+  // launch).
   return tiles < sms ? tiles : sms;
 }
 
