@@ -122,14 +122,17 @@ __global__ void __launch_bounds__(kThreads)
     acc[h] = 0;
   __syncthreads();
 
-  for (int base = begin; base < end; base += kDecodeTile) {
+  // ---- K and V rows of a tile (16-byte pieces, L1 bypassed: the current
+  // row was just written by this CTA), loaded into registers one tile ahead
+  constexpr int kPieces = kDecodeTile * 16 / kThreads;
+  uint4 kr[kPieces], vr[kPieces];
+  const auto load_tile = [&](int base) {
     const int n = min(kDecodeTile, end - base);
-    // ---- K and V rows of the tile (16-byte pieces, L1 bypassed: the
-    // current row was just written by this CTA)
 #pragma unroll
-    for (int j = 0; j < kDecodeTile * 16 / kThreads; ++j) {
+    for (int j = 0; j < kPieces; ++j) {
       const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = kv;
+      kr[j] = make_uint4(0, 0, 0, 0);
+      vr[j] = kr[j];
       if (key < n) {
         const int t = base + key;
         const __half *ks = state.k, *vs = state.v;
@@ -140,13 +143,24 @@ __global__ void __launch_bounds__(kThreads)
           row = size_t(t - position) * stride;
         }
         row += size_t(g) * kHeadDim;
-        kv = __ldcg(reinterpret_cast<const uint4*>(ks + row) + piece);
-        vv = __ldcg(reinterpret_cast<const uint4*>(vs + row) + piece);
+        kr[j] = __ldcg(reinterpret_cast<const uint4*>(ks + row) + piece);
+        vr[j] = __ldcg(reinterpret_cast<const uint4*>(vs + row) + piece);
       }
-      *reinterpret_cast<uint4*>(&s.k[key][piece * 16]) = kv;
-      *reinterpret_cast<uint4*>(&s.v[key][piece * 8]) = vv;
+    }
+  };
+  if (begin < end)
+    load_tile(begin);
+  for (int base = begin; base < end; base += kDecodeTile) {
+    const int n = min(kDecodeTile, end - base);
+#pragma unroll
+    for (int j = 0; j < kPieces; ++j) {
+      const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
+      *reinterpret_cast<uint4*>(&s.k[key][piece * 16]) = kr[j];
+      *reinterpret_cast<uint4*>(&s.v[key][piece * 8]) = vr[j];
     }
     __syncthreads();
+    if (base + kDecodeTile < end)
+      load_tile(base + kDecodeTile);  // in flight during this tile's math
     // ---- scores: thread owns key tid % 64 and half of the heads
     {
       const int t = tid % kDecodeTile, hs = tid / kDecodeTile;
