@@ -31,16 +31,23 @@ namespace {
 constexpr int kMaxTileRows = 64;
 
 struct GemvSmem {
-  uint8_t stage[kGemvStages][kGemvStageBytes];
+  alignas(128) uint8_t ring[kGemvRingBytes];
   float red[kGemvWarps][kMaxTileRows * kMaxBatch];
   float tile[kMaxTileRows * kMaxBatch];
-  uint64_t full[kGemvStages];
-  uint64_t empty[kGemvStages];
+  uint64_t full[kGemvMaxSlots];
+  uint64_t empty[kGemvMaxSlots];
 };
 
 template <int kMT, int kBlocks>
-__device__ __forceinline__ uint32_t stage_bytes() {
+constexpr uint32_t stage_bytes() {
   return kMT * 16 * gemv_pitch_units(kBlocks) * 16;
+}
+// ring slots for a kind's chunks (each slot a multiple of 128 bytes)
+template <int kMT, int kBlocks>
+constexpr int ring_slots() {
+  return kGemvRingBytes / stage_bytes<kMT, kBlocks>() < kGemvMaxSlots
+             ? kGemvRingBytes / stage_bytes<kMT, kBlocks>()
+             : kGemvMaxSlots;
 }
 
 // Issues the tiled copies of (tile t, chunk c) into dst (Plain: one box of
@@ -187,7 +194,9 @@ __device__ void gemv_epilogue(const GemvParams& p, const float* tile, int t,
 template <int kKind, int kBlocks, int kMT>
 __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
   constexpr int kPitch = gemv_pitch_units(kBlocks) * 16;
-  static_assert(kMT * 16 * kPitch <= kGemvStageBytes, "stage overflow");
+  constexpr uint32_t kStageBytes = stage_bytes<kMT, kBlocks>();
+  constexpr int kSlots = ring_slots<kMT, kBlocks>();
+  static_assert(kSlots >= 2 && kStageBytes % 128 == 0, "ring slots");
   constexpr int kPerWarp = kBlocks / kGemvWarps;  // even: 8, 4 or 2
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int grid = gridDim.x, chunks = p.chunks;
@@ -203,10 +212,10 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
       for (int c = 0; c < chunks; ++c) {
         if (!mbar_wait(&s.empty[stage], phase ^ 1, kErrGemvEmptyWait))
           return;
-        mbar_arrive_expect_tx(&s.full[stage], stage_bytes<kMT, kBlocks>());
-        load_unit<kKind, kBlocks, kMT>(p, t, c, s.stage[stage],
+        mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
+        load_unit<kKind, kBlocks, kMT>(p, t, c, s.ring + stage * kStageBytes,
                                        &s.full[stage]);
-        if (++stage == kGemvStages) {
+        if (++stage == kSlots) {
           stage = 0;
           phase ^= 1;
         }
@@ -258,7 +267,7 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
         fetch_chunk(c + 1, next);
       if (!mbar_wait(&s.full[stage], phase, kErrGemvFullWait))
         return;
-      const uint8_t* rows = s.stage[stage] + g * kPitch;
+      const uint8_t* rows = s.ring + stage * kStageBytes + g * kPitch;
 #pragma unroll
       for (int pair = 0; pair < kPerWarp / 2; ++pair) {
         const int b = b0 + 2 * pair;
@@ -272,7 +281,7 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
       __syncwarp();
       if (lane == 0)
         mbar_arrive(&s.empty[stage]);
-      if (++stage == kGemvStages) {
+      if (++stage == kSlots) {
         stage = 0;
         phase ^= 1;
       }
@@ -305,7 +314,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GemvSmem& s = *reinterpret_cast<GemvSmem*>(smem_raw);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kGemvStages; ++i) {
+    for (int i = 0; i < kGemvMaxSlots; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], kGemvWarps);
     }

@@ -37,8 +37,10 @@ constexpr __host__ __device__ int gemv_pitch_units(int blocks) {
   return blocks * 34 / 16 + ((blocks * 34 / 16) % 4 == 0 ? 2 : 0);
 }
 
-constexpr int kGemvStageBytes = 36864;  // max over kinds of rows x pitch
-constexpr int kGemvStages = 2;
+// The weight ring: kGemvRingBytes split into as many equal slots (<= 8) as
+// one chunk of the kernel's kind fits, so several chunks stay in flight.
+constexpr int kGemvRingBytes = 73728;
+constexpr int kGemvMaxSlots = 8;
 constexpr int kGemvWarps = 8;  // consumer warps
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
 
