@@ -15,18 +15,19 @@
 // with twice the MMA work and no per-block epilogue: the K loop stays in the
 // tensor pipe.
 //
-// A tile is 256 weight rows x 128 prompt rows over a K range (split-K for
+// A tile is 256 weight rows x 256 prompt rows over a K range (split-K for
 // matrices with few tiles: FP32 partial sums per split, then a bandwidth-
 // bound pass adds them in split order, hip/ops.hip:2039-2119). Persistent
 // CTAs (one per SM) take units round-robin, split and prompt tile fastest,
 // so the CTAs sharing a weight tile run together and read it once from HBM.
 // Warp roles:
 //   warp 0      TMA producer: the fp16 activation tile of every K32 block
-//               (128 rows x 32, 64-byte swizzle)
+//               (256 rows x 32, 64-byte swizzle)
 //   warp 1      one thread issues tcgen05.mma: per block, two accumulators
-//               (rows 0-127, 128-255) x {hi, lo} x two K16 steps, M128 N128,
-//               into one of two accumulator pairs; commits every stage and
-//               every finished tile
+//               (rows 0-127, 128-255) x {hi, lo} x two K16 steps, M128 N256,
+//               into the accumulator pair (all 512 TMEM columns; the next
+//               tile's MMAs wait for the epilogue to read it); commits every
+//               stage and every finished tile
 //   warps 2-9   converters: thread r owns weight row r of the tile. Raw Q8
 //               rows arrive by TMA 8 blocks (272 bytes per row) at a time,
 //               issued by warp 2's lane 0 as soon as the previous chunk is in
@@ -49,12 +50,14 @@ namespace {
 
 constexpr int kTM = 128;                      // rows per accumulator
 constexpr int kRows = kPrefillTileRows;       // 256
-constexpr int kTN = kPrefillTileTokens;       // 128
+constexpr int kTN = kPrefillTileTokens;       // 256
+// accumulator pairs that fit the 512 TMEM columns (each pair 2 x kTN)
+constexpr int kAccBufs = 512 / (2 * kTN);
 constexpr int kStages = 3;
 constexpr int kWRowBytes = 272;               // 8 blocks of 34 bytes
 constexpr int kWBytes = kRows * kWRowBytes;   // 69,632
 constexpr int kAPartBytes = kRows * 64;       // 256 rows x 32 fp16
-constexpr int kBBytes = kTN * 64;             // 128 rows x 32 fp16
+constexpr int kBBytes = kTN * 64;             // kTN rows x 32 fp16
 constexpr int kThreads = 14 * 32;
 
 struct __align__(1024) PrefillSmem {
@@ -64,12 +67,12 @@ struct __align__(1024) PrefillSmem {
   uint8_t w[kWBytes];
   uint64_t w_full, w_empty;
   uint64_t full[kStages], empty[kStages];
-  uint64_t acc_full[2], acc_empty[2];
+  uint64_t acc_full[kAccBufs], acc_empty[kAccBufs];
   uint32_t tmem_base;
 };
 
 // tcgen05 instruction descriptor: kind::f16, A and B fp16 K-major, D fp32,
-// M = 128, N = 128.
+// M = 128, N = kTN.
 constexpr uint32_t kInstrDesc =
     (1u << 4) | (uint32_t(kTN >> 3) << 17) | (uint32_t(kTM >> 4) << 24);
 
@@ -193,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.full[i], 9);  // 8 converter warps + the producer's bytes
       mbar_init(&s.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(&s.acc_full[i], 1);
       mbar_init(&s.acc_empty[i], 4);
     }
@@ -233,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int j = 0;
       for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
         const Unit x = unit_of(p, u, token_tiles, bps);
-        const int buf = j & 1;
-        if (!mbar_wait(&s.acc_empty[buf], ((j >> 1) & 1) ^ 1,
+        const int buf = j % kAccBufs;
+        if (!mbar_wait(&s.acc_empty[buf], ((j / kAccBufs) & 1) ^ 1,
                        kErrPrefillWait))
           goto done;
         tc_fence_after();
@@ -363,8 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int j = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
       const Unit x = unit_of(p, u, token_tiles, bps);
-      const int buf = j & 1;
-      if (!mbar_wait(&s.acc_full[buf], (j >> 1) & 1, kErrPrefillWait))
+      const int buf = j % kAccBufs;
+      if (!mbar_wait(&s.acc_full[buf], (j / kAccBufs) & 1, kErrPrefillWait))
         goto done;
       tc_fence_after();
       const uint32_t base = tmem + (uint32_t(quarter * 32) << 16) +

@@ -17,13 +17,13 @@ enum PrefillKind : int {
 };
 
 // A work tile is 256 weight rows (two tensor-memory accumulators of 128)
-// by 128 prompt rows; SwiGLU tiles pair 128 gate rows with the same 128 up
+// by 256 prompt rows; SwiGLU tiles pair 128 gate rows with the same 128 up
 // rows.
 constexpr int kPrefillTileRows = 256;
-constexpr int kPrefillTileTokens = 128;
+constexpr int kPrefillTileTokens = 256;
 // Split-K: at most this many (tile, K range) units keep FP32 partial sums
 // (hip/ops.hpp:17-21, kMaxSplitUnits).
-constexpr int kPrefillMaxSplitUnits = 192;
+constexpr int kPrefillMaxSplitUnits = 128;
 constexpr size_t kPrefillPartialFloats =
     size_t(kPrefillMaxSplitUnits) * kPrefillTileRows * kPrefillTileTokens;
 
@@ -38,7 +38,7 @@ struct PrefillParams {
   // TMA maps (filled by launch_q8_prefill): weights as [rows][row_bytes / 8]
   // 8-byte elements with boxes of 34 elements (8 blocks) x 256 rows (128
   // for SwiGLU gate and up), and the activations as [rows of the buffer][K]
-  // fp16 with 128 x 32 boxes, 64-byte swizzle.
+  // fp16 with 256 x 32 boxes, 64-byte swizzle.
   alignas(64) CUtensorMap w_maps[4];
   alignas(64) CUtensorMap x_map;
   int kind;
