@@ -17,6 +17,14 @@
 #include "kernels.cuh"
 #include "tensor_map.hpp"
 
+// the residual norm reads a prompt projection's split partial sums in the
+// projection's tile layout
+static_assert(lfm3::kPrefillTileRows == 256 &&
+                  lfm3::kPrefillTileTokens == 256 &&
+                  lfm3::kSplitTileFloats ==
+                      lfm3::kPrefillTileRows * lfm3::kPrefillTileTokens,
+              "split partial layout");
+
 namespace lfm3 {
 namespace {
 
@@ -575,9 +583,12 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
   const auto prefill = [&](PrefillParams p, int first) {
     p.x_row0 = first;
     p.partial = split_partial_.as<float>();
+    int splits = 1;
     Timed(kPromptProjection, [&] {
-      Check(launch_q8_prefill(p, half, int(half_elems / size_t(p.K)), s));
+      Check(launch_q8_prefill(p, half, int(half_elems / size_t(p.K)), s,
+                              &splits));
     });
+    return splits;
   };
   const auto other = [&](auto launch) { Timed(kPromptOther, launch); };
   const auto rows = [&](auto launch) { Timed(kRowKernels, launch); };
@@ -596,8 +607,17 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
                                n_rows, width, s));
       });
   };
+  // a projection into the residual branch: its output, or the partial sums
+  // of its K splits, which the residual norm adds in split order
+  struct Branch {
+    const float* data;
+    SplitBranch split;
+    const SplitBranch* parts() const { return split.partial ? &split : nullptr; }
+  };
   const auto plain = [&](int K, int rows, int first_row, const float* in32,
-                         std::initializer_list<PrefillOutput> outs) {
+                         std::initializer_list<PrefillOutput> outs,
+                         bool planes = false) {
+    const Branch whole{outs.begin()->out, {}};
     if (bf16) {
       GemvParams g{};
       g.kind = kGemvPlain;
@@ -610,7 +630,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
         Throw(cudaErrorInvalidValue);
       Timed(kPromptProjection,
             [&] { Check(launch_bf16_gemv(g, in32, K, rows, s)); });
-      return;
+      return whole;
     }
     PrefillParams p{};
     p.kind = kPrefillPlain;
@@ -621,7 +641,14 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     for (const auto& o : outs)
       p.o[j++] = o;
     p.scale = scale + first_row;
-    prefill(p, first_row);
+    p.keep_splits = planes;
+    const int splits = prefill(p, first_row);
+    return planes && splits > 1
+               ? Branch{nullptr,
+                        SplitBranch{split_partial_.as<float>(), p.scale, splits,
+                                    (rows + kPrefillTileTokens - 1) /
+                                        kPrefillTileTokens}}
+               : whole;
   };
   const auto pout = [](const lfm3_tensor& t, float* o, int ld) {
     return PrefillOutput{static_cast<const uint8_t*>(t.data), o, int(t.rows),
@@ -646,6 +673,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     const auto& l = w.layers[i];
     const int rows_in = live_in[i], rows_out = live_out[i];
     const int o_in = n - rows_in, o = n - rows_out;
+    Branch branch{};
     if (c.layer_type[i] == LFM3_CONV) {
       float* p = p_.as<float>();
       plain(H, rows_in, o_in, zf + size_t(o_in) * H,
@@ -659,8 +687,8 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
                                 int(c.conv_width), true, s));
       });
       to_half(a + size_t(o) * H, o, rows_out, H);
-      plain(H, rows_out, o, a + size_t(o) * H,
-            {pout(l.out_proj, out + size_t(o) * H, H)});
+      branch = plain(H, rows_out, o, a + size_t(o) * H,
+                     {pout(l.out_proj, out + size_t(o) * H, H)}, true);
     } else {
       const int kvh = int(c.kv_heads[i]), kv = kvh * 128;
       const size_t stride = size_t(kv);
@@ -699,14 +727,14 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
                                 n, kv, int(position_), int(st.capacity), s));
         });
       to_half(a + size_t(o) * A, o, rows_out, A);
-      plain(A, rows_out, o, a + size_t(o) * A,
-            {pout(l.attn_out, out + size_t(o) * H, H)});
+      branch = plain(A, rows_out, o, a + size_t(o) * A,
+                     {pout(l.attn_out, out + size_t(o) * H, H)}, true);
     }
     rows([&] {
       Check(launch_residual_norm(
-          out + size_t(o) * H, static_cast<const float*>(l.post_norm.data),
+          branch.data, static_cast<const float*>(l.post_norm.data),
           x + size_t(o) * H, static_cast<const float*>(l.ffn_norm.data),
-          norm_out(o), rows_out, H, c.eps, s, false));
+          norm_out(o), rows_out, H, c.eps, s, false, branch.parts()));
     });
     if (bf16) {
       float* ff = ff_.as<float>();
@@ -723,8 +751,8 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       Timed(kPromptProjection, [&] {
         Check(launch_bf16_gemv(g, zf + size_t(o) * H, H, rows_out, s));
       });
-      plain(F, rows_out, o, ff + size_t(o) * F,
-            {pout(l.down, out + size_t(o) * H, H)});
+      branch = plain(F, rows_out, o, ff + size_t(o) * F,
+                     {pout(l.down, out + size_t(o) * H, H)});
     } else {
       float* ff = ff_.as<float>();
       unsigned* row_max = row_max_.as<unsigned>();
@@ -743,16 +771,18 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
         Check(launch_half_rows(ff + size_t(o) * F, row_max + o,
                                half_at(o, F), scale + o, rows_out, F, s));
       });
-      plain(F, rows_out, o, nullptr, {pout(l.down, out + size_t(o) * H, H)});
+      branch = plain(F, rows_out, o, nullptr,
+                     {pout(l.down, out + size_t(o) * H, H)}, true);
     }
     const bool last = i + 1 == L;
     rows([&] {
       Check(launch_residual_norm(
-          out + size_t(o) * H,
-          static_cast<const float*>(l.post_ffn_norm.data), x + size_t(o) * H,
+          branch.data, static_cast<const float*>(l.post_ffn_norm.data),
+          x + size_t(o) * H,
           last ? nullptr
                : static_cast<const float*>(w.layers[i + 1].norm.data),
-          last ? NormOut{} : norm_out(o), rows_out, H, c.eps, s, false));
+          last ? NormOut{} : norm_out(o), rows_out, H, c.eps, s, false,
+          branch.parts()));
     });
   }
   // frontier = output_norm(last row); logits from it when asked

@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kNormThreads)
     residual_norm_kernel(const float* __restrict__ branch,
                          const float* __restrict__ post_w, float* x,
                          const float* __restrict__ norm_w, NormOut out, int H,
-                         float eps) {
+                         float eps, SplitBranch split) {
   __shared__ float scratch[kNormThreads / 32];
   // the norm weights do not depend on the previous kernel: load them while
   // it finishes
@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kNormThreads)
   grid_dependency_wait();
   allow_dependents();
   const int row = blockIdx.x, groups = H / 8 / kNormThreads + 1;
+  const bool has_branch = branch || split.partial;
   float v[G][8];
   float b[G][8];
   float* xr = x + size_t(row) * H;
@@ -144,9 +145,29 @@ __global__ void __launch_bounds__(kNormThreads)
       const float4 c1 = *reinterpret_cast<const float4*>(br + 4);
       b[j][0] = c0.x, b[j][1] = c0.y, b[j][2] = c0.z, b[j][3] = c0.w;
       b[j][4] = c1.x, b[j][5] = c1.y, b[j][6] = c1.z, b[j][7] = c1.w;
+    } else if (split.partial) {
+      // the branch is scale[row] * (sum over K splits, in split order)
+      const int tile = (k0 >> 8) * split.token_tiles + (row >> 8);
+      const float* src = split.partial +
+                         size_t(tile) * split.splits * kSplitTileFloats +
+                         (row & 255) * 256 + (k0 & 255);
+      float4 s0 = __ldcg(reinterpret_cast<const float4*>(src));
+      float4 s1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      for (int q = 1; q < split.splits; ++q) {
+        const float* sq = src + size_t(q) * kSplitTileFloats;
+        const float4 d0 = __ldcg(reinterpret_cast<const float4*>(sq));
+        const float4 d1 = __ldcg(reinterpret_cast<const float4*>(sq + 4));
+        s0.x += d0.x, s0.y += d0.y, s0.z += d0.z, s0.w += d0.w;
+        s1.x += d1.x, s1.y += d1.y, s1.z += d1.z, s1.w += d1.w;
+      }
+      const float sc = split.scale[row];
+      b[j][0] = s0.x * sc, b[j][1] = s0.y * sc, b[j][2] = s0.z * sc,
+      b[j][3] = s0.w * sc;
+      b[j][4] = s1.x * sc, b[j][5] = s1.y * sc, b[j][6] = s1.z * sc,
+      b[j][7] = s1.w * sc;
     }
   }
-  if (branch) {
+  if (has_branch) {
     if (post_w) {
       float squares = 0;
       for (int j = 0; j < live; ++j)
@@ -289,12 +310,20 @@ cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block,
 cudaError_t launch_residual_norm(const float* branch, const float* post_w,
                                  float* x, const float* norm_w, NormOut out,
                                  int rows, int H, float eps,
-                                 cudaStream_t stream, bool pdl) {
+                                 cudaStream_t stream, bool pdl,
+                                 const SplitBranch* split) {
   if (H % 8 || H > kNormThreads * 8 * kNormMaxGroups)
     return cudaErrorInvalidValue;
+  SplitBranch sb{};
+  if (split) {
+    sb = *split;
+    if (branch || !sb.partial || !sb.scale || sb.splits < 1 ||
+        sb.token_tiles < (rows + 255) / 256 || H % 256)
+      return cudaErrorInvalidValue;
+  }
   if (!rows)
     return cudaSuccess;
-  void* args[] = {&branch, &post_w, &x, &norm_w, &out, &H, &eps};
+  void* args[] = {&branch, &post_w, &x, &norm_w, &out, &H, &eps, &sb};
   const void* kernel =
       H <= 2048   ? reinterpret_cast<const void*>(residual_norm_kernel<1>)
       : H <= 4096 ? reinterpret_cast<const void*>(residual_norm_kernel<2>)

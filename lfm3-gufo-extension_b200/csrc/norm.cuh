@@ -15,12 +15,26 @@ struct NormOut {
   float* scale;    // [rows] 2^-e for half
 };
 
-// x += RMSNorm_post(branch) (when branch; post_w may be null: plain add),
-// then out = RMSNorm(x) * norm_w (when norm_w). hip/ops.hip:890-970.
+// A residual branch still split over K: the FP32 partial sums of a prompt
+// projection, one [256 prompt rows][256 output rows] block per (tile, split)
+// with tile = output row tile * token_tiles + prompt row tile; the branch
+// is scale[prompt row] * (sum of the splits in split order).
+constexpr int kSplitTileFloats = 256 * 256;
+struct SplitBranch {
+  const float* partial;
+  const float* scale;
+  int splits;
+  int token_tiles;
+};
+
+// x += RMSNorm_post(branch) (when branch, or split; post_w may be null:
+// plain add), then out = RMSNorm(x) * norm_w (when norm_w).
+// hip/ops.hip:890-970.
 cudaError_t launch_residual_norm(const float* branch, const float* post_w,
                                  float* x, const float* norm_w, NormOut out,
                                  int rows, int H, float eps,
-                                 cudaStream_t stream, bool pdl);
+                                 cudaStream_t stream, bool pdl,
+                                 const SplitBranch* split = nullptr);
 
 // x[r] = embedding row ids[r] (F32 / F16 / BF16 / Q8_0 rows), then out =
 // RMSNorm(x) * norm_w. hip/ops.hip:858-875 fused with the first norm.

@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, int* splits) {
   int device = 0, sms = 148;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess)
@@ -572,6 +572,8 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
       p.first_tile[j] = tiles;
     p.row_tiles = tiles;
     // split K when the tiles leave SMs idle: fewest waves x K range
+    if (p.keep_splits && p.n_out != 1)
+      return cudaErrorInvalidValue;
     if (p.partial) {
       const int stages = p.K / 256, all = tiles * token_tiles;
       long best = long((all + sms - 1) / sms) * stages;
@@ -606,7 +608,9 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
   q8_prefill_tc_kernel<<<units < sms ? units : sms, kThreads, smem, stream>>>(
       p);
   e = cudaGetLastError();
-  if (e != cudaSuccess || p.splits == 1)
+  if (splits)
+    *splits = p.splits;
+  if (e != cudaSuccess || p.splits == 1 || p.keep_splits)
     return e;
   ReduceParams r{};
   r.partial = p.partial;

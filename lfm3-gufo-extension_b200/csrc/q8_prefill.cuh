@@ -56,12 +56,19 @@ struct PrefillParams {
   // Optional split-K workspace of kPrefillPartialFloats floats (16-byte
   // aligned); without it no projection splits K.
   float* partial;
+  // Plain with one output only: a projection that splits K leaves its FP32
+  // partial sums in `partial` ([row tile][token tile][split] blocks of
+  // [256 prompt rows][256 output rows], row scales not applied) for the
+  // consumer to add in split order, instead of reducing them into o[0].out
+  bool keep_splits;
 };
 
 // Fills the maps and the tiling of p (x is [x_rows][K] fp16; the pass reads
 // rows x_row0 .. x_row0 + tokens - 1) and launches. K must be a multiple of
 // 256.
+// *splits (optional) receives the K ranges used: with keep_splits set and
+// more than one, the output is left as partial sums in `partial`.
 cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
-                              cudaStream_t stream);
+                              cudaStream_t stream, int* splits = nullptr);
 
 }  // namespace lfm3
