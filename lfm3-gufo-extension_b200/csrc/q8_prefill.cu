@@ -402,9 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sc = __shfl_sync(0xffffffffu, lane_scale, i);
             const float gv = __uint_as_float(g[i]) * sc;
             const float uv = __uint_as_float(v[i]) * sc;
-            // BatchedSwiGLUActivationKernel's formula (hip/ops.hip:175-177);
-            // __frcp_rn is the correctly rounded 1 / x
-            const float sig = __frcp_rn(1.0F + expf(-gv));
+            // BatchedSwiGLUActivationKernel's formula (hip/ops.hip:175-177)
+            // with the hardware exponential and reciprocal (a few ulp in
+            // FP32): h is rounded to FP16 before the down projection reads
+            // it, and the correctly rounded forms cost the epilogue three
+            // times the stores' time
+            const float sig = __fdividef(1.0F, 1.0F + __expf(-gv));
             const float h = (gv * sig) * uv;
             if (valid && c * 32 + i < ntok)
               out[size_t(tok0 + c * 32 + i) * ld + row] = h;
