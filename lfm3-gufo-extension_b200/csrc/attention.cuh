@@ -65,7 +65,8 @@ cudaError_t launch_prompt_heads(float* q, float* k, const float* v, int ldq,
                                 const float* k_norm, const float* freq,
                                 const float* factors, __half* k16, __half* v16,
                                 int n, int heads, int kv_heads, int position,
-                                float eps, cudaStream_t stream);
+                                float eps, cudaStream_t stream,
+                                bool pdl = false);
 
 // Causal attention of n prompt rows at position: keys at or after position
 // from k16/v16 (chunk rows), earlier keys from the ring (slot t % capacity),
@@ -79,13 +80,14 @@ cudaError_t launch_prompt_attention(const float* q, int ldq, const __half* k16,
                                     int ldg, float* out, int n, int heads,
                                     int kv_heads, int position, int capacity,
                                     int window, float* scratch,
-                                    cudaStream_t stream);
+                                    cudaStream_t stream, bool pdl = false);
 size_t prompt_attention_scratch_floats(int heads, int rows, int keys);
 
 // Copies the last min(n, capacity) chunk rows into the ring at
 // position (hip/ops.hip:1737-1749).
 cudaError_t launch_store_kv(const __half* k16, const __half* v16,
                             __half* ring_k, __half* ring_v, int n, int stride,
-                            int position, int capacity, cudaStream_t stream);
+                            int position, int capacity, cudaStream_t stream,
+                            bool pdl = false);
 
 }  // namespace lfm3

@@ -31,6 +31,8 @@ __global__ void prompt_heads_kernel(float* q, float* k, const float* v,
                                     __half* v16, int heads, int kv_heads,
                                     int position, float eps) {
   const int head = blockIdx.x, row = blockIdx.y, i = threadIdx.x;
+  grid_dependency_wait();
+  allow_dependents();
   const bool is_key = head >= heads;
   const int kvh = head - heads;
   float* x = is_key ? k + size_t(row) * ldk + size_t(kvh) * kHeadDim
@@ -139,6 +141,8 @@ __global__ void __launch_bounds__(G * 32)
     return max(max(lo, 0), span_first);
   }();
   const int last_key = min(P + q0 + nq - 1, span_last);
+  grid_dependency_wait();
+  allow_dependents();
 
   // Q fragments: 16 queries x 128 dims, scaled, FP16
   const float scale = 0.0883883476483184405F * 1.44269504088896341F;
@@ -330,6 +334,8 @@ __global__ void prompt_combine_kernel(const float* __restrict__ partial,
                                       int spans) {
   const int rh = blockIdx.x, d = threadIdx.x;
   const int row = rh / heads, head = rh % heads;
+  grid_dependency_wait();
+  allow_dependents();
   const auto part = [&](int s) {
     return partial + ((size_t(s) * n + row) * heads + head) * (kHeadDim + 2);
   };
@@ -351,6 +357,8 @@ __global__ void store_kv_kernel(const __half* k, const __half* v, __half* ck,
                                 __half* cv, int n, int stride, int position,
                                 int capacity) {
   const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  grid_dependency_wait();
+  allow_dependents();
   const int kept = min(n, capacity), first = n - kept;
   if (i >= size_t(kept) * stride)
     return;
@@ -378,14 +386,13 @@ cudaError_t launch_prompt_heads(float* q, float* k, const float* v, int ldq,
                                 const float* k_norm, const float* freq,
                                 const float* factors, __half* k16, __half* v16,
                                 int n, int heads, int kv_heads, int position,
-                                float eps, cudaStream_t stream) {
+                                float eps, cudaStream_t stream, bool pdl) {
   if (n <= 0)
     return cudaSuccess;
-  note_launch();
-  prompt_heads_kernel<<<dim3(heads + kv_heads, n), 64, 0, stream>>>(
-      q, k, v, ldq, ldk, q_norm, k_norm, freq, factors, k16, v16, heads,
-      kv_heads, position, eps);
-  return cudaGetLastError();
+  return launch_kernel(prompt_heads_kernel, dim3(heads + kv_heads, n),
+                       dim3(64), 0, stream, pdl, q, k, v, ldq, ldk, q_norm,
+                       k_norm, freq, factors, k16, v16, heads, kv_heads,
+                       position, eps);
 }
 
 size_t prompt_attention_scratch_floats(int heads, int rows, int keys) {
@@ -400,7 +407,7 @@ cudaError_t launch_prompt_attention(const float* q, int ldq, const __half* k16,
                                     int ldg, float* out, int n, int heads,
                                     int kv_heads, int position, int capacity,
                                     int window, float* scratch,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, bool pdl) {
   if (kv_heads <= 0 || heads % kv_heads || n <= 0)
     return n == 0 ? cudaSuccess : cudaErrorInvalidValue;
   PromptArgs a{q,    ldq,   k16,       v16,      ring_k,   ring_v,
@@ -421,36 +428,31 @@ cudaError_t launch_prompt_attention(const float* q, int ldq, const __half* k16,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     configured = true;
   }
-  note_launch(a.spans > 1 ? 2 : 1);
-  switch (heads / kv_heads) {
-    case 2:
-      prompt_attention_kernel<2><<<grid, 64, kSmem, stream>>>(a);
-      break;
-    case 4:
-      prompt_attention_kernel<4><<<grid, 128, kSmem, stream>>>(a);
-      break;
-    case 8:
-      prompt_attention_kernel<8><<<grid, 256, kSmem, stream>>>(a);
-      break;
-    default:
-      return cudaErrorInvalidValue;
-  }
-  if (a.spans > 1)
-    prompt_combine_kernel<<<n * heads, kHeadDim, 0, stream>>>(
-        scratch, gate, ldg, out, n, heads, a.spans);
-  return cudaGetLastError();
+  const int group = heads / kv_heads;
+  if (group != 2 && group != 4 && group != 8)
+    return cudaErrorInvalidValue;
+  cudaError_t e = launch_kernel(
+      group == 2   ? prompt_attention_kernel<2>
+      : group == 4 ? prompt_attention_kernel<4>
+                   : prompt_attention_kernel<8>,
+      grid, dim3(32 * group), kSmem, stream, pdl, a);
+  if (e != cudaSuccess || a.spans == 1)
+    return e;
+  return launch_kernel(prompt_combine_kernel, dim3(n * heads), dim3(kHeadDim),
+                       0, stream, pdl, static_cast<const float*>(scratch), gate,
+                       ldg, out, n, heads, a.spans);
 }
 
 cudaError_t launch_store_kv(const __half* k16, const __half* v16,
                             __half* ring_k, __half* ring_v, int n, int stride,
-                            int position, int capacity, cudaStream_t stream) {
+                            int position, int capacity, cudaStream_t stream,
+                            bool pdl) {
   if (n <= 0)
     return cudaSuccess;
   const size_t count = size_t(min(n, capacity)) * stride;
-  note_launch();
-  store_kv_kernel<<<(count + 255) / 256, 256, 0, stream>>>(
-      k16, v16, ring_k, ring_v, n, stride, position, capacity);
-  return cudaGetLastError();
+  return launch_kernel(store_kv_kernel, dim3(unsigned((count + 255) / 256)),
+                       dim3(256), 0, stream, pdl, k16, v16, ring_k, ring_v, n,
+                       stride, position, capacity);
 }
 
 }  // namespace lfm3

@@ -37,6 +37,8 @@ __global__ void conv_window_kernel(const float* __restrict__ p,
   for (int t = 0; t < kCap; ++t)
     if (t < L)
       taps[t] = w[size_t(ch) * L + t];
+  grid_dependency_wait();
+  allow_dependents();
 #pragma unroll
   for (int t = 0; t < kCap - 1; ++t)
     if (t < L - 1)
@@ -62,6 +64,8 @@ __global__ void conv_history_kernel(const float* __restrict__ p,
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= H)
     return;
+  grid_dependency_wait();
+  allow_dependents();
   float past[kMaxWidth];
   for (int j = 0; j < L - 1; ++j)
     past[j] = product(p, history, n - (L - 1) + j, ch, H, L);
@@ -73,21 +77,21 @@ __global__ void conv_history_kernel(const float* __restrict__ p,
 
 cudaError_t launch_short_conv(const float* p, const float* w, float* history,
                               float* y, int n, int H, int L, bool update,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, bool pdl) {
   if (L < 2 || L > kMaxWidth || n < 0)
     return cudaErrorInvalidValue;
   if (n == 0)
     return cudaSuccess;
   const dim3 grid((H + 127) / 128, (n + kConvRows - 1) / kConvRows);
-  note_launch(update ? 2 : 1);
-  if (L == 7)  // the LFM3 width (l_cache)
-    conv_window_kernel<7><<<grid, 128, 0, stream>>>(p, w, history, y, n, H, L);
-  else
-    conv_window_kernel<0><<<grid, 128, 0, stream>>>(p, w, history, y, n, H, L);
-  if (update)
-    conv_history_kernel<<<(H + 127) / 128, 128, 0, stream>>>(p, history, n, H,
-                                                             L);
-  return cudaGetLastError();
+  // the LFM3 width (l_cache) as a compile-time constant
+  cudaError_t e = launch_kernel(L == 7 ? conv_window_kernel<7>
+                                       : conv_window_kernel<0>,
+                                grid, dim3(128), 0, stream, pdl, p, w,
+                                static_cast<const float*>(history), y, n, H, L);
+  if (e != cudaSuccess || !update)
+    return e;
+  return launch_kernel(conv_history_kernel, dim3((H + 127) / 128), dim3(128), 0,
+                       stream, pdl, p, history, n, H, L);
 }
 
 }  // namespace lfm3

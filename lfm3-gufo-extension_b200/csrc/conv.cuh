@@ -13,6 +13,6 @@ namespace lfm3 {
 // hip/ops.hip:971-1044, 1135-1151).
 cudaError_t launch_short_conv(const float* p, const float* w, float* history,
                               float* y, int n, int H, int L, bool update,
-                              cudaStream_t stream);
+                              cudaStream_t stream, bool pdl = false);
 
 }  // namespace lfm3

@@ -264,7 +264,6 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     gate_ = DeviceBuffer(R * c.heads * 4);
     a_ = DeviceBuffer(R * std::max(A, H) * 4);
     ff_ = DeviceBuffer(R * F * 4);
-    row_max_ = DeviceBuffer(R * 4);
     zf_ = DeviceBuffer(R * H * 4);
     split_partial_ = DeviceBuffer(kPrefillPartialFloats * 4);
     half_ = DeviceBuffer(R * width * 2);
@@ -557,6 +556,9 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
   cudaStream_t s = stream_;
   Check(cudaMemcpyAsync(ids_.data(), tokens.data(), tokens.size_bytes(),
                         cudaMemcpyHostToDevice, s));
+  // every prompt kernel waits for its predecessor in-kernel, so each may
+  // launch while the previous one finishes (programmatic dependent launch)
+  constexpr bool kPdl = true;
   // live rows (engine.cpp:304-323): after the last full-attention layer
   // only the frontier row, plus conv_width - 1 rows per trailing conv.
   std::vector<int> live_in(L, n), live_out(L, n);
@@ -586,7 +588,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     int splits = 1;
     Timed(kPromptProjection, [&] {
       Check(launch_q8_prefill(p, half, int(half_elems / size_t(p.K)), s,
-                              &splits));
+                              &splits, kPdl));
     });
     return splits;
   };
@@ -604,7 +606,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     if (!bf16)
       Timed(kPromptOther, [&] {
         Check(launch_half_rows(src, nullptr, half_at(row, width), scale + row,
-                               n_rows, width, s));
+                               n_rows, width, s, kPdl));
       });
   };
   // a projection into the residual branch: its output, or the partial sums
@@ -660,13 +662,13 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
     rows([&] {
       Check(launch_embed_norm(w.embedding.data, w.embedding.type,
                               ids_.as<uint32_t>(), nullptr, x, nullptr,
-                              NormOut{}, n, H, c.eps, s, false));
+                              NormOut{}, n, H, c.eps, s, kPdl));
     });
     rows([&] {
       Check(launch_residual_norm(
           nullptr, nullptr, x + size_t(o_in) * H,
           static_cast<const float*>(w.layers[0].norm.data),
-          norm_out(o_in), live_in[0], H, c.eps, s, false));
+          norm_out(o_in), live_in[0], H, c.eps, s, kPdl));
     });
   }
   for (int i = 0; i < L; ++i) {
@@ -684,7 +686,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
                                 static_cast<const float*>(l.conv.data),
                                 states_[i].conv.as<float>(),
                                 a + size_t(o_in) * H, rows_in, H,
-                                int(c.conv_width), true, s));
+                                int(c.conv_width), true, s, kPdl));
       });
       to_half(a + size_t(o) * H, o, rows_out, H);
       branch = plain(H, rows_out, o, a + size_t(o) * H,
@@ -709,7 +711,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
             q, k, v, A, kv, static_cast<const float*>(l.q_norm.data),
             static_cast<const float*>(l.k_norm.data), model_->frequencies(swa),
             swa ? nullptr : static_cast<const float*>(w.rope_freqs.data), kc,
-            vc, n, c.heads, kvh, int(position_), c.eps, s));
+            vc, n, c.heads, kvh, int(position_), c.eps, s, kPdl));
       });
       const int skip = n - std::min(n, rows_out);
       float* a = a_.as<float>();
@@ -719,12 +721,13 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
             vc + size_t(skip) * stride, st.k.as<__half>(), st.v.as<__half>(),
             g + size_t(skip) * c.heads, c.heads, a + size_t(skip) * A,
             n - skip, c.heads, kvh, int(position_) + skip, int(st.capacity),
-            swa ? int(c.window) : 0, prompt_scratch_.as<float>(), s));
+            swa ? int(c.window) : 0, prompt_scratch_.as<float>(), s, kPdl));
       });
       if (swa)
         other([&] {
           Check(launch_store_kv(kc, vc, st.k.as<__half>(), st.v.as<__half>(),
-                                n, kv, int(position_), int(st.capacity), s));
+                                n, kv, int(position_), int(st.capacity), s,
+                                kPdl));
         });
       to_half(a + size_t(o) * A, o, rows_out, A);
       branch = plain(A, rows_out, o, a + size_t(o) * A,
@@ -734,7 +737,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       Check(launch_residual_norm(
           branch.data, static_cast<const float*>(l.post_norm.data),
           x + size_t(o) * H, static_cast<const float*>(l.ffn_norm.data),
-          norm_out(o), rows_out, H, c.eps, s, false, branch.parts()));
+          norm_out(o), rows_out, H, c.eps, s, kPdl, branch.parts()));
     });
     if (bf16) {
       float* ff = ff_.as<float>();
@@ -754,9 +757,9 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       branch = plain(F, rows_out, o, ff + size_t(o) * F,
                      {pout(l.down, out + size_t(o) * H, H)});
     } else {
+      // h rows in FP32, then FP16 with per-row scales (half_rows finds each
+      // row's maximum itself)
       float* ff = ff_.as<float>();
-      unsigned* row_max = row_max_.as<unsigned>();
-      Check(cudaMemsetAsync(row_max + o, 0, size_t(rows_out) * 4, s));
       PrefillParams p{};
       p.kind = kPrefillSwiGLU;
       p.K = H;
@@ -765,11 +768,10 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
       p.o[0] = pout(l.gate, ff + size_t(o) * F, F);
       p.o[1] = pout(l.up, nullptr, F);
       p.scale = scale + o;
-      p.row_max = row_max + o;
       prefill(p, o);
       other([&] {
-        Check(launch_half_rows(ff + size_t(o) * F, row_max + o,
-                               half_at(o, F), scale + o, rows_out, F, s));
+        Check(launch_half_rows(ff + size_t(o) * F, nullptr, half_at(o, F),
+                               scale + o, rows_out, F, s, kPdl));
       });
       branch = plain(F, rows_out, o, nullptr,
                      {pout(l.down, out + size_t(o) * H, H)}, true);
@@ -781,7 +783,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
           x + size_t(o) * H,
           last ? nullptr
                : static_cast<const float*>(w.layers[i + 1].norm.data),
-          last ? NormOut{} : norm_out(o), rows_out, H, c.eps, s, false,
+          last ? NormOut{} : norm_out(o), rows_out, H, c.eps, s, kPdl,
           branch.parts()));
     });
   }
@@ -791,7 +793,7 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
         nullptr, nullptr, x + size_t(n - 1) * H,
         static_cast<const float*>(w.output_norm.data),
         NormOut{frontier_.as<float>(), z_split_.data(), nullptr, nullptr}, 1,
-        H, c.eps, s, false));
+        H, c.eps, s, kPdl));
   });
   if (want_logits)
     Timed(kDecodeProjection,

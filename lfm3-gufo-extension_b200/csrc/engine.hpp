@@ -176,7 +176,7 @@ private:
   DeviceBuffer layer_table_;  // LayerState[n_layers]
   DeviceBuffer frontier_, logits_;
   // workspace (this session's passes, and rounds it leads)
-  DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_, row_max_,
+  DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_,
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
       attn_tickets_, prompt_scratch_, split_partial_, zf_;

@@ -24,4 +24,26 @@ int set_last_error(int code, const char* message);
 void note_launch(int kernels = 1);
 unsigned long long launch_count();
 
+// kernel<<<grid, block, smem, stream>>>(args...), counted. With pdl the
+// kernel may start while the previous kernel in the stream finishes
+// (programmatic stream serialization): it must reach grid_dependency_wait()
+// before it touches anything an earlier kernel writes or reads.
+template <typename... Params, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block,
+                          size_t smem, cudaStream_t stream, bool pdl,
+                          Args... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  note_launch();
+  return cudaLaunchKernelEx(&config, kernel, Params(args)...);
+}
+
 }  // namespace lfm3

@@ -253,11 +253,62 @@ __global__ void __launch_bounds__(kNormThreads)
     finish_norm(v, live, nw, out, row, H, eps, scratch);
 }
 
+// One row per CTA held in registers, G 8-element groups per thread
+// (K <= 2048 G, K % 8 == 0): maximum, exponent, then 16-byte stores.
+template <int G>
 __global__ void __launch_bounds__(kNormThreads)
     half_rows_kernel(const float* __restrict__ x,
                      const unsigned* __restrict__ row_max, __half* values,
                      float* scale, int K) {
   __shared__ float scratch[kNormThreads / 32];
+  grid_dependency_wait();
+  allow_dependents();
+  const int row = blockIdx.x;
+  const float* src = x + size_t(row) * K;
+  float v[G][8];
+  float m = 0;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    if (k0 >= K)
+      break;
+    const float4 a = *reinterpret_cast<const float4*>(src + k0);
+    const float4 b = *reinterpret_cast<const float4*>(src + k0 + 4);
+    v[j][0] = a.x, v[j][1] = a.y, v[j][2] = a.z, v[j][3] = a.w;
+    v[j][4] = b.x, v[j][5] = b.y, v[j][6] = b.z, v[j][7] = b.w;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m = fmaxf(m, fabsf(v[j][i]));
+  }
+  const float maximum =
+      row_max ? __uint_as_float(row_max[row]) : block_max(m, scratch);
+  const int e = row_exponent(maximum);
+  if (threadIdx.x == 0)
+    scale[row] = ldexpf(1.0F, -e);
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int k0 = (threadIdx.x + j * kNormThreads) * 8;
+    if (k0 >= K)
+      break;
+    union {
+      __half h[8];
+      uint4 u;
+    } pack;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      pack.h[i] = __float2half_rn(ldexpf(v[j][i], e));
+    *reinterpret_cast<uint4*>(values + size_t(row) * K + k0) = pack.u;
+  }
+}
+
+// Any K: two passes over the row.
+__global__ void __launch_bounds__(kNormThreads)
+    half_rows_any_kernel(const float* __restrict__ x,
+                         const unsigned* __restrict__ row_max, __half* values,
+                         float* scale, int K) {
+  __shared__ float scratch[kNormThreads / 32];
+  grid_dependency_wait();
+  allow_dependents();
   const int row = blockIdx.x;
   const float* src = x + size_t(row) * K;
   float maximum;
@@ -351,13 +402,20 @@ cudaError_t launch_embed_norm(const void* table, uint32_t type,
 
 cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
                              __half* values, float* scale, int rows, int K,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, bool pdl) {
   if (!rows)
     return cudaSuccess;
-  note_launch();
-  half_rows_kernel<<<rows, kNormThreads, 0, stream>>>(x, row_max, values,
-                                                       scale, K);
-  return cudaGetLastError();
+  const int groups = (K / 8 + kNormThreads - 1) / kNormThreads;
+  const bool vector = K % 8 == 0 && groups <= 8 &&
+                      reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(values) % 16 == 0;
+  const auto kernel = !vector      ? half_rows_any_kernel
+                      : groups <= 1 ? half_rows_kernel<1>
+                      : groups <= 2 ? half_rows_kernel<2>
+                      : groups <= 4 ? half_rows_kernel<4>
+                                    : half_rows_kernel<8>;
+  return launch_kernel(kernel, dim3(rows), dim3(kNormThreads), 0, stream, pdl,
+                       x, row_max, values, scale, K);
 }
 
 cudaError_t launch_split_rows(const float* x, void* split, int rows, int K,

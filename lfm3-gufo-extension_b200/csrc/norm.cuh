@@ -51,7 +51,7 @@ cudaError_t launch_embed_norm(const void* table, uint32_t type,
 // (hip/q8_prefill.hpp:52-74).
 cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
                              __half* values, float* scale, int rows, int K,
-                             cudaStream_t stream);
+                             cudaStream_t stream, bool pdl = false);
 
 // FP32 rows -> split records (x = hi + lo, fp16 each).
 cudaError_t launch_split_rows(const float* x, void* split, int rows, int K,

@@ -35,8 +35,8 @@
 //               lo A tiles (fp16, K-major, 64-byte swizzle)
 //   warps 10-13 epilogue: thread owns one TMEM lane (weight row) of both
 //               accumulators; applies the prompt-row scales and writes the
-//               outputs (SwiGLU: silu(g) * u and per-row maxima; split tiles:
-//               the FP32 partial sums)
+//               outputs (SwiGLU: silu(g) * u, optionally per-row maxima;
+//               split tiles: the FP32 partial sums)
 // Stages hand over through mbarriers and every wait is bounded: a pipeline
 // that stops making progress reports kErrPrefillWait and the CTA returns.
 // When that happens every copy and MMA it issued is seconds old and complete.
@@ -212,10 +212,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // launched behind the previous kernel (programmatic dependent launch): the
+  // weight chunks, conversions and MMAs read nothing it writes; the
+  // activation tiles and the epilogue wait for it
+  allow_dependents();
 
   if (warp == 0) {
     // ---- activation tiles
     if (lane == 0) {
+      grid_dependency_wait();
       Ring b;
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const Unit x = unit_of(p, u, token_tiles, bps);
@@ -361,6 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---- epilogue: thread owns TMEM lane r of both accumulators
+    grid_dependency_wait();
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     int j = 0;
@@ -413,6 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               out[size_t(tok0 + c * 32 + i) * ld + row] = h;
             g[i] = valid ? __float_as_uint(fabsf(h)) : 0u;
           }
+          if (!p.row_max)
+            continue;
           // max |h| over the warp's 32 rows per prompt row (non-negative
           // floats order as their bit patterns); lane i keeps row i's
           unsigned mine = 0;
@@ -421,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const unsigned m = __reduce_max_sync(0xffffffffu, g[i]);
             mine = lane == i ? m : mine;
           }
-          if (tl < ntok && p.row_max)
+          if (tl < ntok)
             atomicMax(p.row_max + tok0 + tl, mine);
         }
         continue;
@@ -498,6 +506,8 @@ struct ReduceParams {
 
 __global__ void __launch_bounds__(256)
     prefill_split_reduce_kernel(const __grid_constant__ ReduceParams p) {
+  grid_dependency_wait();
+  allow_dependents();
   const int quads = kRows / 4;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;  // tile, t, row quad
   const int tile = e / (kTN * quads);
@@ -534,7 +544,7 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
-                              cudaStream_t stream, int* splits) {
+                              cudaStream_t stream, int* splits, bool pdl) {
   int device = 0, sms = 148;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess)
@@ -607,10 +617,8 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
   if (e != cudaSuccess)
     return e;
   const int units = p.row_tiles * token_tiles * p.splits;
-  note_launch();
-  q8_prefill_tc_kernel<<<units < sms ? units : sms, kThreads, smem, stream>>>(
-      p);
-  e = cudaGetLastError();
+  e = launch_kernel(q8_prefill_tc_kernel, dim3(units < sms ? units : sms),
+                    dim3(kThreads), smem, stream, pdl, p);
   if (splits)
     *splits = p.splits;
   if (e != cudaSuccess || p.splits == 1 || p.keep_splits)
@@ -630,10 +638,9 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
     r.ld[j] = p.o[j].ld;
   }
   const long threads = long(p.row_tiles) * token_tiles * kTN * (kRows / 4);
-  note_launch();
-  prefill_split_reduce_kernel<<<unsigned((threads + 255) / 256), 256, 0,
-                                stream>>>(r);
-  return cudaGetLastError();
+  return launch_kernel(prefill_split_reduce_kernel,
+                       dim3(unsigned((threads + 255) / 256)), dim3(256), 0,
+                       stream, pdl, r);
 }
 
 }  // namespace lfm3

@@ -69,6 +69,7 @@ struct PrefillParams {
 // *splits (optional) receives the K ranges used: with keep_splits set and
 // more than one, the output is left as partial sums in `partial`.
 cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
-                              cudaStream_t stream, int* splits = nullptr);
+                              cudaStream_t stream, int* splits = nullptr,
+                              bool pdl = false);
 
 }  // namespace lfm3
