@@ -28,6 +28,9 @@ struct DecodeAttentionParams {
   int heads, kv_heads;
   int window;  // 0: full attention
   int max_splits;  // key spans per (row, KV group), <= kMaxDecodeSplits
+  // spans launched per (row, KV group): at least the most any row of the
+  // round uses (decode_spans_used); 0 launches kMaxDecodeSplits
+  int span_grid;
   float eps;
   void* out_split;   // [rows][heads * 128] split records
   float* out_f32;    // optional [rows][heads * 128]
@@ -54,6 +57,8 @@ cudaError_t launch_decode_attention(const DecodeAttentionParams& p, int rows,
                                     cudaStream_t stream, bool pdl);
 
 size_t decode_attention_partial_floats(int heads);
+// Key spans the decode attention kernel uses for a row at `position`.
+int decode_spans_used(int position, int window, int max_splits);
 
 // ---- prompt pass ------------------------------------------------------------
 

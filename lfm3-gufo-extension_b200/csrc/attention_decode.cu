@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kThreads)
   const int tiles = (position + 1 - first + kDecodeTile - 1) / kDecodeTile;
   const int max_splits = max(1, min(p.max_splits, kMaxDecodeSplits));
   const int per = (tiles + max_splits - 1) / max_splits;
-  const int used = (tiles + per - 1) / per;
+  const int used = (tiles + per - 1) / per;  // decode_spans_used
   if (split >= used)
     return;
   const int begin = first + split * per * kDecodeTile;
@@ -295,7 +295,10 @@ template <int G>
 cudaError_t launch_group(const DecodeAttentionParams& p, int rows,
                          cudaStream_t stream, bool pdl) {
   cudaLaunchConfig_t config = {};
-  config.gridDim = dim3(p.kv_heads, kMaxDecodeSplits, rows);
+  const int spans = p.span_grid > 0 && p.span_grid < kMaxDecodeSplits
+                        ? p.span_grid
+                        : kMaxDecodeSplits;
+  config.gridDim = dim3(p.kv_heads, spans, rows);
   config.blockDim = dim3(kThreads);
   config.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -308,6 +311,14 @@ cudaError_t launch_group(const DecodeAttentionParams& p, int rows,
 }
 
 }  // namespace
+
+int decode_spans_used(int position, int window, int max_splits) {
+  const int first = window > 0 ? max(0, position + 1 - window) : 0;
+  const int tiles = (position + 1 - first + kDecodeTile - 1) / kDecodeTile;
+  const int splits = max(1, min(max_splits, kMaxDecodeSplits));
+  const int per = (tiles + splits - 1) / splits;
+  return (tiles + per - 1) / per;
+}
 
 size_t decode_attention_partial_floats(int heads) {
   return size_t(kMaxBatch) * heads * kMaxDecodeSplits * (kHeadDim + 2);

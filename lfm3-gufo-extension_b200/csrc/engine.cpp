@@ -482,6 +482,10 @@ void Session::DecodeRound(std::span<Session* const> batch,
       ap.window = swa ? int(c.window) : 0;
       // about two CTAs per SM over the round's (row, group) pairs
       ap.max_splits = std::max(1, 4 * model_->sms() / (B * int(c.kv_heads[i])));
+      for (int r = 0; r < B; ++r)
+        ap.span_grid = std::max(
+            ap.span_grid,
+            decode_spans_used(rows.position[r], ap.window, ap.max_splits));
       ap.eps = c.eps;
       ap.out_split = a_split_.data();
       ap.partials = attn_partials_.as<float>();

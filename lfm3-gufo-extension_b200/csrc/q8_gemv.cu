@@ -121,15 +121,16 @@ __device__ __forceinline__ void run_block(const uint8_t* block, int pitch,
     uint32_t a1[4], a2[4];
     float d[2];
     block_fragments<kAligned>(block + m * 16 * pitch, pitch, cq, a1, a2, d);
-    float cc[4] = {0, 0, 0, 0};
-    mma_f16(cc, a1, xh.x, xh.y);
-    mma_f16(cc, a1, xl.x, xl.y);
-    mma_f16(cc, a2, xh.z, xh.w);
-    mma_f16(cc, a2, xl.z, xl.w);
-    acc[m][0] = fmaf(d[0], cc[0], acc[m][0]);
-    acc[m][1] = fmaf(d[0], cc[1], acc[m][1]);
-    acc[m][2] = fmaf(d[1], cc[2], acc[m][2]);
-    acc[m][3] = fmaf(d[1], cc[3], acc[m][3]);
+    // the hi and lo input terms in two independent MMA chains
+    float ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
+    mma_f16(ch, a1, xh.x, xh.y);
+    mma_f16(cl, a1, xl.x, xl.y);
+    mma_f16(ch, a2, xh.z, xh.w);
+    mma_f16(cl, a2, xl.z, xl.w);
+    acc[m][0] = fmaf(d[0], ch[0] + cl[0], acc[m][0]);
+    acc[m][1] = fmaf(d[0], ch[1] + cl[1], acc[m][1]);
+    acc[m][2] = fmaf(d[1], ch[2] + cl[2], acc[m][2]);
+    acc[m][3] = fmaf(d[1], ch[3] + cl[3], acc[m][3]);
   }
 }
 
