@@ -6,8 +6,13 @@
 // CTA whose span ends at the row's position also stores the new K/V row in
 // the ring. Keys stream through shared memory in tiles of 64 and an online
 // softmax keeps FP32 scores, probabilities and accumulators (the decode
-// precision of hip/ops.hip:1562-1691). With several spans, each CTA writes
-// its maximum, denominator and unnormalised output, and whichever CTA of the
+// precision of hip/ops.hip:1562-1691). Both products run on the tensor cores
+// (mma.sync m16n8k16, FP32 accumulation) with the FP32 operands split in two
+// fp16 terms, x = hi + lo (22 significant bits): S^T = K (Q_hi + Q_lo)^T with
+// the keys as M and the group's heads (padded to 8) as N, then
+// O^T = V^T (P_hi + P_lo)^T with the 128 dimensions as M; K and V are the
+// cache's fp16 values, exactly. With several spans, each CTA writes its
+// maximum, denominator and unnormalised output, and whichever CTA of the
 // group finishes last (a ticket, not a wait) merges them in span order and
 // applies the gate (hip/ops.hip:1710-1728).
 #include "attention.cuh"
@@ -18,18 +23,50 @@ namespace lfm3 {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kKPitch = 272;  // bytes per K row in shared memory
+constexpr int kWarps = kThreads / 32;
 constexpr float kScoreScale = 0.0883883476483184405F;  // 1 / sqrt(128)
 
-template <int G>
+// Shared rows are 16-byte pieces of 8 fp16; piece c of row i sits at
+// c ^ (i & 7), so the eight rows of one ldmatrix fetch hit distinct banks.
+__device__ __forceinline__ int at128(int row, int piece) {  // 128-wide rows
+  return row * kHeadDim + ((piece ^ (row & 7)) << 3);
+}
+__device__ __forceinline__ int at64(int row, int piece) {  // 64-wide rows
+  return row * kDecodeTile + ((piece ^ (row & 7)) << 3);
+}
+
 struct DecodeSmem {
-  float q[G][kHeadDim];
-  alignas(16) uint8_t k[kDecodeTile][kKPitch];
-  alignas(16) __half v[kDecodeTile][kHeadDim];
-  float s[kDecodeTile][G];  // scores, then probabilities
-  float m[G], l[G], alpha[G];
+  alignas(16) __half k[kDecodeTile * kHeadDim];  // [key][dim]
+  alignas(16) __half v[kDecodeTile * kHeadDim];  // [key][dim]
+  alignas(16) __half qh[8 * kHeadDim], ql[8 * kHeadDim];      // [head][dim]
+  alignas(16) __half ph[8 * kDecodeTile], pl[8 * kDecodeTile];  // [head][key]
+  float tile_max[kWarps][8];
+  float l[kWarps][8];  // running denominators of each warp's keys
+  float m[8], lsum[8];
   int last;
 };
+// After the key loop the K tile holds the output and the merge weights.
+static_assert(sizeof(float) * (8 * kHeadDim + 2 * 8 * kMaxDecodeSplits) <=
+                  sizeof(__half) * kDecodeTile * kHeadDim,
+              "output staging fits the K tile");
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_addr(p)));
+}
 
 // RMSNorm (weight w) and RoPE of one 128-wide head held as pairs
 // (i, i + 64) for i in {lane, lane + 32}; returns the rotated pairs.
@@ -56,10 +93,11 @@ __device__ __forceinline__ void norm_rope(float (&x0)[2], float (&x1)[2],
   }
 }
 
+// Four CTAs per SM (128 registers): a round's spans run in one wave.
 template <int G>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
     decode_attention_kernel(const __grid_constant__ DecodeAttentionParams p) {
-  __shared__ DecodeSmem<G> s;
+  __shared__ DecodeSmem s;
   const int g = blockIdx.x, split = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   grid_dependency_wait();
@@ -82,17 +120,26 @@ __global__ void __launch_bounds__(kThreads)
   const int end = min(begin + per * kDecodeTile, position + 1);
   const size_t stride = size_t(p.kv_heads) * kHeadDim;
 
-  // ---- query heads of this group (normalised, rotated, FP32)
-  for (int h = warp; h < G; h += kThreads / 32) {
-    const float* qr = p.q + size_t(r) * p.ldq + size_t(g * G + h) * kHeadDim;
-    float x0[2] = {qr[lane], qr[lane + 32]};
-    float x1[2] = {qr[lane + 64], qr[lane + 96]};
-    if (!op)
-      norm_rope(x0, x1, p.q_norm, p.freq, p.factors, position, p.eps, lane);
-    s.q[h][lane] = x0[0];
-    s.q[h][lane + 32] = x0[1];
-    s.q[h][lane + 64] = x1[0];
-    s.q[h][lane + 96] = x1[1];
+  // ---- query heads of this group (normalised, rotated), as hi + lo fp16
+  // terms; heads G..7 are zero
+  for (int h = warp; h < 8; h += kWarps) {
+    float x0[2] = {0, 0}, x1[2] = {0, 0};
+    if (h < G) {
+      const float* qr =
+          p.q + size_t(r) * p.ldq + size_t(g * G + h) * kHeadDim;
+      x0[0] = qr[lane], x0[1] = qr[lane + 32];
+      x1[0] = qr[lane + 64], x1[1] = qr[lane + 96];
+      if (!op)
+        norm_rope(x0, x1, p.q_norm, p.freq, p.factors, position, p.eps, lane);
+    }
+    const float e[4] = {x0[0], x0[1], x1[0], x1[1]};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      const SplitPair t = split_value(e[j]);
+      s.qh[at128(h, i / 8) + i % 8] = t.hi;
+      s.ql[at128(h, i / 8) + i % 8] = t.lo;
+    }
   }
   // ---- the new K/V row goes to its ring slot (span holding `position`)
   if (!op && split == used - 1 && warp == 0) {
@@ -112,15 +159,18 @@ __global__ void __launch_bounds__(kThreads)
       state.v[slot + i + 64] = __float2half_rn(vr[i + 64]);
     }
   }
-  if (tid < G) {
-    s.m[tid] = -INFINITY;
-    s.l[tid] = 0;
-  }
-  float acc[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-    acc[h] = 0;
+  if (tid < kWarps * 8)
+    s.l[tid / 8][tid % 8] = 0;
   __syncthreads();
+
+  // fragment coordinates: row fg (and fg + 8), column pair 2 cq, 2 cq + 1
+  const int fg = lane / 4, cq = lane % 4;
+  // ldmatrix lane roles: matrix mj = lane / 8 takes its row from lane mrow
+  const int mj = lane / 8, mrow = lane % 8;
+  // this thread's running maxima of heads 2 cq, 2 cq + 1 (every thread holds
+  // the same values) and its O^T fragments of dimension tiles 2 w, 2 w + 1
+  float mrun[2] = {-INFINITY, -INFINITY};
+  float o[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 
   // ---- K and V rows of a tile (16-byte pieces, L1 bypassed: the current
   // row was just written by this CTA), loaded into registers one tile ahead
@@ -155,85 +205,141 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int j = 0; j < kPieces; ++j) {
       const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-      *reinterpret_cast<uint4*>(&s.k[key][piece * 16]) = kr[j];
-      *reinterpret_cast<uint4*>(&s.v[key][piece * 8]) = vr[j];
+      *reinterpret_cast<uint4*>(&s.k[at128(key, piece)]) = kr[j];
+      *reinterpret_cast<uint4*>(&s.v[at128(key, piece)]) = vr[j];
     }
     __syncthreads();
     if (base + kDecodeTile < end)
       load_tile(base + kDecodeTile);  // in flight during this tile's math
-    // ---- scores: thread owns key tid % 64 and half of the heads
+
+    // ---- S^T = K Q^T: warp w owns keys 16 w .. 16 w + 15
+    float sh[4] = {0, 0, 0, 0}, sl[4] = {0, 0, 0, 0};
     {
-      const int t = tid % kDecodeTile, hs = tid / kDecodeTile;
-      constexpr int kH = G / 2;
-      float dot[kH];
+      const int key = warp * 16 + (mj & 1) * 8 + mrow;
 #pragma unroll
-      for (int j = 0; j < kH; ++j)
-        dot[j] = 0;
-      const uint4* krow = reinterpret_cast<const uint4*>(s.k[t]);
-#pragma unroll 4
-      for (int c = 0; c < 16; ++c) {
-        const uint4 raw = krow[c];
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-        float kf[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
-          kf[2 * i] = f.x;
-          kf[2 * i + 1] = f.y;
-        }
-#pragma unroll
-        for (int j = 0; j < kH; ++j) {
-          const float* qh = s.q[hs * kH + j] + c * 8;
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dot[j] = fmaf(qh[i], kf[i], dot[j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kH; ++j)
-        s.s[t][hs * kH + j] = t < n ? dot[j] * kScoreScale : -INFINITY;
-    }
-    __syncthreads();
-    // ---- online softmax per head
-    for (int h = warp; h < G; h += kThreads / 32) {
-      const float a = s.s[lane][h], b = s.s[lane + 32][h];
-      const float top = warp_max(fmaxf(a, b));
-      const float old = s.m[h];
-      const float next = fmaxf(old, top);
-      const float pa = expf(a - next), pb = expf(b - next);
-      s.s[lane][h] = pa;
-      s.s[lane + 32][h] = pb;
-      const float sum = warp_sum(pa + pb);
-      if (lane == 0) {
-        const float alpha = expf(old - next);  // 0 for the first tile
-        s.alpha[h] = alpha;
-        s.l[h] = s.l[h] * alpha + sum;
-        s.m[h] = next;
+      for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+        uint32_t a[4], bh[2], bl[2];
+        ldsm_x4(a, &s.k[at128(key, 2 * ks + (mj >> 1))]);
+        ldsm_x2(bh, &s.qh[at128(mrow, 2 * ks + (mj & 1))]);
+        ldsm_x2(bl, &s.ql[at128(mrow, 2 * ks + (mj & 1))]);
+        mma_f16(sh, a, bh[0], bh[1]);
+        mma_f16(sl, a, bl[0], bl[1]);
       }
     }
-    __syncthreads();
-    // ---- P V: thread owns dimension tid of every head
-    {
+    // this thread: keys k0 = 16 w + fg and k0 + 8, heads 2 cq and 2 cq + 1
+    const int k0 = warp * 16 + fg;
+    float sc[4];
 #pragma unroll
-      for (int h = 0; h < G; ++h)
-        acc[h] *= s.alpha[h];
-      for (int t = 0; t < n; ++t) {
-        const float vt = __half2float(s.v[t][tid]);
+    for (int i = 0; i < 4; ++i)
+      sc[i] = (sh[i] + sl[i]) * kScoreScale;
+    if (k0 >= n)
+      sc[0] = sc[1] = -INFINITY;
+    if (k0 + 8 >= n)
+      sc[2] = sc[3] = -INFINITY;
+    float t0 = fmaxf(sc[0], sc[2]), t1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
-        for (int h = 0; h < G; ++h)
-          acc[h] = fmaf(s.s[t][h], vt, acc[h]);
-      }
+    for (int x = 4; x < 32; x <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, x));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, x));
+    }
+    if (fg == 0) {
+      s.tile_max[warp][2 * cq] = t0;
+      s.tile_max[warp][2 * cq + 1] = t1;
     }
     __syncthreads();
+    // ---- online softmax over the tile's keys of every warp
+    float top[2] = {s.tile_max[0][2 * cq], s.tile_max[0][2 * cq + 1]};
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) {
+      top[0] = fmaxf(top[0], s.tile_max[w][2 * cq]);
+      top[1] = fmaxf(top[1], s.tile_max[w][2 * cq + 1]);
+    }
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float next = fmaxf(mrun[h], top[h]);
+      alpha[h] = expf(mrun[h] - next);  // 0 for the first tile
+      mrun[h] = next;
+    }
+    const float pr[4] = {expf(sc[0] - mrun[0]), expf(sc[1] - mrun[1]),
+                         expf(sc[2] - mrun[0]), expf(sc[3] - mrun[1])};
+    float q0 = pr[0] + pr[2], q1 = pr[1] + pr[3];
+#pragma unroll
+    for (int x = 4; x < 32; x <<= 1) {
+      q0 += __shfl_xor_sync(0xffffffffu, q0, x);
+      q1 += __shfl_xor_sync(0xffffffffu, q1, x);
+    }
+    if (fg == 0) {
+      s.l[warp][2 * cq] = s.l[warp][2 * cq] * alpha[0] + q0;
+      s.l[warp][2 * cq + 1] = s.l[warp][2 * cq + 1] * alpha[1] + q1;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int head = 2 * cq + (i & 1), key = k0 + (i >> 1) * 8;
+      const SplitPair t = split_value(pr[i]);
+      s.ph[at64(head, key / 8) + key % 8] = t.hi;
+      s.pl[at64(head, key / 8) + key % 8] = t.lo;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      o[mt][0] *= alpha[0];
+      o[mt][1] *= alpha[1];
+      o[mt][2] *= alpha[0];
+      o[mt][3] *= alpha[1];
+    }
+    __syncthreads();
+    // ---- O^T += V^T P^T: warp w owns dimensions 32 w .. 32 w + 31
+#pragma unroll
+    for (int ks = 0; ks < kDecodeTile / 16; ++ks) {
+      uint32_t bh[2], bl[2];
+      ldsm_x2(bh, &s.ph[at64(mrow, 2 * ks + (mj & 1))]);
+      ldsm_x2(bl, &s.pl[at64(mrow, 2 * ks + (mj & 1))]);
+      const int key = ks * 16 + (mj >> 1) * 8 + mrow;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t a[4];
+        ldsm_x4_trans(a, &s.v[at128(key, 2 * (2 * warp + mt) + (mj & 1))]);
+        mma_f16(o[mt], a, bh[0], bh[1]);
+        mma_f16(o[mt], a, bl[0], bl[1]);
+      }
+    }
+    __syncthreads();  // before the next tile overwrites k, v and p
   }
 
+  // ---- O (FP32 [head][dim]), maxima and denominators to shared memory
+  float* so = reinterpret_cast<float*>(s.k);
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    const int dim = (2 * warp + mt) * 16 + fg;
+    so[(2 * cq) * kHeadDim + dim] = o[mt][0];
+    so[(2 * cq + 1) * kHeadDim + dim] = o[mt][1];
+    so[(2 * cq) * kHeadDim + dim + 8] = o[mt][2];
+    so[(2 * cq + 1) * kHeadDim + dim + 8] = o[mt][3];
+  }
+  if (warp == 0 && fg == 0) {
+    s.m[2 * cq] = mrun[0];
+    s.m[2 * cq + 1] = mrun[1];
+  }
+  __syncthreads();
+  if (tid < 8) {
+    float l = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w)
+      l += s.l[w][tid];
+    s.lsum[tid] = l;
+  }
+  __syncthreads();
   const int d = tid;
+  float acc[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    acc[h] = so[h * kHeadDim + d];
   if (used == 1) {
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const int head = g * G + h;
       const float gate = p.gate[size_t(r) * p.ldg + head];
-      const float y = (acc[h] / s.l[h]) / (1 + expf(-gate));
+      const float y = (acc[h] / s.lsum[h]) / (1 + expf(-gate));
       if (p.out_split)
         store_split(p.out_split, r, p.heads * kHeadDim, head * kHeadDim + d, y);
       if (p.out_f32)
@@ -252,7 +358,7 @@ __global__ void __launch_bounds__(kThreads)
     float* out = part(split, g * G + h);
     if (d == 0) {
       out[0] = s.m[h];
-      out[1] = s.l[h];
+      out[1] = s.lsum[h];
     }
     out[2 + d] = acc[h];
   }
@@ -269,21 +375,45 @@ __global__ void __launch_bounds__(kThreads)
   if (!s.last)
     return;
   __threadfence();
+  // every span's maximum and denominator at once, then the span weights
+  // exp(m_sp - max) per head (one thread per head), then the outputs
+  float* mw = so + 8 * kHeadDim;  // [span][8]
+  float* lw = mw + 8 * kMaxDecodeSplits;
+  for (int i = tid; i < used * G; i += kThreads) {
+    const int sp = i / G, h = i % G;
+    const float* pp = part(sp, g * G + h);
+    mw[sp * 8 + h] = __ldcg(pp);
+    lw[sp * 8 + h] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float maximum = -INFINITY;
+    for (int sp = 0; sp < used; ++sp)
+      maximum = fmaxf(maximum, mw[sp * 8 + tid]);
+    float sum = 0;
+    for (int sp = 0; sp < used; ++sp) {
+      const float w = expf(mw[sp * 8 + tid] - maximum);
+      mw[sp * 8 + tid] = w;
+      sum = fmaf(lw[sp * 8 + tid], w, sum);
+    }
+    s.lsum[tid] = sum;
+  }
+  __syncthreads();
+  float value[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    value[h] = 0;
+#pragma unroll 2
+  for (int sp = 0; sp < used; ++sp)
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+      value[h] = fmaf(__ldcg(part(sp, g * G + h) + 2 + d), mw[sp * 8 + h],
+                      value[h]);
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     const int head = g * G + h;
-    float maximum = -INFINITY;
-    for (int sp = 0; sp < used; ++sp)
-      maximum = fmaxf(maximum, __ldcg(part(sp, head)));
-    float sum = 0, value = 0;
-    for (int sp = 0; sp < used; ++sp) {
-      const float* pp = part(sp, head);
-      const float w = expf(__ldcg(pp) - maximum);
-      sum = fmaf(__ldcg(pp + 1), w, sum);
-      value = fmaf(__ldcg(pp + 2 + d), w, value);
-    }
     const float gate = p.gate[size_t(r) * p.ldg + head];
-    const float y = (value / sum) / (1 + expf(-gate));
+    const float y = (value[h] / s.lsum[h]) / (1 + expf(-gate));
     if (p.out_split)
       store_split(p.out_split, r, p.heads * kHeadDim, head * kHeadDim + d, y);
     if (p.out_f32)
