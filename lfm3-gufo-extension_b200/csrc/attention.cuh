@@ -28,9 +28,17 @@ struct DecodeAttentionParams {
   int heads, kv_heads;
   int window;  // 0: full attention
   int max_splits;  // key spans per (row, KV group), <= kMaxDecodeSplits
+  // > 0: key tiles per span instead (every row's spans about equally long,
+  // as many spans as that takes, up to kMaxDecodeSplits)
+  int span_tiles;
   // spans launched per (row, KV group): at least the most any row of the
   // round uses (decode_spans_used); 0 launches kMaxDecodeSplits
   int span_grid;
+  // 1 when every ring row before a row's position was complete before the
+  // launch's stream predecessor started (the engine synchronises its stream
+  // before each round): the kernel then fetches its first key tile while
+  // that predecessor still runs
+  int ring_settled;
   float eps;
   void* out_split;   // [rows][heads * 128] split records
   float* out_f32;    // optional [rows][heads * 128]
@@ -57,8 +65,22 @@ cudaError_t launch_decode_attention(const DecodeAttentionParams& p, int rows,
                                     cudaStream_t stream, bool pdl);
 
 size_t decode_attention_partial_floats(int heads);
-// Key spans the decode attention kernel uses for a row at `position`.
-int decode_spans_used(int position, int window, int max_splits);
+// Key tiles per span of a row with `tiles` key tiles.
+__host__ __device__ inline int decode_span_tiles(int tiles, int max_splits,
+                                                 int span_tiles) {
+  const int fit = (tiles + kMaxDecodeSplits - 1) / kMaxDecodeSplits;
+  if (span_tiles > 0)
+    return span_tiles > fit ? span_tiles : fit;
+  const int splits = max_splits < 1                  ? 1
+                     : max_splits > kMaxDecodeSplits ? kMaxDecodeSplits
+                                                     : max_splits;
+  return (tiles + splits - 1) / splits;
+}
+// Key tiles of a row at `position` and the spans the decode attention kernel
+// uses for it.
+int decode_key_tiles(int position, int window);
+int decode_spans_used(int position, int window, int max_splits,
+                      int span_tiles);
 
 // ---- prompt pass ------------------------------------------------------------
 

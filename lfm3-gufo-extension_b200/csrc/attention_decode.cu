@@ -43,6 +43,7 @@ struct DecodeSmem {
   float tile_max[kWarps][8];
   float l[kWarps][8];  // running denominators of each warp's keys
   float m[8], lsum[8];
+  alignas(16) __half newk[kHeadDim], newv[kHeadDim];  // the row at `position`
   int last;
 };
 // After the key loop the K tile holds the output and the merge weights.
@@ -68,12 +69,43 @@ __device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
                : "r"(smem_addr(p)));
 }
 
-// RMSNorm (weight w) and RoPE of one 128-wide head held as pairs
-// (i, i + 64) for i in {lane, lane + 32}; returns the rotated pairs.
+// A lane's share of one 128-wide head: pairs (i, i + 64) for
+// i in {lane, lane + 32}. The norm weights and the rotation of the row's
+// position are constants of the launch, read before the dependency wait.
+struct LaneNorm {
+  float a[2], b[2];  // w[i], w[i + 64]
+};
+struct LaneRotation {
+  float cs[2], sn[2];
+};
+__device__ __forceinline__ LaneNorm lane_norm(const float* w, int lane) {
+  LaneNorm n;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    n.a[j] = w[lane + 32 * j];
+    n.b[j] = w[lane + 32 * j + 64];
+  }
+  return n;
+}
+__device__ __forceinline__ LaneRotation lane_rotation(const float* freq,
+                                                      const float* factors,
+                                                      int position, int lane) {
+  LaneRotation t;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = lane + 32 * j;
+    float angle = float(position) * freq[i];
+    if (factors)
+      angle /= factors[i];
+    sincosf(angle, &t.sn[j], &t.cs[j]);
+  }
+  return t;
+}
+// RMSNorm and RoPE of the head held as the lane's pairs; returns the
+// rotated pairs.
 __device__ __forceinline__ void norm_rope(float (&x0)[2], float (&x1)[2],
-                                          const float* w, const float* freq,
-                                          const float* factors, int position,
-                                          float eps, int lane) {
+                                          const LaneNorm& w,
+                                          const LaneRotation& t, float eps) {
   float squares = 0;
 #pragma unroll
   for (int j = 0; j < 2; ++j)
@@ -81,15 +113,9 @@ __device__ __forceinline__ void norm_rope(float (&x0)[2], float (&x1)[2],
   const float inv = 1.0F / sqrtf(warp_sum(squares) / 128.0F + eps);
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
-    const int i = lane + 32 * j;
-    const float a = (x0[j] * inv) * w[i], b = (x1[j] * inv) * w[i + 64];
-    float angle = float(position) * freq[i];
-    if (factors)
-      angle /= factors[i];
-    float sn, cs;
-    sincosf(angle, &sn, &cs);
-    x0[j] = a * cs - b * sn;
-    x1[j] = b * cs + a * sn;
+    const float a = (x0[j] * inv) * w.a[j], b = (x1[j] * inv) * w.b[j];
+    x0[j] = a * t.cs[j] - b * t.sn[j];
+    x1[j] = b * t.cs[j] + a * t.sn[j];
   }
 }
 
@@ -100,8 +126,9 @@ __global__ void __launch_bounds__(kThreads, 4)
   __shared__ DecodeSmem s;
   const int g = blockIdx.x, split = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  grid_dependency_wait();
-  allow_dependents();
+  // ---- before the dependency wait: the row table (written before the
+  // round), the launch's constants and, with settled rings, the first key
+  // tile
   const bool op = p.rows == nullptr;
   const int position = op ? p.position : p.rows->position[r];
   const LayerState state =
@@ -111,14 +138,60 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int capacity = state.capacity;
   const int first = p.window > 0 ? max(0, position + 1 - p.window) : 0;
   const int tiles = (position + 1 - first + kDecodeTile - 1) / kDecodeTile;
-  const int max_splits = max(1, min(p.max_splits, kMaxDecodeSplits));
-  const int per = (tiles + max_splits - 1) / max_splits;
+  const int per = decode_span_tiles(tiles, p.max_splits, p.span_tiles);
   const int used = (tiles + per - 1) / per;  // decode_spans_used
   if (split >= used)
     return;
   const int begin = first + split * per * kDecodeTile;
   const int end = min(begin + per * kDecodeTile, position + 1);
   const size_t stride = size_t(p.kv_heads) * kHeadDim;
+  // this CTA writes the row at `position` (and uses it from shared memory)
+  const bool stores_row = !op && split == used - 1;
+  LaneNorm qn{}, kn{};
+  LaneRotation rot{};
+  if (!op) {
+    qn = lane_norm(p.q_norm, lane);
+    kn = lane_norm(p.k_norm, lane);
+    rot = lane_rotation(p.freq, p.factors, position, lane);
+  }
+
+  // ---- K and V rows of a tile (16-byte pieces, L1 bypassed), loaded into
+  // registers one tile ahead
+  constexpr int kPieces = kDecodeTile * 16 / kThreads;
+  uint4 kr[kPieces], vr[kPieces];
+  const auto load_tile = [&](int base) {
+    const int n = min(kDecodeTile, end - base);
+    const int slot0 = base % capacity;  // ring slot of key `base`
+#pragma unroll
+    for (int j = 0; j < kPieces; ++j) {
+      const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
+      kr[j] = make_uint4(0, 0, 0, 0);
+      vr[j] = kr[j];
+      if (key < n) {
+        const int t = base + key;
+        const __half *ks = state.k, *vs = state.v;
+        int slot = slot0 + key;
+        if (slot >= capacity)
+          slot = capacity >= kDecodeTile ? slot - capacity : slot % capacity;
+        size_t row = size_t(slot) * stride;
+        if (op && t >= position) {
+          ks = p.chunk_k;
+          vs = p.chunk_v;
+          row = size_t(t - position) * stride;
+        }
+        row += size_t(g) * kHeadDim;
+        kr[j] = __ldcg(reinterpret_cast<const uint4*>(ks + row) + piece);
+        vr[j] = __ldcg(reinterpret_cast<const uint4*>(vs + row) + piece);
+      }
+    }
+  };
+  const bool early = !op && p.ring_settled;
+  if (early)
+    load_tile(begin);
+  grid_dependency_wait();
+  allow_dependents();
+  if (!early)
+    load_tile(begin);
 
   // ---- query heads of this group (normalised, rotated), as hi + lo fp16
   // terms; heads G..7 are zero
@@ -130,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 4)
       x0[0] = qr[lane], x0[1] = qr[lane + 32];
       x1[0] = qr[lane + 64], x1[1] = qr[lane + 96];
       if (!op)
-        norm_rope(x0, x1, p.q_norm, p.freq, p.factors, position, p.eps, lane);
+        norm_rope(x0, x1, qn, rot, p.eps);
     }
     const float e[4] = {x0[0], x0[1], x1[0], x1[1]};
 #pragma unroll
@@ -142,21 +215,27 @@ __global__ void __launch_bounds__(kThreads, 4)
     }
   }
   // ---- the new K/V row goes to its ring slot (span holding `position`)
-  if (!op && split == used - 1 && warp == 0) {
-    const float* kr = p.k + size_t(r) * p.ldk + size_t(g) * kHeadDim;
-    const float* vr = p.v + size_t(r) * p.ldk + size_t(g) * kHeadDim;
-    float x0[2] = {kr[lane], kr[lane + 32]};
-    float x1[2] = {kr[lane + 64], kr[lane + 96]};
-    norm_rope(x0, x1, p.k_norm, p.freq, p.factors, position, p.eps, lane);
+  if (stores_row && warp == 0) {
+    const float* kx = p.k + size_t(r) * p.ldk + size_t(g) * kHeadDim;
+    const float* vx = p.v + size_t(r) * p.ldk + size_t(g) * kHeadDim;
+    float x0[2] = {kx[lane], kx[lane + 32]};
+    float x1[2] = {kx[lane + 64], kx[lane + 96]};
+    norm_rope(x0, x1, kn, rot, p.eps);
     const size_t slot = size_t(position % capacity) * stride +
                         size_t(g) * kHeadDim;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int i = lane + 32 * j;
-      state.k[slot + i] = __float2half_rn(x0[j]);
-      state.k[slot + i + 64] = __float2half_rn(x1[j]);
-      state.v[slot + i] = __float2half_rn(vr[i]);
-      state.v[slot + i + 64] = __float2half_rn(vr[i + 64]);
+      const __half k0 = __float2half_rn(x0[j]), k1 = __float2half_rn(x1[j]);
+      const __half v0 = __float2half_rn(vx[i]), v1 = __float2half_rn(vx[i + 64]);
+      state.k[slot + i] = k0;
+      state.k[slot + i + 64] = k1;
+      state.v[slot + i] = v0;
+      state.v[slot + i + 64] = v1;
+      s.newk[i] = k0;
+      s.newk[i + 64] = k1;
+      s.newv[i] = v0;
+      s.newv[i + 64] = v1;
     }
   }
   if (tid < kWarps * 8)
@@ -172,41 +251,19 @@ __global__ void __launch_bounds__(kThreads, 4)
   float mrun[2] = {-INFINITY, -INFINITY};
   float o[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 
-  // ---- K and V rows of a tile (16-byte pieces, L1 bypassed: the current
-  // row was just written by this CTA), loaded into registers one tile ahead
-  constexpr int kPieces = kDecodeTile * 16 / kThreads;
-  uint4 kr[kPieces], vr[kPieces];
-  const auto load_tile = [&](int base) {
-    const int n = min(kDecodeTile, end - base);
-#pragma unroll
-    for (int j = 0; j < kPieces; ++j) {
-      const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-      kr[j] = make_uint4(0, 0, 0, 0);
-      vr[j] = kr[j];
-      if (key < n) {
-        const int t = base + key;
-        const __half *ks = state.k, *vs = state.v;
-        size_t row = size_t(t % capacity) * stride;
-        if (op && t >= position) {
-          ks = p.chunk_k;
-          vs = p.chunk_v;
-          row = size_t(t - position) * stride;
-        }
-        row += size_t(g) * kHeadDim;
-        kr[j] = __ldcg(reinterpret_cast<const uint4*>(ks + row) + piece);
-        vr[j] = __ldcg(reinterpret_cast<const uint4*>(vs + row) + piece);
-      }
-    }
-  };
-  if (begin < end)
-    load_tile(begin);
   for (int base = begin; base < end; base += kDecodeTile) {
     const int n = min(kDecodeTile, end - base);
 #pragma unroll
     for (int j = 0; j < kPieces; ++j) {
       const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-      *reinterpret_cast<uint4*>(&s.k[at128(key, piece)]) = kr[j];
-      *reinterpret_cast<uint4*>(&s.v[at128(key, piece)]) = vr[j];
+      uint4 kv = kr[j], vv = vr[j];
+      if (stores_row && base + key == position) {
+        // the ring slot may have been read before this CTA wrote it
+        kv = *reinterpret_cast<const uint4*>(&s.newk[piece * 8]);
+        vv = *reinterpret_cast<const uint4*>(&s.newv[piece * 8]);
+      }
+      *reinterpret_cast<uint4*>(&s.k[at128(key, piece)]) = kv;
+      *reinterpret_cast<uint4*>(&s.v[at128(key, piece)]) = vv;
     }
     __syncthreads();
     if (base + kDecodeTile < end)
@@ -399,16 +456,28 @@ __global__ void __launch_bounds__(kThreads, 4)
     s.lsum[tid] = sum;
   }
   __syncthreads();
+  // the spans' values in chunks whose loads are all in flight at once,
+  // accumulated in span order
+  constexpr int kChunk = 32 / G;
   float value[G];
 #pragma unroll
   for (int h = 0; h < G; ++h)
     value[h] = 0;
-#pragma unroll 2
-  for (int sp = 0; sp < used; ++sp)
+  for (int sp0 = 0; sp0 < used; sp0 += kChunk) {
+    float x[kChunk][G];
 #pragma unroll
-    for (int h = 0; h < G; ++h)
-      value[h] = fmaf(__ldcg(part(sp, g * G + h) + 2 + d), mw[sp * 8 + h],
-                      value[h]);
+    for (int j = 0; j < kChunk; ++j)
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        x[j][h] = sp0 + j < used ? __ldcg(part(sp0 + j, g * G + h) + 2 + d)
+                                 : 0.0F;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j)
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        if (sp0 + j < used)
+          value[h] = fmaf(x[j][h], mw[(sp0 + j) * 8 + h], value[h]);
+  }
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     const int head = g * G + h;
@@ -442,11 +511,15 @@ cudaError_t launch_group(const DecodeAttentionParams& p, int rows,
 
 }  // namespace
 
-int decode_spans_used(int position, int window, int max_splits) {
+int decode_key_tiles(int position, int window) {
   const int first = window > 0 ? max(0, position + 1 - window) : 0;
-  const int tiles = (position + 1 - first + kDecodeTile - 1) / kDecodeTile;
-  const int splits = max(1, min(max_splits, kMaxDecodeSplits));
-  const int per = (tiles + splits - 1) / splits;
+  return (position + 1 - first + kDecodeTile - 1) / kDecodeTile;
+}
+
+int decode_spans_used(int position, int window, int max_splits,
+                      int span_tiles) {
+  const int tiles = decode_key_tiles(position, window);
+  const int per = decode_span_tiles(tiles, max_splits, span_tiles);
   return (tiles + per - 1) / per;
 }
 

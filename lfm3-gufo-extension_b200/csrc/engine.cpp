@@ -480,12 +480,22 @@ void Session::DecodeRound(std::span<Session* const> batch,
       ap.heads = c.heads;
       ap.kv_heads = int(c.kv_heads[i]);
       ap.window = swa ? int(c.window) : 0;
-      // about two CTAs per SM over the round's (row, group) pairs
-      ap.max_splits = std::max(1, 4 * model_->sms() / (B * int(c.kv_heads[i])));
+      // spans of about equal length over the round's rows, about four CTAs
+      // (one wave) per SM
+      {
+        long key_tiles = 0;
+        for (int r = 0; r < B; ++r)
+          key_tiles += decode_key_tiles(rows.position[r], ap.window);
+        const long slots = 4L * model_->sms();
+        ap.span_tiles = int(std::max(
+            1L, (key_tiles * ap.kv_heads + slots - 1) / slots));
+      }
       for (int r = 0; r < B; ++r)
         ap.span_grid = std::max(
-            ap.span_grid,
-            decode_spans_used(rows.position[r], ap.window, ap.max_splits));
+            ap.span_grid, decode_spans_used(rows.position[r], ap.window,
+                                            ap.max_splits, ap.span_tiles));
+      // the stream was synchronised at the start of the round
+      ap.ring_settled = 1;
       ap.eps = c.eps;
       ap.out_split = a_split_.data();
       ap.partials = attn_partials_.as<float>();
