@@ -134,9 +134,33 @@ __device__ __forceinline__ void run_block(const uint8_t* block, int pitch,
   }
 }
 
+// Conv epilogue inputs of one (channel, token) read ahead of the step: the
+// session's history window and the channel's taps.
+constexpr int kConvAhead = 8;  // widths up to 8 are read ahead
+struct ConvAhead {
+  float hist[kConvAhead - 1], w[kConvAhead];
+  bool ok;  // read for tile `blockIdx.x`
+};
+__device__ __forceinline__ ConvAhead conv_ahead(const GemvParams& p, int tid) {
+  ConvAhead a;
+  const int i = tid / kMaxBatch, tok = tid % kMaxBatch;
+  const int ch = blockIdx.x * 16 + i, L = p.L;
+  a.ok = i < 16 && tok < p.tokens && ch < p.H && L <= kConvAhead;
+  if (a.ok) {
+    const float* own = p.rows->layers[tok][p.layer].conv + size_t(ch) * (L - 1);
+#pragma unroll
+    for (int j = 0; j < kConvAhead - 1; ++j)
+      a.hist[j] = j < L - 1 ? own[j] : 0.0F;
+#pragma unroll
+    for (int j = 0; j < kConvAhead; ++j)
+      a.w[j] = j < L ? p.conv_w[size_t(ch) * L + j] : 0.0F;
+  }
+  return a;
+}
+
 template <int kKind, int kMT>
 __device__ void gemv_epilogue(const GemvParams& p, const float* tile, int t,
-                              int tid) {
+                              int tid, const ConvAhead* ahead = nullptr) {
   if (kKind == kGemvPlain) {
     int j = 0;
 #pragma unroll
@@ -180,14 +204,26 @@ __device__ void gemv_epilogue(const GemvParams& p, const float* tile, int t,
   const float c = tile[(16 + i) * kMaxBatch + tok];
   const float x = tile[(32 + i) * kMaxBatch + tok];
   float* own = p.rows->layers[tok][p.layer].conv + size_t(ch) * (L - 1);
-  const float* w = p.conv_w + size_t(ch) * L;
   const float current = b * x;
   float sum = 0;
-  for (int j = 0; j < L - 1; ++j)
-    sum = fmaf(w[j], own[j], sum);
-  sum = fmaf(w[L - 1], current, sum);
-  for (int j = 0; j < L - 2; ++j)
-    own[j] = own[j + 1];
+  if (ahead && ahead->ok && t == int(blockIdx.x)) {
+#pragma unroll
+    for (int j = 0; j < kConvAhead - 1; ++j)
+      if (j < L - 1)
+        sum = fmaf(ahead->w[j], ahead->hist[j], sum);
+    sum = fmaf(ahead->w[L - 1], current, sum);
+#pragma unroll
+    for (int j = 0; j < kConvAhead - 2; ++j)
+      if (j < L - 2)
+        own[j] = ahead->hist[j + 1];
+  } else {
+    const float* w = p.conv_w + size_t(ch) * L;
+    for (int j = 0; j < L - 1; ++j)
+      sum = fmaf(w[j], own[j], sum);
+    sum = fmaf(w[L - 1], current, sum);
+    for (int j = 0; j < L - 2; ++j)
+      own[j] = own[j + 1];
+  }
   own[L - 2] = current;
   store_split(p.split_out, tok, p.split_width, ch, sum * c);
 }
@@ -225,6 +261,11 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
   }
 
   // ---- consumers
+  // the conv step's history and taps of the first tile: written only by
+  // this layer's step of an earlier round, so read before the wait
+  ConvAhead ahead{};
+  if (kKind == kGemvConv)
+    ahead = conv_ahead(p, tid);
   grid_dependency_wait();
   const int g = lane / 4, cq = lane % 4;
   const uint4* x = static_cast<const uint4*>(p.x);
@@ -306,7 +347,7 @@ __device__ void gemv_body(const GemvParams& p, GemvSmem& s) {
       s.tile[e] = v;
     }
     named_barrier(1, kGemvWarps * 32);
-    gemv_epilogue<kKind, kMT>(p, s.tile, t, tid);
+    gemv_epilogue<kKind, kMT>(p, s.tile, t, tid, &ahead);
   }
 }
 
