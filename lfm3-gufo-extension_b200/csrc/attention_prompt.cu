@@ -20,7 +20,7 @@ namespace {
 
 constexpr int kQ = 16;       // queries per CTA
 constexpr int kKeys = 64;    // keys per tile
-constexpr int kMinSpan = 2048, kMaxSpans = 8;
+constexpr int kMinSpan = 1024, kMaxSpans = 8;
 
 // ---- prompt heads ----------------------------------------------------------
 // Block = one head of one row, 64 threads (one RoPE pair each).
@@ -225,20 +225,31 @@ __global__ void __launch_bounds__(G * 32)
           mma_f16(sc[2 * jp + 1], qa[ks], b[2], b[3]);
         }
       }
-      // mask, online softmax (base 2)
+      // mask (only tiles that reach past a bound), online softmax (base 2)
       float top[2] = {-INFINITY, -INFINITY};
+      const bool inside = base + kKeys - 1 <= last_key &&
+                          base + kKeys - 1 <= P + q0 && base >= span_first &&
+                          (a.window <= 0 || base > P + q0 + nq - 1 - a.window);
+      if (inside) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = base + j * 8 + 2 * cq + (e & 1);
-          const int qp = qpos[e >> 1];
-          const bool ok = t <= last_key && t <= qp &&
-                          (a.window <= 0 || t > qp - a.window) &&
-                          t >= span_first;
-          sc[j][e] = ok ? sc[j][e] : -INFINITY;
-          top[e >> 1] = fmaxf(top[e >> 1], sc[j][e]);
-        }
+          for (int e = 0; e < 4; ++e)
+            top[e >> 1] = fmaxf(top[e >> 1], sc[j][e]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = base + j * 8 + 2 * cq + (e & 1);
+            const int qp = qpos[e >> 1];
+            const bool ok = t <= last_key && t <= qp &&
+                            (a.window <= 0 || t > qp - a.window) &&
+                            t >= span_first;
+            sc[j][e] = ok ? sc[j][e] : -INFINITY;
+            top[e >> 1] = fmaxf(top[e >> 1], sc[j][e]);
+          }
+      }
       float alpha[2], shift[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
