@@ -511,18 +511,19 @@ def main():
     step_bytes = decode_round_bytes(cfg, [d + args.steps // 2 for d in depths])
 
     # ---- end to end through the host API: pinned token/logit buffers
-    pinned_logits = [torch.empty(cfg.vocab, dtype=torch.float32, pin_memory=True).numpy()
-                     for _ in sessions]
+    # one pinned [sessions][vocab] block; each session's logits are a row view
+    logit_block = torch.empty((SESSIONS, cfg.vocab), dtype=torch.float32,
+                              pin_memory=True).numpy()
+    pinned_logits = [logit_block[r] for r in range(SESSIONS)]
     pinned_tokens = torch.empty(SESSIONS, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
     for r, s in enumerate(sessions):
         pinned_logits[r][:] = s.read_logits()
-    pinned_tokens[:] = [int(np.argmax(l)) for l in pinned_logits]
+    pinned_tokens[:] = logit_block.argmax(axis=1)
 
     def host_rounds(k):
         for _ in range(k):
             lfm3.Session.forward_batch(sessions, pinned_tokens, outs=pinned_logits)
-            for r in range(SESSIONS):
-                pinned_tokens[r] = int(np.argmax(pinned_logits[r]))
+            pinned_tokens[:] = logit_block.argmax(axis=1)  # greedy, on the host
 
     host_rounds(args.warmup)
     barrier()

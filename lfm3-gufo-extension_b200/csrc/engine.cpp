@@ -549,15 +549,21 @@ void Session::DecodeRound(std::span<Session* const> batch,
   if (logits)
     Timed(kDecodeProjection,
           [&] { LaunchLmHead(z, B, batch_logits_.as<float>()); });
+  // each session's frontier (and logits) rows, in one launch
+  static_assert(kMaxRowCopies >= 2 * kMaxBatch, "round-end copies");
+  RowCopies copies{};
   for (int r = 0; r < B; ++r) {
     Session* row = batch[r];
-    Check(cudaMemcpyAsync(row->frontier_.data(), z32_.as<float>() + size_t(r) * H,
-                          size_t(H) * 4, cudaMemcpyDeviceToDevice, s));
-    if (logits)
-      Check(cudaMemcpyAsync(row->logits_.data(),
-                            batch_logits_.as<float>() + size_t(r) * c.vocab,
-                            size_t(c.vocab) * 4, cudaMemcpyDeviceToDevice, s));
+    copies.src[copies.count] = z32_.as<float>() + size_t(r) * H;
+    copies.dst[copies.count] = row->frontier_.as<float>();
+    copies.floats[copies.count++] = H;
+    if (logits) {
+      copies.src[copies.count] = batch_logits_.as<float>() + size_t(r) * c.vocab;
+      copies.dst[copies.count] = row->logits_.as<float>();
+      copies.floats[copies.count++] = int(c.vocab);
+    }
   }
+  Check(launch_row_copies(copies, s, true));
 }
 
 // ---- prompt pass --------------------------------------------------------------

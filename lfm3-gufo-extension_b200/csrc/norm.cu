@@ -327,6 +327,20 @@ __global__ void __launch_bounds__(kNormThreads)
     values[size_t(row) * K + k] = __float2half_rn(ldexpf(src[k], e));
 }
 
+__global__ void __launch_bounds__(256)
+    row_copies_kernel(const __grid_constant__ RowCopies c) {
+  grid_dependency_wait();
+  allow_dependents();
+  const int i = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c.vector[i]) {
+    if (e < c.floats[i] / 4)
+      reinterpret_cast<float4*>(c.dst[i])[e] =
+          reinterpret_cast<const float4*>(c.src[i])[e];
+  } else if (e < c.floats[i]) {
+    c.dst[i][e] = c.src[i][e];
+  }
+}
+
 __global__ void split_rows_kernel(const float* __restrict__ x, void* split,
                                   int rows, int K) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // record index
@@ -416,6 +430,27 @@ cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
                                     : half_rows_kernel<8>;
   return launch_kernel(kernel, dim3(rows), dim3(kNormThreads), 0, stream, pdl,
                        x, row_max, values, scale, K);
+}
+
+cudaError_t launch_row_copies(const RowCopies& copies, cudaStream_t stream,
+                              bool pdl) {
+  if (copies.count < 0 || copies.count > kMaxRowCopies)
+    return cudaErrorInvalidValue;
+  RowCopies c = copies;
+  int most = 0;  // pieces of the longest copy
+  for (int i = 0; i < c.count; ++i) {
+    if (c.floats[i] < 0 || (c.floats[i] && (!c.src[i] || !c.dst[i])))
+      return cudaErrorInvalidValue;
+    c.vector[i] = c.floats[i] % 4 == 0 &&
+                  reinterpret_cast<uintptr_t>(c.src[i]) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(c.dst[i]) % 16 == 0;
+    const int pieces = c.vector[i] ? c.floats[i] / 4 : c.floats[i];
+    most = pieces > most ? pieces : most;
+  }
+  if (!c.count || !most)
+    return cudaSuccess;
+  return launch_kernel(row_copies_kernel, dim3((most + 255) / 256, c.count),
+                       dim3(256), 0, stream, pdl, c);
 }
 
 cudaError_t launch_split_rows(const float* x, void* split, int rows, int K,

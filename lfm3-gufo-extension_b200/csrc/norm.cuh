@@ -54,6 +54,20 @@ cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
                              cudaStream_t stream, bool pdl = false);
 
 // FP32 rows -> split records (x = hi + lo, fp16 each).
+// Up to kMaxRowCopies FP32 row copies in one launch (16-byte pieces when
+// both rows are 16-byte aligned and the length a multiple of 4): the end of
+// a decode round hands each session its frontier and logits rows.
+constexpr int kMaxRowCopies = 16;
+struct RowCopies {
+  const float* src[kMaxRowCopies];
+  float* dst[kMaxRowCopies];
+  int floats[kMaxRowCopies];
+  int vector[kMaxRowCopies];  // set by launch_row_copies
+  int count;
+};
+cudaError_t launch_row_copies(const RowCopies& c, cudaStream_t stream,
+                              bool pdl);
+
 cudaError_t launch_split_rows(const float* x, void* split, int rows, int K,
                               cudaStream_t stream);
 
