@@ -218,7 +218,9 @@ int lfm3_session_forward_batch(lfm3_session* const* sessions,
  * rows[i] (device embedding rows) must be NULL in this build (tokens[i] is
  * the input). With logits set, each session's logits are computed into its
  * device buffer (lfm3_session_continuation_data tensor 0) without a copy to
- * the host. */
+ * the host. Returns once the round is queued: work queued on a session's
+ * lfm3_session_stream runs after it, the session's reads wait for it, and a
+ * device wait that gave up is reported by the next call that waits. */
 int lfm3_session_forward_batch_inputs(lfm3_session* const* sessions,
                                       const uint32_t* tokens,
                                       const float* const* rows, size_t count,

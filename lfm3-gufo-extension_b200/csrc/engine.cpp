@@ -226,6 +226,7 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     kv_max = std::max(kv_max, c.kv_heads[i]);
   const size_t KV = size_t(kv_max) * 128;
   Throw(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  Throw(cudaEventCreateWithFlags(&round_done_, cudaEventDisableTiming));
   try {
     // recurrent state (engine.cpp:55-77)
     std::vector<LayerState> table(c.n_layers);
@@ -301,6 +302,8 @@ Session::~Session() {
   }
   for (cudaEvent_t e : events_)
     cudaEventDestroy(e);
+  if (round_done_)
+    cudaEventDestroy(round_done_);
   if (host_rows_)
     cudaFreeHost(host_rows_);
 }
@@ -399,8 +402,13 @@ void Session::DecodeRound(std::span<Session* const> batch,
     Timed(kDecodeProjection,
           [&] { Check(RunGemv(p, *model_, s)); });
   };
-  // the rows of this round
-  Check(cudaStreamSynchronize(s));  // host_rows_ is reused between rounds
+  // the rows of this round; host_rows_ is reused between rounds, and an
+  // earlier round that returned without waiting reports its device wait
+  // failures here
+  Check(cudaStreamSynchronize(s));
+  if (const unsigned e = take_device_error())
+    throw std::runtime_error("device wait gave up in an earlier round, code " +
+                             std::to_string(e));
   DecodeRows& rows = *host_rows_;
   rows.count = B;
   for (int r = 0; r < B; ++r) {
@@ -820,6 +828,16 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
           [&] { LaunchLmHead(z_split_.data(), 1, logits_.as<float>()); });
 }
 
+// Waits for everything queued for this session (its own stream also waits
+// for rounds other sessions led) and reports a device wait that gave up.
+void Session::Settle() {
+  Check(cudaStreamSynchronize(stream_));
+  if (const unsigned e = take_device_error()) {
+    poisoned_ = true;
+    throw std::runtime_error("device wait gave up, code " + std::to_string(e));
+  }
+}
+
 void Session::EnsureLogits() {
   if (logits_ready_)
     return;
@@ -941,17 +959,39 @@ bool Session::Batch(std::span<Session* const> sessions,
       if (s != front)
         front->Check(cudaStreamSynchronize(s->stream_));
     front->DecodeRound(sessions, tokens, want);
-    for (size_t r = 0; r < logits.size(); ++r)
+    // logits spans that are consecutive rows of one block take one copy of
+    // the round's logits; otherwise one copy per session
+    bool block = !logits.empty();
+    for (size_t r = 0; r < logits.size() && block; ++r)
+      block = logits[r].size() == logits[0].size() &&
+              logits[r].data() == logits[0].data() + r * logits[0].size();
+    if (block)
+      front->Check(cudaMemcpyAsync(logits[0].data(),
+                                   front->batch_logits_.data(),
+                                   logits.size() * logits[0].size_bytes(),
+                                   cudaMemcpyDeviceToHost, front->stream_));
+    for (size_t r = 0; r < logits.size() && !block; ++r)
       if (!logits[r].empty())
         front->Check(cudaMemcpyAsync(logits[r].data(),
                                      sessions[r]->logits_.data(),
                                      logits[r].size_bytes(),
                                      cudaMemcpyDeviceToHost, front->stream_));
-    front->Check(cudaStreamSynchronize(front->stream_));
-    if (const unsigned e = take_device_error())
-      throw std::runtime_error("device wait gave up, code " +
-                               std::to_string(e));
-    front->CollectProfile();
+    // ForwardBatchInputs (no host logits, no profiling) returns once the
+    // round is enqueued: every batch session's own stream waits for it on
+    // the device, and the next call that synchronises (a round, a read, a
+    // prompt pass, a reset, a snapshot) reports a device wait that gave up
+    if (logits.empty() && !front->profiling_) {
+      front->Check(cudaEventRecord(front->round_done_, front->stream_));
+      for (Session* s : sessions)
+        if (s != front)
+          front->Check(cudaStreamWaitEvent(s->stream_, front->round_done_, 0));
+    } else {
+      front->Check(cudaStreamSynchronize(front->stream_));
+      if (const unsigned e = take_device_error())
+        throw std::runtime_error("device wait gave up, code " +
+                                 std::to_string(e));
+      front->CollectProfile();
+    }
     for (size_t r = 0; r < sessions.size(); ++r) {
       sessions[r]->position_ += 1;
       sessions[r]->logits_ready_ = want;
@@ -970,7 +1010,7 @@ bool Session::ReadHidden(std::span<float> hidden, std::string* error) {
   try {
     if (hidden.size() != model_->config().hidden)
       throw std::invalid_argument("hidden must hold hidden floats");
-    Check(cudaStreamSynchronize(stream_));
+    Settle();
     Check(cudaMemcpy(hidden.data(), frontier_.data(), hidden.size_bytes(),
                      cudaMemcpyDeviceToHost));
     return true;
@@ -990,6 +1030,7 @@ bool Session::ReadLogits(std::span<float> logits, std::string* error) {
     if (!position_)
       throw std::runtime_error("no row advanced yet");
     EnsureLogits();
+    Settle();
     Check(cudaMemcpy(logits.data(), logits_.data(), logits.size_bytes(),
                      cudaMemcpyDeviceToHost));
     return true;
@@ -1140,6 +1181,8 @@ bool Session::RestoreSnapshot(std::span<const uint8_t> payload,
                               std::string* error) {
   const auto& c = model_->config();
   try {
+    // nothing queued may still write this session's state
+    Throw(cudaStreamSynchronize(stream_));
     if (payload.size() < kSnapshotHeaderBytes)
       throw std::invalid_argument("truncated LFM3 snapshot");
     const uint8_t* p = payload.data();

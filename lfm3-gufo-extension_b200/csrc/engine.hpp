@@ -106,7 +106,10 @@ public:
                            std::string* error = nullptr);
   // ForwardBatchInputs (engine.hpp:107-114) for token rows: logits, when
   // requested, stay in each session's device buffer (ContinuationData
-  // kLogits); DeviceHidden of every session is updated.
+  // kLogits); DeviceHidden of every session is updated. Returns once the
+  // round is queued (unless profiling): work a caller queues on a session's
+  // DeviceStream runs after it, the session's host reads wait for it, and a
+  // device wait that gave up is reported by the next call that waits.
   static bool ForwardBatchInputs(std::span<Session* const> sessions,
                                  std::span<const uint32_t> tokens, bool logits,
                                  std::string* error = nullptr);
@@ -157,6 +160,7 @@ private:
   void DecodeRound(std::span<Session* const> batch,
                    std::span<const uint32_t> tokens, bool logits);
   void EnsureLogits();
+  void Settle();
   static bool Batch(std::span<Session* const> sessions,
                     std::span<const uint32_t> tokens,
                     std::span<const std::span<float>> logits,
@@ -183,6 +187,8 @@ private:
   DecodeRows* host_rows_ = nullptr;  // pinned
   bool profiling_ = false;
   std::vector<cudaEvent_t> events_;
+  // end of the last round this session led without waiting for it
+  cudaEvent_t round_done_ = nullptr;
   size_t events_used_ = 0;
   struct Pending {
     int cls;
