@@ -125,7 +125,10 @@ DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
 }
 
 // ---- Model ----------------------------------------------------------------------
-Model::~Model() = default;
+Model::~Model() {
+  if (error_host_)
+    cudaFreeHost(error_host_);
+}
 
 std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
                                    std::string* error) {
@@ -176,6 +179,11 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
       freq[64 + i] =
           float(std::pow(double(c.theta_swa), double(-2.0F * i / 128)));
     }
+    Throw(cudaHostAlloc(reinterpret_cast<void**>(&m->error_host_),
+                        sizeof(unsigned), cudaHostAllocMapped));
+    *m->error_host_ = 0;
+    Throw(cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->error_device_),
+                                   m->error_host_, 0));
     m->freq_ = DeviceBuffer(sizeof(freq));
     Throw(cudaMemcpy(m->freq_.data(), freq, sizeof(freq),
                      cudaMemcpyHostToDevice));
@@ -406,9 +414,12 @@ void Session::DecodeRound(std::span<Session* const> batch,
   // earlier round that returned without waiting reports its device wait
   // failures here
   Check(cudaStreamSynchronize(s));
-  if (const unsigned e = take_device_error())
-    throw std::runtime_error("device wait gave up in an earlier round, code " +
-                             std::to_string(e));
+  if (model_->RoundErrors()) {
+    model_->ClearRoundErrors();
+    if (const unsigned e = take_device_error())
+      throw std::runtime_error(
+          "device wait gave up in an earlier round, code " + std::to_string(e));
+  }
   DecodeRows& rows = *host_rows_;
   rows.count = B;
   for (int r = 0; r < B; ++r) {
@@ -560,6 +571,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
   // each session's frontier (and logits) rows, in one launch
   static_assert(kMaxRowCopies >= 2 * kMaxBatch, "round-end copies");
   RowCopies copies{};
+  copies.error_out = model_->RoundErrorWord();
   for (int r = 0; r < B; ++r) {
     Session* row = batch[r];
     copies.src[copies.count] = z32_.as<float>() + size_t(r) * H;

@@ -65,6 +65,14 @@ public:
     return freq_.as<float>() + (sliding ? 64 : 0);
   }
   int sms() const { return sms_; }
+  // The host-mapped round error word: nonzero once a decode round ended with
+  // the device error word set (its device address goes to that round's last
+  // kernel).
+  unsigned RoundErrors() const {
+    return *static_cast<volatile unsigned*>(error_host_);
+  }
+  void ClearRoundErrors() { *static_cast<volatile unsigned*>(error_host_) = 0; }
+  unsigned* RoundErrorWord() const { return error_device_; }
   // BF16 numerical-reference matrices (else Q8_0)
   bool bf16() const { return device_.output.type == LFM3_BF16; }
   // Device bytes of the weight segments.
@@ -80,6 +88,12 @@ private:
   std::vector<DeviceBuffer> segments_;
   DeviceBuffer freq_;  // [2][64]: global then sliding theta
   int sms_ = 148;
+  // Host-mapped copy of the device error word, written by the last kernel
+  // of every decode round, so a round can check its predecessors without a
+  // device-to-host copy (host and device addresses of one pinned word)
+  unsigned* error_host_ = nullptr;
+  unsigned* error_device_ = nullptr;
+
   size_t weight_bytes_ = 0;
   std::mutex maps_mutex_;
   std::map<std::pair<const void*, int>, CUtensorMap> maps_;

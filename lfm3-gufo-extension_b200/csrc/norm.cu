@@ -332,6 +332,8 @@ __global__ void __launch_bounds__(256)
   grid_dependency_wait();
   allow_dependents();
   const int i = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c.error_out && i == 0 && e == 0)
+    *c.error_out = *const_cast<volatile unsigned*>(&g_device_error);
   if (c.vector[i]) {
     if (e < c.floats[i] / 4)
       reinterpret_cast<float4*>(c.dst[i])[e] =
@@ -447,8 +449,13 @@ cudaError_t launch_row_copies(const RowCopies& copies, cudaStream_t stream,
     const int pieces = c.vector[i] ? c.floats[i] / 4 : c.floats[i];
     most = pieces > most ? pieces : most;
   }
-  if (!c.count || !most)
-    return cudaSuccess;
+  if (!c.count || !most) {
+    if (!c.error_out)
+      return cudaSuccess;
+    c.count = 1;  // one (empty) copy still reports the error word
+    c.floats[0] = 0;
+    most = 1;
+  }
   return launch_kernel(row_copies_kernel, dim3((most + 255) / 256, c.count),
                        dim3(256), 0, stream, pdl, c);
 }

@@ -64,6 +64,9 @@ struct RowCopies {
   int floats[kMaxRowCopies];
   int vector[kMaxRowCopies];  // set by launch_row_copies
   int count;
+  // optional: receives the device error word once every earlier kernel in
+  // the stream has finished (host-mapped memory)
+  unsigned* error_out;
 };
 cudaError_t launch_row_copies(const RowCopies& c, cudaStream_t stream,
                               bool pdl);
