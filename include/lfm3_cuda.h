@@ -43,6 +43,11 @@ const char* lfm3_last_error(void);
 /* Reads and clears the device error word set by bounded waits that gave up
  * (0: none). */
 unsigned lfm3_cuda_take_device_error(void);
+/* Diagnostic with no counterpart in the reference (its kernels do not bound
+ * their waits): one kernel whose wait nothing ends gives up after limit_us
+ * (1..1000000) and leaves code 5 in the device error word; the context stays
+ * usable. Exercises the failure path of every bounded wait. */
+int lfm3_cuda_wait_probe(unsigned limit_us, void* stream);
 
 /* ---- operators (hip/ops.hpp) -------------------------------------------- */
 

@@ -42,6 +42,7 @@ def library():
     sigs = {
         "lfm3_last_error": ([], ctypes.c_char_p),
         "lfm3_cuda_take_device_error": ([], ctypes.c_uint),
+        "lfm3_cuda_wait_probe": ([U32, P], I),
         "lfm3_cuda_dense_workspace_bytes": ([SZ, SZ], SZ),
         "lfm3_cuda_split_partial_bytes": ([], SZ),
         "lfm3_cuda_split_ticket_words": ([], SZ),

@@ -205,6 +205,14 @@ const char* lfm3_last_error(void) { return g_last_error.c_str(); }
 
 unsigned lfm3_cuda_take_device_error(void) { return lfm3::take_device_error(); }
 
+int lfm3_cuda_wait_probe(unsigned limit_us, void* stream) {
+  if (limit_us == 0 || limit_us > 1000000)
+    return lfm3::set_last_error(LFM3_ERR_INVALID,
+                                "wait probe limit must be 1..1000000 us");
+  return Cuda(lfm3::launch_wait_probe(uint64_t(limit_us) * 1000,
+                                      Stream(stream)));
+}
+
 size_t lfm3_cuda_dense_workspace_bytes(size_t rows, size_t K) {
   // FP16 prompt rows + scales, or split decode rows (4 bytes per element)
   return std::max(rows * K * 2 + rows * 4, rows * K * 4);

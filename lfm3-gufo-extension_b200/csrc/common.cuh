@@ -17,6 +17,7 @@ enum DeviceError : unsigned {
   kErrGemvEmptyWait = 2,
   kErrPrefillWait = 3,
   kErrTmemAlloc = 4,
+  kErrWaitProbe = 5,  // lfm3_cuda_wait_probe's deliberate wait
 };
 // Defined once in device_error.cu (the library is built with relocatable
 // device code).
@@ -77,16 +78,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 // Waits for the phase with this parity; false (and an error report) once
-// kWaitLimitNs have passed.
+// limit_ns (kWaitLimitNs by default) have passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          unsigned error_code) {
+                                          unsigned error_code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity))
     return true;
   const uint64_t start = global_timer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity))
       return true;
-    if (global_timer_ns() - start > kWaitLimitNs) {
+    if (global_timer_ns() - start > limit_ns) {
       report_error(error_code);
       return false;
     }

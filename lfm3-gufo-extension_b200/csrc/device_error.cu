@@ -14,6 +14,23 @@ std::atomic<unsigned long long> g_launches{0};
 void note_launch(int kernels) { g_launches += kernels; }
 unsigned long long launch_count() { return g_launches.load(); }
 
+namespace {
+// One thread waits on an mbarrier that nothing arrives at: the bounded wait
+// gives up after limit_ns and records kErrWaitProbe.
+__global__ void wait_probe_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  mbar_wait(&bar, 0, kErrWaitProbe, limit_ns);
+}
+}  // namespace
+
+cudaError_t launch_wait_probe(uint64_t limit_ns, cudaStream_t stream) {
+  note_launch();
+  wait_probe_kernel<<<1, 1, 0, stream>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 unsigned take_device_error() {
   unsigned value = 0;
   if (cudaMemcpyFromSymbol(&value, g_device_error, sizeof(value)) !=

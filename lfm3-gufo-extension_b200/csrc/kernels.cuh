@@ -16,6 +16,9 @@ cudaError_t launch_q8_gemv(const GemvParams& p, int grid, cudaStream_t stream,
 
 // Reads and clears the device error word (bounded waits that gave up).
 unsigned take_device_error();
+// One bounded wait that nothing ends, given up after limit_ns (the device
+// error word then holds kErrWaitProbe): exercises the failure path.
+cudaError_t launch_wait_probe(uint64_t limit_ns, cudaStream_t stream);
 
 // Records the message lfm3_last_error() returns on this thread; returns code.
 int set_last_error(int code, const char* message);

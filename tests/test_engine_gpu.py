@@ -174,6 +174,46 @@ def test_device_failure_poisons_until_reset(small):
     assert lfm3.library().lfm3_cuda_take_device_error() == 0
 
 
+def test_bounded_wait_gives_up_and_reports():
+    """A device wait that nothing ends gives up after its limit and records
+    its code in the device error word; the context stays usable."""
+    lib = lfm3.library()
+    lib.lfm3_cuda_take_device_error()
+    lfm3.check(lib.lfm3_cuda_wait_probe(20000, None))
+    torch.cuda.synchronize()
+    assert lib.lfm3_cuda_take_device_error() == 5
+    assert lib.lfm3_cuda_take_device_error() == 0
+    x = torch.arange(1024, device="cuda", dtype=torch.float32)
+    assert float(x.sum()) == 1023 * 1024 / 2
+
+
+def test_device_wait_failure_reported_by_next_round(small):
+    """ForwardBatchInputs returns before its round ends: a device wait that
+    gave up is reported by the next round, which fails and poisons its
+    sessions until Reset."""
+    w, model = small
+    lib = lfm3.library()
+    a, b = model.session(64), model.session(64)
+    a.forward([1, 2, 3], logits=False)
+    b.forward([4, 5], logits=False)
+    lfm3.Session.forward_batch_inputs([a, b], [6, 7])
+    torch.cuda.synchronize()  # that round ends before the failing wait runs
+    lib.lfm3_cuda_take_device_error()
+    lfm3.check(lib.lfm3_cuda_wait_probe(5000, None))
+    torch.cuda.synchronize()
+    # this round's last kernel sees the error word; the next round reports it
+    lfm3.Session.forward_batch_inputs([a, b], [8, 9])
+    with pytest.raises(lfm3.Lfm3Error):
+        lfm3.Session.forward_batch_inputs([a, b], [10, 11])
+    assert not a.coherent and not b.coherent
+    assert lib.lfm3_cuda_take_device_error() == 0
+    a.reset()
+    b.reset()
+    assert a.coherent and b.coherent
+    fresh = model.session(64)
+    np.testing.assert_array_equal(a.forward([1, 2, 3]), fresh.forward([1, 2, 3]))
+
+
 # ---- BF16 numerical-reference weights (north-star logits tolerance 2e-2) ------
 BF16_MAX_ABS = 2e-2
 
