@@ -293,7 +293,10 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
                          1) *
         4);
     Throw(cudaMallocHost(reinterpret_cast<void**>(&host_rows_),
-                         sizeof(DecodeRows)));
+                         kRowTables * sizeof(DecodeRows)));
+    for (cudaEvent_t& e : rows_copied_)
+      Throw(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    Throw(cudaEventCreateWithFlags(&ready_, cudaEventDisableTiming));
     Throw(cudaDeviceSynchronize());
   } catch (...) {
     if (host_rows_)
@@ -312,6 +315,11 @@ Session::~Session() {
     cudaEventDestroy(e);
   if (round_done_)
     cudaEventDestroy(round_done_);
+  for (cudaEvent_t e : rows_copied_)
+    if (e)
+      cudaEventDestroy(e);
+  if (ready_)
+    cudaEventDestroy(ready_);
   if (host_rows_)
     cudaFreeHost(host_rows_);
 }
@@ -410,17 +418,19 @@ void Session::DecodeRound(std::span<Session* const> batch,
     Timed(kDecodeProjection,
           [&] { Check(RunGemv(p, *model_, s)); });
   };
-  // the rows of this round; host_rows_ is reused between rounds, and an
-  // earlier round that returned without waiting reports its device wait
-  // failures here
-  Check(cudaStreamSynchronize(s));
+  // the rows of this round go through a pinned table whose previous copy is
+  // done; an earlier round that returned without waiting and has finished
+  // reports its device wait failures here
+  const int slot = rows_next_;
+  rows_next_ = (rows_next_ + 1) % kRowTables;
+  Check(cudaEventSynchronize(rows_copied_[slot]));
   if (model_->RoundErrors()) {
     model_->ClearRoundErrors();
     if (const unsigned e = take_device_error())
       throw std::runtime_error(
           "device wait gave up in an earlier round, code " + std::to_string(e));
   }
-  DecodeRows& rows = *host_rows_;
+  DecodeRows& rows = host_rows_[slot];
   rows.count = B;
   for (int r = 0; r < B; ++r) {
     rows.position[r] = int(batch[r]->position_);
@@ -430,6 +440,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
   const DecodeRows* dev_rows = rows_.as<DecodeRows>();
   Check(cudaMemcpyAsync(rows_.data(), &rows, sizeof(DecodeRows),
                         cudaMemcpyHostToDevice, s));
+  Check(cudaEventRecord(rows_copied_[slot], s));
   float* x = x_.as<float>();
   float* out = out_.as<float>();
   void* z = z_split_.data();
@@ -440,7 +451,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
                                 offsetof(DecodeRows, token)),
                             x, static_cast<const float*>(w.layers[0].norm.data),
                             NormOut{nullptr, z, nullptr, nullptr}, B, H, c.eps,
-                            s, true));
+                            s, /*pdl=*/false));  // after all earlier work
   });
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     const auto& l = w.layers[i];
@@ -513,7 +524,8 @@ void Session::DecodeRound(std::span<Session* const> batch,
         ap.span_grid = std::max(
             ap.span_grid, decode_spans_used(rows.position[r], ap.window,
                                             ap.max_splits, ap.span_tiles));
-      // the stream was synchronised at the start of the round
+      // the round's first kernel starts only after every earlier kernel of
+      // the front stream and of the batch sessions' streams
       ap.ring_settled = 1;
       ap.eps = c.eps;
       ap.out_split = a_split_.data();
@@ -966,10 +978,12 @@ bool Session::Batch(std::span<Session* const> sessions,
     want = want || !l.empty();
   try {
     // all sessions' earlier work must be done before the front stream
-    // touches their state
+    // touches their state: the front stream waits for it on the device
     for (Session* s : sessions)
-      if (s != front)
-        front->Check(cudaStreamSynchronize(s->stream_));
+      if (s != front) {
+        front->Check(cudaEventRecord(s->ready_, s->stream_));
+        front->Check(cudaStreamWaitEvent(front->stream_, s->ready_, 0));
+      }
     front->DecodeRound(sessions, tokens, want);
     // logits spans that are consecutive rows of one block take one copy of
     // the round's logits; otherwise one copy per session

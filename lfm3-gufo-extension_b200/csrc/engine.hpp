@@ -198,7 +198,14 @@ private:
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
       attn_tickets_, prompt_scratch_, split_partial_, zf_;
-  DecodeRows* host_rows_ = nullptr;  // pinned
+  // the rows of the rounds this session leads: kRowTables pinned tables in
+  // turn, each reused once its copy to the device is done
+  static constexpr int kRowTables = 4;
+  DecodeRows* host_rows_ = nullptr;
+  cudaEvent_t rows_copied_[kRowTables] = {};
+  int rows_next_ = 0;
+  // this session's queued work, waited for by a round another session leads
+  cudaEvent_t ready_ = nullptr;
   bool profiling_ = false;
   std::vector<cudaEvent_t> events_;
   // end of the last round this session led without waiting for it

@@ -201,8 +201,10 @@ def test_device_wait_failure_reported_by_next_round(small):
     lib.lfm3_cuda_take_device_error()
     lfm3.check(lib.lfm3_cuda_wait_probe(5000, None))
     torch.cuda.synchronize()
-    # this round's last kernel sees the error word; the next round reports it
+    # this round's last kernel sees the error word; once it has finished, the
+    # next round reports it
     lfm3.Session.forward_batch_inputs([a, b], [8, 9])
+    torch.cuda.synchronize()
     with pytest.raises(lfm3.Lfm3Error):
         lfm3.Session.forward_batch_inputs([a, b], [10, 11])
     assert not a.coherent and not b.coherent
