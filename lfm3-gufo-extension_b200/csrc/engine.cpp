@@ -905,11 +905,15 @@ bool Session::Forward(std::span<const uint32_t> tokens, std::span<float> logits,
       } else {
         Prompt(chunk, last && !logits.empty());
       }
-      Check(cudaStreamSynchronize(stream_));
-      if (const unsigned e = take_device_error())
-        throw std::runtime_error("device wait gave up, code " +
-                                 std::to_string(e));
-      CollectProfile();
+      // the chunks queue back to back; the last one (every one when
+      // profiling) is waited for and its device waits checked
+      if (last || profiling_) {
+        Check(cudaStreamSynchronize(stream_));
+        if (const unsigned e = take_device_error())
+          throw std::runtime_error("device wait gave up, code " +
+                                   std::to_string(e));
+        CollectProfile();
+      }
       position_ += uint32_t(chunk.size());
     }
     logits_ready_ = !logits.empty();
