@@ -194,28 +194,44 @@ class ClockSampler:
             handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
         return pynvml, handle
 
-    def _poll(self):
+    def _sample(self):
         nv, h = self.nvml
-        self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
         reasons_of = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
             nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        while not self.stop.is_set():
-            self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
-            bits = reasons_of(h)
-            for name, bit in self.REASONS.items():
-                if bits & bit:
-                    self.reasons.add(name)
-            self.stop.wait(0.005)
+        self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+        bits = reasons_of(h)
+        for name, bit in self.REASONS.items():
+            if bits & bit:
+                self.reasons.add(name)
+
+    def _poll(self):
+        while not self.stop.wait(0.005):
+            self._sample()
+
+    def _query(self):
+        # one nvidia-smi reading (short timed regions end between its -lms ticks)
+        try:
+            out = subprocess.run(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index)], capture_output=True, text=True, timeout=10).stdout
+            self.lines += [l.strip() for l in out.splitlines() if l.strip()]
+        except (OSError, subprocess.SubprocessError):
+            pass
 
     def __enter__(self):
+        # a reading at each end of the region, and the poller in between
         try:
             self.nvml = self._nvml_handle()
+            nv, h = self.nvml
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._sample()
             self.stop = threading.Event()
             self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
             return self
         except Exception:
             self.nvml = None
+        self._query()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -235,7 +251,12 @@ class ClockSampler:
         if self.nvml:
             self.stop.set()
             self.thread.join(5)
+            try:
+                self._sample()
+            except Exception:
+                pass
             return
+        self._query()
         if self.proc:
             self.proc.terminate()
             try:
