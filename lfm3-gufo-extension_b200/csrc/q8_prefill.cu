@@ -534,11 +534,15 @@ __global__ void __launch_bounds__(256)
   const float sc = p.scale[tok];
   const int row = (rt - p.first_tile[j]) * kRows + 4 * q;
   float* out = p.out[j] + size_t(tok) * p.ld[j];
-  const float v[4] = {sum.x, sum.y, sum.z, sum.w};
+  const float v[4] = {sum.x * sc, sum.y * sc, sum.z * sc, sum.w * sc};
+  if (row + 4 <= p.rows[j] && reinterpret_cast<uintptr_t>(out + row) % 16 == 0) {
+    *reinterpret_cast<float4*>(out + row) = make_float4(v[0], v[1], v[2], v[3]);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     if (row + i < p.rows[j])
-      out[row + i] = v[i] * sc;
+      out[row + i] = v[i];
 }
 
 }  // namespace
