@@ -175,6 +175,8 @@ class Model:
     def __init__(self, weights):
         lib = library()
         self._weights = weights  # the host copy must outlive nothing here
+        # bound now: at interpreter exit the module's globals may be gone
+        self._free = lib.lfm3_model_free
         self.handle = lib.lfm3_model_load(ctypes.byref(weights))
         if not self.handle:
             raise Lfm3Error(-1, lib.lfm3_last_error().decode())
@@ -189,8 +191,8 @@ class Model:
         return Session(self, context)
 
     def close(self):
-        if self.handle:
-            library().lfm3_model_free(self.handle)
+        if getattr(self, "handle", None):
+            self._free(self.handle)
             self.handle = None
 
     def __del__(self):
@@ -208,6 +210,7 @@ class Session:
         self.model = model
         self.vocab = model.config.vocab
         self.hidden = model.config.hidden
+        self._free = lib.lfm3_session_free  # see Model.__init__
         self.handle = lib.lfm3_session_create(model.handle, context)
         if not self.handle:
             raise Lfm3Error(-1, lib.lfm3_last_error().decode())
@@ -306,8 +309,8 @@ class Session:
         check(library().lfm3_session_inject_failure(self.handle, after_calls))
 
     def close(self):
-        if self.handle:
-            library().lfm3_session_free(self.handle)
+        if getattr(self, "handle", None):
+            self._free(self.handle)
             self.handle = None
 
     def __del__(self):
