@@ -53,8 +53,10 @@ int lfm3_cuda_wait_probe(unsigned limit_us, void* stream);
 
 /* DenseWorkspace (hip/ops.hpp:21-26): quantized holds FP16 prompt
  * activations or split decode activations, row_max one word per row,
- * partial and tickets (zeroed once, kept zero between calls) the split-K
- * fix-up of the decode projections. */
+ * partial the FP32 split-K partial sums of prompt projections with few
+ * tiles (added in split order by a reduce pass). tickets keeps the
+ * reference's layout; this build's split-K needs no tickets and leaves it
+ * untouched. */
 typedef struct lfm3_dense_workspace {
   void* quantized;
   unsigned* row_max;
