@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="no timing: a fixed launch sequence for ncu captures "
                          "(see profile_sequence)")
+    ap.add_argument("--profile-workload", action="store_true",
+                    help="no timing: the bench's own sessions, then decode rounds "
+                         "for ncu captures (see profile_workload)")
     return ap.parse_args()
 
 
@@ -444,6 +447,28 @@ def profile_sequence():
                       "prompt": PROFILE_PROMPT, "warm_rounds": PROFILE_WARM_ROUNDS}))
 
 
+def profile_workload(prompt_max):
+    """A fixed, untimed launch sequence over the bench's own rank-0 workload for
+    ncu: the 8 sessions' prompts U[64, prompt_max] (seed 1) prefilled, then
+    PROFILE_WARM_ROUNDS + 1 decode rounds of the 8 rows. Before the last round
+    the sequence has launched PROFILE_WARM_ROUNDS x 11 decode_attention_kernel
+    launches (the prompts' passes use the prompt attention kernel)."""
+    import torch
+    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
+    weights = lfm3.SyntheticWeights(seed=0)
+    cfg = weights.config
+    model = lfm3.Model(weights.weights)
+    lengths, prompts = rank_workload(0, prompt_max, cfg.vocab)
+    sessions = [model.session(int(n) + PROFILE_WARM_ROUNDS + 2) for n in lengths]
+    for s, p in zip(sessions, prompts):
+        s.forward(p, logits=False)
+    tokens = [int(t) for t in np.random.default_rng([2, 0]).integers(0, cfg.vocab, SESSIONS)]
+    for _ in range(PROFILE_WARM_ROUNDS + 1):
+        lfm3.Session.forward_batch_inputs(sessions, tokens, logits=True)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_workload": "done", "depths": [s.position for s in sessions]}))
+
+
 # ---- our arm ---------------------------------------------------------------------------------
 def main():
     args = parse()
@@ -452,6 +477,9 @@ def main():
         return
     if args.profile:
         profile_sequence()
+        return
+    if args.profile_workload:
+        profile_workload(args.prompt_max)
         return
     import torch
 
