@@ -35,9 +35,9 @@ struct DecodeAttentionParams {
   // round uses (decode_spans_used); 0 launches kMaxDecodeSplits
   int span_grid;
   // 1 when every ring row before a row's position was complete before the
-  // launch's stream predecessor started (the engine synchronises its stream
-  // before each round): the kernel then fetches its first key tile while
-  // that predecessor still runs
+  // launch's stream predecessor started (the engine launches a round's first
+  // kernel only after all earlier work of the batch's streams): the kernel
+  // then fetches its first key tile while that predecessor still runs
   int ring_settled;
   float eps;
   void* out_split;   // [rows][heads * 128] split records

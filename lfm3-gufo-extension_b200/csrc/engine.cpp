@@ -1008,8 +1008,10 @@ bool Session::Batch(std::span<Session* const> sessions,
                                      cudaMemcpyDeviceToHost, front->stream_));
     // ForwardBatchInputs (no host logits, no profiling) returns once the
     // round is enqueued: every batch session's own stream waits for it on
-    // the device, and the next call that synchronises (a round, a read, a
-    // prompt pass, a reset, a snapshot) reports a device wait that gave up
+    // the device; a device wait that gave up is reported by a host read,
+    // prompt pass, reset or snapshot of these sessions (they synchronise
+    // first), or by a round that starts after this one has finished (the
+    // host-mapped error word its last kernel writes)
     if (logits.empty() && !front->profiling_) {
       front->Check(cudaEventRecord(front->round_done_, front->stream_));
       for (Session* s : sessions)
