@@ -35,9 +35,11 @@ __device__ __forceinline__ int at64(int row, int piece) {  // 64-wide rows
   return row * kDecodeTile + ((piece ^ (row & 7)) << 3);
 }
 
+// Two key tiles in flight: K and V of tile t in buffer t % 2.
+constexpr int kTileBufs = 2;
 struct DecodeSmem {
-  alignas(16) __half k[kDecodeTile * kHeadDim];  // [key][dim]
-  alignas(16) __half v[kDecodeTile * kHeadDim];  // [key][dim]
+  alignas(16) __half k[kTileBufs][kDecodeTile * kHeadDim];  // [key][dim]
+  alignas(16) __half v[kTileBufs][kDecodeTile * kHeadDim];  // [key][dim]
   alignas(16) __half qh[8 * kHeadDim], ql[8 * kHeadDim];      // [head][dim]
   alignas(16) __half ph[8 * kDecodeTile], pl[8 * kDecodeTile];  // [head][key]
   float tile_max[kWarps][8];
@@ -46,10 +48,27 @@ struct DecodeSmem {
   alignas(16) __half newk[kHeadDim], newv[kHeadDim];  // the row at `position`
   int last;
 };
-// After the key loop the K tile holds the output and the merge weights.
+// After the key loop the first K tile holds the output and the merge
+// weights.
 static_assert(sizeof(float) * (8 * kHeadDim + 2 * 8 * kMaxDecodeSplits) <=
                   sizeof(__half) * kDecodeTile * kHeadDim,
               "output staging fits the K tile");
+
+// 16 bytes global -> shared, zero-filled when !valid (cp.async, L1 bypassed)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src,
+                                           bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// every group but the newest has landed (this thread's copies)
+__device__ __forceinline__ void cp_async_wait_older() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
   asm volatile(
@@ -121,9 +140,10 @@ __device__ __forceinline__ void norm_rope(float (&x0)[2], float (&x1)[2],
 
 // Four CTAs per SM (128 registers): a round's spans run in one wave.
 template <int G>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, 3)
     decode_attention_kernel(const __grid_constant__ DecodeAttentionParams p) {
-  __shared__ DecodeSmem s;
+  extern __shared__ __align__(128) uint8_t decode_smem_raw[];
+  DecodeSmem& s = *reinterpret_cast<DecodeSmem*>(decode_smem_raw);
   const int g = blockIdx.x, split = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   // ---- before the dependency wait: the row table (written before the
@@ -155,22 +175,22 @@ __global__ void __launch_bounds__(kThreads, 4)
     rot = lane_rotation(p.freq, p.factors, position, lane);
   }
 
-  // ---- K and V rows of a tile (16-byte pieces, L1 bypassed), loaded into
-  // registers one tile ahead
+  // ---- K and V rows of a tile (16-byte pieces) copied into buffer
+  // (tile % kTileBufs), one cp.async group per tile (empty past the span)
   constexpr int kPieces = kDecodeTile * 16 / kThreads;
-  uint4 kr[kPieces], vr[kPieces];
-  const auto load_tile = [&](int base) {
-    const int n = min(kDecodeTile, end - base);
-    const int slot0 = base % capacity;  // ring slot of key `base`
+  const auto issue_tile = [&](int tile) {
+    const int base = begin + tile * kDecodeTile;
+    if (base < end) {
+      const int n = min(kDecodeTile, end - base);
+      const int slot0 = base % capacity;  // ring slot of key `base`
+      __half* sk = s.k[tile % kTileBufs];
+      __half* sv = s.v[tile % kTileBufs];
 #pragma unroll
-    for (int j = 0; j < kPieces; ++j) {
-      const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-      kr[j] = make_uint4(0, 0, 0, 0);
-      vr[j] = kr[j];
-      if (key < n) {
-        const int t = base + key;
+      for (int j = 0; j < kPieces; ++j) {
+        const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
+        const int t = base + min(key, n - 1);
         const __half *ks = state.k, *vs = state.v;
-        int slot = slot0 + key;
+        int slot = slot0 + min(key, n - 1);
         if (slot >= capacity)
           slot = capacity >= kDecodeTile ? slot - capacity : slot % capacity;
         size_t row = size_t(slot) * stride;
@@ -180,18 +200,27 @@ __global__ void __launch_bounds__(kThreads, 4)
           row = size_t(t - position) * stride;
         }
         row += size_t(g) * kHeadDim;
-        kr[j] = __ldcg(reinterpret_cast<const uint4*>(ks + row) + piece);
-        vr[j] = __ldcg(reinterpret_cast<const uint4*>(vs + row) + piece);
+        cp_async16(&sk[at128(key, piece)],
+                   reinterpret_cast<const uint4*>(ks + row) + piece, key < n);
+        cp_async16(&sv[at128(key, piece)],
+                   reinterpret_cast<const uint4*>(vs + row) + piece, key < n);
       }
     }
+    cp_async_commit();
   };
+  // with settled rings the first tiles are copied while the previous
+  // kernel finishes (the row at `position` is patched in below)
   const bool early = !op && p.ring_settled;
-  if (early)
-    load_tile(begin);
+  if (early) {
+    issue_tile(0);
+    issue_tile(1);
+  }
   grid_dependency_wait();
   allow_dependents();
-  if (!early)
-    load_tile(begin);
+  if (!early) {
+    issue_tile(0);
+    issue_tile(1);
+  }
 
   // ---- query heads of this group (normalised, rotated), as hi + lo fp16
   // terms; heads G..7 are zero
@@ -251,23 +280,27 @@ __global__ void __launch_bounds__(kThreads, 4)
   float mrun[2] = {-INFINITY, -INFINITY};
   float o[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 
-  for (int base = begin; base < end; base += kDecodeTile) {
+  for (int tile = 0, base = begin; base < end; ++tile, base += kDecodeTile) {
     const int n = min(kDecodeTile, end - base);
-#pragma unroll
-    for (int j = 0; j < kPieces; ++j) {
-      const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-      uint4 kv = kr[j], vv = vr[j];
-      if (stores_row && base + key == position) {
-        // the ring slot may have been read before this CTA wrote it
-        kv = *reinterpret_cast<const uint4*>(&s.newk[piece * 8]);
-        vv = *reinterpret_cast<const uint4*>(&s.newv[piece * 8]);
-      }
-      *reinterpret_cast<uint4*>(&s.k[at128(key, piece)]) = kv;
-      *reinterpret_cast<uint4*>(&s.v[at128(key, piece)]) = vv;
-    }
+    __half* const tk = s.k[tile % kTileBufs];
+    __half* const tv = s.v[tile % kTileBufs];
+    cp_async_wait_older();  // this tile's group (the next one may fly)
     __syncthreads();
-    if (base + kDecodeTile < end)
-      load_tile(base + kDecodeTile);  // in flight during this tile's math
+    if (stores_row && position >= base && position < base + n) {
+      // the ring slot may have been copied before this CTA wrote it
+      if (tid < 32) {
+        const int key = position - base;
+        for (int piece = tid % 16; piece < 16; piece += 16) {
+          if (tid < 16)
+            *reinterpret_cast<uint4*>(&tk[at128(key, piece)]) =
+                *reinterpret_cast<const uint4*>(&s.newk[piece * 8]);
+          else
+            *reinterpret_cast<uint4*>(&tv[at128(key, piece)]) =
+                *reinterpret_cast<const uint4*>(&s.newv[piece * 8]);
+        }
+      }
+      __syncthreads();
+    }
 
     // ---- S^T = K Q^T: warp w owns keys 16 w .. 16 w + 15
     float sh[4] = {0, 0, 0, 0}, sl[4] = {0, 0, 0, 0};
@@ -276,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 4)
 #pragma unroll
       for (int ks = 0; ks < kHeadDim / 16; ++ks) {
         uint32_t a[4], bh[2], bl[2];
-        ldsm_x4(a, &s.k[at128(key, 2 * ks + (mj >> 1))]);
+        ldsm_x4(a, &tk[at128(key, 2 * ks + (mj >> 1))]);
         ldsm_x2(bh, &s.qh[at128(mrow, 2 * ks + (mj & 1))]);
         ldsm_x2(bl, &s.ql[at128(mrow, 2 * ks + (mj & 1))]);
         mma_f16(sh, a, bh[0], bh[1]);
@@ -355,16 +388,17 @@ __global__ void __launch_bounds__(kThreads, 4)
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         uint32_t a[4];
-        ldsm_x4_trans(a, &s.v[at128(key, 2 * (2 * warp + mt) + (mj & 1))]);
+        ldsm_x4_trans(a, &tv[at128(key, 2 * (2 * warp + mt) + (mj & 1))]);
         mma_f16(o[mt], a, bh[0], bh[1]);
         mma_f16(o[mt], a, bl[0], bl[1]);
       }
     }
-    __syncthreads();  // before the next tile overwrites k, v and p
+    __syncthreads();  // this tile's buffers and p are free
+    issue_tile(tile + kTileBufs);
   }
 
   // ---- O (FP32 [head][dim]), maxima and denominators to shared memory
-  float* so = reinterpret_cast<float*>(s.k);
+  float* so = reinterpret_cast<float*>(s.k[0]);
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
     const int dim = (2 * warp + mt) * 16 + fg;
@@ -497,8 +531,18 @@ cudaError_t launch_group(const DecodeAttentionParams& p, int rows,
   const int spans = p.span_grid > 0 && p.span_grid < kMaxDecodeSplits
                         ? p.span_grid
                         : kMaxDecodeSplits;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        decode_attention_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        int(sizeof(DecodeSmem)));
+    if (e != cudaSuccess)
+      return e;
+    configured = true;
+  }
   config.gridDim = dim3(p.kv_heads, spans, rows);
   config.blockDim = dim3(kThreads);
+  config.dynamicSmemBytes = sizeof(DecodeSmem);
   config.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
