@@ -8,9 +8,14 @@ lengths uniform in [64, 4096] (seed 1, + rank), prefilled through 512-row
 prompt passes; then decode rounds of all 8 ragged rows. A "step" is one
 decode round (8 tokens per GPU); `value` is whole-job decode tok/s with every
 input resident on the device (ForwardBatchInputs, logits left in HBM), `e2e`
-is the same through the host API (ForwardBatch with pinned host token and
-logits buffers, greedy tokens chosen on the host). Prefill tok/s of the
-workload's 512-row passes and of a standalone 512-row pass go beside it.
+is the same through the host API with token selection on the device
+(ForwardBatchSample: pinned tokens in, the reference runner's sampler
+applied on the device, selected tokens out), `e2e_logits` through
+ForwardBatch (every session's logits to pinned host memory, greedy selection
+on the host). Prefill tok/s of the workload's 512-row passes and of a
+standalone 512-row pass go beside it, and `config3_job` runs BASELINE config
+3 whole: arrivals 0-2 rounds apart, prompt passes between decode rounds,
+256 sampled tokens per session.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -411,6 +416,136 @@ def rank_workload(rank, prompt_max, vocab):
     return lengths, prompts
 
 
+SAMPLER = (0.1, 50, 1.1)  # the reference runner's defaults (runner.cpp:31-35)
+GOLDEN64 = np.uint64(0x9E3779B97F4A7C15)
+
+
+class SampledRounds:
+    """Decode rounds of a fixed batch through the host API with selection on
+    the device (lfm3_session_forward_batch_sample): the reference runner's
+    sampler (temperature 0.1, top-k 50, repeat penalty 1.1) over each
+    session's last 64 tokens, kept as a ring in one host table that is
+    updated in place; a fresh seed per draw from (session seed, position).
+    Pinned token buffers in and out, as a C++ host would hold them."""
+
+    def __init__(self, lfm3, sessions, tokens, histories, seed):
+        import torch
+        n = len(sessions)
+        self.lfm3, self.lib, self.n = lfm3, lfm3.library(), n
+        self.handles = (ctypes.c_void_p * n)(*[s.handle for s in sessions])
+        self.sampler = lfm3.sampler(*SAMPLER)
+        self.table = np.zeros((n, 64), np.uint32)
+        self.count = np.zeros(n, np.uint32)
+        self.ring = np.zeros(n, np.int64)
+        for r, h in enumerate(histories):
+            h = np.asarray(h, np.uint32)[-64:]
+            self.table[r, :h.size] = h
+            self.count[r] = h.size
+            self.ring[r] = h.size % 64
+        self.tokens = torch.empty(n, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+        self.out = torch.empty(n, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+        self.tokens[:] = tokens
+        self.base = np.array([(seed << 8) + r for r in range(n)], np.uint64)
+        self.positions = np.array([s.position for s in sessions], np.uint64)
+        self.seeds = np.zeros(n, np.uint64)
+        self.rows = np.arange(n)
+        ptr = lambda a: ctypes.c_void_p(a.ctypes.data)  # noqa: E731
+        self.args = (self.handles, ptr(self.tokens), n, ctypes.byref(self.sampler),
+                     ptr(self.table), ptr(self.count), ptr(self.seeds), ptr(self.out))
+        # bytes each round sends to the device: the round's row table
+        # (DecodeRows) and the selection's per-row tables (kernel parameters)
+        self.h2d_bytes = 136 + n * (64 * 4 + 4 + 8)
+        self.d2h_bytes = 4 * n
+
+    def round(self):
+        # the token this round consumes joins its session's penalty window
+        self.table[self.rows, self.ring] = self.tokens
+        self.ring = (self.ring + 1) % 64
+        np.minimum(self.count + 1, 64, out=self.count)
+        with np.errstate(over="ignore"):
+            self.seeds[:] = self.base ^ (self.positions * GOLDEN64)
+        self.lfm3.check(self.lib.lfm3_session_forward_batch_sample(*self.args))
+        self.positions += 1
+        self.tokens[:] = self.out
+
+
+def config3_job(lfm3, model, cfg, rank, prompt_max, decode_tokens=256, trace=None):
+    """BASELINE config 3 as one whole job on this GPU: 8 sessions (prompts
+    U[64, prompt_max], seed (1, rank)) arriving 0-2 decode rounds apart
+    (seed (2, rank)). Each scheduler step runs one prompt pass of at most 512
+    rows for the first arrived session with prompt left (FIFO), then one
+    decode round of every decoding session with the reference runner's
+    sampler on the device (ForwardBatchSample); a session's first token is
+    selected on the host from its last pass's logits (lfm3_sample_host).
+    Every session decodes `decode_tokens` tokens. Each call returns with its
+    results on the host, so host time per call is the end-to-end time.
+    `trace`, when given, receives (step, "pass", session) and (step, "round",
+    sessions) in order."""
+    lengths, prompts = rank_workload(rank, prompt_max, cfg.vocab)
+    rng = np.random.default_rng([2, rank])
+    arrive = np.concatenate([[0], np.cumsum(rng.integers(0, 3, SESSIONS - 1))])
+    sessions = [model.session(int(n) + decode_tokens + 8) for n in lengths]
+    smp = lfm3.sampler(*SAMPLER)
+    done = [0] * SESSIONS
+    decoded = [0] * SESSIONS
+    pending = [None] * SESSIONS
+    history = [list(map(int, p[-64:])) for p in prompts]
+
+    def seed(i, position):
+        return ((1000 + rank) << 40) ^ (i << 32) ^ position
+
+    t_prefill = t_decode = 0.0
+    prefill_tokens = decode_rows = rounds = passes = 0
+    step = 0
+    t_job = time.perf_counter()
+    while any(d < decode_tokens for d in decoded):
+        queue = [i for i in range(SESSIONS)
+                 if arrive[i] <= step and done[i] < len(prompts[i])]
+        if queue:
+            i = queue[0]
+            a = done[i]
+            b = min(a + 512, len(prompts[i]))
+            last = b == len(prompts[i])
+            t0 = time.perf_counter()
+            logits = sessions[i].forward(prompts[i][a:b], logits=last)
+            if last:
+                pending[i] = int(lfm3.sample_host(logits, smp, recent=[history[i]],
+                                                  seeds=[seed(i, b)])[0])
+                decoded[i] = 1
+            t_prefill += time.perf_counter() - t0
+            if trace is not None:
+                trace.append((step, "pass", i))
+            prefill_tokens += b - a
+            passes += 1
+            done[i] = b
+        live = [i for i in range(SESSIONS)
+                if pending[i] is not None and decoded[i] < decode_tokens]
+        if live:
+            for i in live:
+                history[i] = (history[i] + [pending[i]])[-64:]
+            t0 = time.perf_counter()
+            nxt = lfm3.Session.forward_batch_sample(
+                [sessions[i] for i in live], [pending[i] for i in live], smp,
+                recent=[history[i] for i in live],
+                seeds=[seed(i, sessions[i].position) for i in live])
+            t_decode += time.perf_counter() - t0
+            if trace is not None:
+                trace.append((step, "round", live))
+            for i, t in zip(live, nxt):
+                pending[i] = int(t)
+                decoded[i] += 1
+            decode_rows += len(live)
+            rounds += 1
+        step += 1
+    t_job = time.perf_counter() - t_job
+    for s in sessions:
+        s.close()
+    return {"decode_tokens": decode_rows, "decode_s": t_decode,
+            "prefill_tokens": prefill_tokens, "prefill_s": t_prefill,
+            "job_s": t_job, "rounds": rounds, "passes": passes,
+            "arrivals": [int(a) for a in arrive]}
+
+
 def job_rate(tokens_per_rank, world, max_ms):
     """Whole-job throughput: every rank's tokens over the slowest rank's time."""
     return tokens_per_rank * world / (max_ms / 1e3)
@@ -586,6 +721,24 @@ def main():
     barrier()
     e2e_ms_max = sync_max(e2e_ms)
 
+    # ---- end to end with token selection on the device: the same rounds
+    # through ForwardBatchSample (pinned tokens in, selected tokens out)
+    rounds = SampledRounds(lfm3, sessions, pinned_tokens,
+                           [p[-64:] for p in prompts], seed=1000 + rank)
+    for _ in range(args.warmup):
+        rounds.round()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    start.record(fst)
+    for _ in range(args.steps):
+        rounds.round()
+    end.record(fst)
+    end.synchronize()
+    sampled_ms = max(start.elapsed_time(end), (time.perf_counter() - t0) * 1e3)
+    barrier()
+    sampled_ms_max = sync_max(sampled_ms)
+
     # ---- profiled pass (events around each kernel; not the headline timing)
     front.set_profiling(True)
     front.take_profile()
@@ -607,8 +760,15 @@ def main():
                "sample": f"{threads} sessions x 2 decode tokens at depth 3, one session "
                          f"per host thread ({elapsed:.1f} s)"}
 
+    # ---- BASELINE config 3 as a whole job (arrivals, passes between rounds)
+    job = config3_job(lfm3, model, cfg, rank, args.prompt_max)
+    job_decode_s = sync_max(job["decode_s"])
+    job_prefill_s = sync_max(job["prefill_s"])
+    job_s = sync_max(job["job_s"])
+
     value = job_rate(SESSIONS * args.steps, world, decode_ms_max)
-    e2e = job_rate(SESSIONS * args.steps, world, e2e_ms_max)
+    e2e = job_rate(SESSIONS * args.steps, world, sampled_ms_max)
+    e2e_logits = job_rate(SESSIONS * args.steps, world, e2e_ms_max)
     prefill_rate = ranks.sync_sum(prefill_tokens) / (sync_max(prefill_ms) / 1e3)
     if rank != 0:
         ranks.close()
@@ -663,8 +823,27 @@ def main():
         },
         "kernel_ms_per_round": {k: v[0] / profiled_rounds for k, v in prof.items() if v[1]},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 136,
-                "d2h_bytes_per_step": 4 * cfg.vocab * SESSIONS},
+        "e2e": {"value": e2e, "unit": "tok/s",
+                "h2d_bytes_per_step": rounds.h2d_bytes,
+                "d2h_bytes_per_step": rounds.d2h_bytes,
+                "path": "lfm3_session_forward_batch_sample: pinned tokens in, the "
+                        "tokens selected on the device out (temperature 0.1, top-k 50, "
+                        "repeat penalty 1.1 over each session's last 64 tokens)"},
+        "e2e_logits": {"value": e2e_logits, "unit": "tok/s", "h2d_bytes_per_step": 136,
+                       "d2h_bytes_per_step": 4 * cfg.vocab * SESSIONS,
+                       "path": "lfm3_session_forward_batch: pinned tokens in, every "
+                               "session's logits out, greedy selection on the host"},
+        "config3_job": {
+            "decode_tok_s": job["decode_tokens"] * world / job_decode_s,
+            "prefill_tok_s": job["prefill_tokens"] * world / job_prefill_s,
+            "job_s": job_s, "rounds": job["rounds"], "passes": job["passes"],
+            "decode_tokens": job["decode_tokens"] * world,
+            "prefill_tokens": job["prefill_tokens"] * world,
+            "arrivals_rank0": job["arrivals"],
+            "how": "8 sessions/GPU, prompts U[64,4096], arrivals 0-2 rounds apart; each "
+                   "step one <=512-row prompt pass (FIFO) then one decode round of every "
+                   "decoding session with device sampling; 256 tokens per session; "
+                   "host-timed calls, max over ranks"},
         "gpu_launches": int(launches),
         "clocks": clocks,
     }

@@ -197,6 +197,44 @@ int lfm3_cuda_batched_rmsnorm(const float* x, const float* weight, float* out,
                               void* out_bf16, size_t batch, size_t dim,
                               float eps, void* stream);
 
+/* ---- token selection --------------------------------------------------------
+ * The reference's runner reads each round's logits to the host and samples
+ * them with Gufo core's sampling::SamplerState (runner.cpp:268-296, defaults
+ * temperature 0.1, top-k 50, repeat penalty 1.1 at runner.cpp:31-35). That
+ * sampler is not in the reference tree; this library's rule, the same on the
+ * device and on the host:
+ *   1. each distinct token of a row's recent tokens: l = l > 0 ? l / p : l * p
+ *   2. the top_k largest logits, ordered by (logit descending, id ascending)
+ *   3. w_i = exp((l_i - l_0) / temperature) in double precision, S = w_0 +
+ *      w_1 + ... in that order, u = uniform [0, 1) from the row's seed
+ *      (SplitMix64), token = first candidate whose running sum exceeds u * S.
+ * Temperature 0 selects the largest penalised logit (lowest id on ties).
+ * Per-row tables are HOST memory read at call time: recent[r * 64 + j] for
+ * j < recent_count[r] (<= 64; the caller's penalty window, e.g. the row's
+ * last 64 tokens), seeds[r] (a fresh value per draw, e.g. a hash of the
+ * session's seed and position). */
+#define LFM3_SAMPLE_MAX_TOP_K 64
+#define LFM3_SAMPLE_MAX_RECENT 64
+typedef struct lfm3_sampler {
+  float temperature;    /* >= 0; 0 selects the largest logit */
+  uint32_t top_k;       /* 1..64 (ignored at temperature 0) */
+  float repeat_penalty; /* > 0; 1 disables the penalty */
+} lfm3_sampler;
+
+/* Device scratch bytes of lfm3_cuda_sample for rows x vocab. */
+size_t lfm3_cuda_sample_scratch_bytes(int rows, int vocab, int top_k);
+/* Device selection: logits [rows][ld] and tokens[rows] are device memory,
+ * the tables host memory; vocab <= 64 x 4096 / top_k. */
+int lfm3_cuda_sample(const float* logits, int rows, int vocab, int ld,
+                     const lfm3_sampler* sampler, const uint32_t* recent,
+                     const uint32_t* recent_count, const uint64_t* seeds,
+                     uint32_t* tokens, void* scratch, void* stream);
+/* The same selection on the host (host logits and tokens). */
+int lfm3_sample_host(const float* logits, int rows, int vocab, int ld,
+                     const lfm3_sampler* sampler, const uint32_t* recent,
+                     const uint32_t* recent_count, const uint64_t* seeds,
+                     uint32_t* tokens);
+
 /* ---- engine (engine.hpp) --------------------------------------------------- */
 
 typedef struct lfm3_model lfm3_model;
@@ -232,6 +270,18 @@ int lfm3_session_forward_batch_inputs(lfm3_session* const* sessions,
                                       const uint32_t* tokens,
                                       const float* const* rows, size_t count,
                                       int logits);
+/* A batched round followed by token selection on the device: the runner's
+ * AdvanceBatch + SelectNext (runner.cpp:268-351) without the logits' trip
+ * to the host. One token per session in, next[i] (host) the token selected
+ * from session i's new logits by `sampler` with row i of the host tables
+ * (see lfm3_sampler); the logits also stay readable by
+ * lfm3_session_read_logits. Returns after the tokens are on the host. */
+int lfm3_session_forward_batch_sample(lfm3_session* const* sessions,
+                                      const uint32_t* tokens, size_t count,
+                                      const lfm3_sampler* sampler,
+                                      const uint32_t* recent,
+                                      const uint32_t* recent_count,
+                                      const uint64_t* seeds, uint32_t* next);
 int lfm3_session_read_logits(lfm3_session* session, float* logits);
 int lfm3_session_read_hidden(lfm3_session* session, float* hidden);
 int lfm3_session_reset(lfm3_session* session);

@@ -93,6 +93,14 @@ def library():
         "lfm3_session_set_profiling": ([P, I], I),
         "lfm3_session_take_profile": ([P, P, P], I),
         "lfm3_cuda_launch_count": ([], ctypes.c_ulonglong),
+        "lfm3_cuda_sample_scratch_bytes": ([I, I, I], SZ),
+        "lfm3_cuda_sample": ([P, I, I, I, ctypes.POINTER(abi.Sampler), P, P,
+                              P, P, P, P], I),
+        "lfm3_sample_host": ([P, I, I, I, ctypes.POINTER(abi.Sampler), P, P,
+                              P, P], I),
+        "lfm3_session_forward_batch_sample": ([P, P, SZ,
+                                               ctypes.POINTER(abi.Sampler),
+                                               P, P, P, P], I),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -116,6 +124,40 @@ def check(code):
 
 def _ptr(array):
     return ctypes.c_void_p(array.ctypes.data) if array is not None else None
+
+
+# ---- token selection -------------------------------------------------------------
+
+def sampler(temperature=0.1, top_k=50, repeat_penalty=1.1):
+    """lfm3_sampler; the defaults are the reference runner's (runner.cpp:31-35)."""
+    return abi.Sampler(float(temperature), int(top_k), float(repeat_penalty))
+
+
+def sample_tables(rows, recent=None, seeds=None):
+    """Host tables of lfm3_sampler's rows: recent[r] (a sequence of at most 64
+    tokens; only its distinct values matter) and seeds[r] (uint64)."""
+    table = np.zeros((rows, abi.SAMPLE_MAX_RECENT), np.uint32)
+    count = np.zeros(rows, np.uint32)
+    for r, toks in enumerate(recent or []):
+        toks = np.asarray(toks, dtype=np.uint32)[-abi.SAMPLE_MAX_RECENT:]
+        table[r, :toks.size] = toks
+        count[r] = toks.size
+    seed = np.zeros(rows, np.uint64)
+    if seeds is not None:
+        seed[:] = np.asarray(seeds, dtype=np.uint64)
+    return table, count, seed
+
+
+def sample_host(logits, sampler_, recent=None, seeds=None):
+    """lfm3_sample_host over host logits [rows][vocab]: the selected tokens."""
+    x = np.ascontiguousarray(np.atleast_2d(np.asarray(logits, np.float32)))
+    rows, vocab = x.shape
+    table, count, seed = sample_tables(rows, recent, seeds)
+    out = np.zeros(rows, np.uint32)
+    check(library().lfm3_sample_host(
+        _ptr(x), rows, vocab, vocab, ctypes.byref(sampler_), _ptr(table),
+        _ptr(count), _ptr(seed), _ptr(out)))
+    return out
 
 
 # ---- synthetic weights -----------------------------------------------------------
@@ -237,6 +279,21 @@ class Session:
                 if logits else None)
         check(lib.lfm3_session_forward_batch(handles, _ptr(toks), n, ptrs))
         return outs if logits else None
+
+    @staticmethod
+    def forward_batch_sample(sessions, tokens, sampler_, recent=None,
+                             seeds=None):
+        """ForwardBatch followed by token selection on the device: returns
+        the selected token of each session (uint32 array)."""
+        n = len(sessions)
+        handles = (ctypes.c_void_p * n)(*[s.handle for s in sessions])
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        table, count, seed = sample_tables(n, recent, seeds)
+        out = np.zeros(n, np.uint32)
+        check(library().lfm3_session_forward_batch_sample(
+            handles, _ptr(toks), n, ctypes.byref(sampler_), _ptr(table),
+            _ptr(count), _ptr(seed), _ptr(out)))
+        return out
 
     @staticmethod
     def forward_batch_inputs(sessions, tokens, logits=True):

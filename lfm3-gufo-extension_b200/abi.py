@@ -77,6 +77,20 @@ class SynthModel(ctypes.Structure):
     ]
 
 
+SAMPLE_MAX_TOP_K = 64
+SAMPLE_MAX_RECENT = 64
+
+
+class Sampler(ctypes.Structure):
+    """lfm3_sampler (include/lfm3_cuda.h): temperature 0 selects the largest
+    logit; top_k 1..64; repeat_penalty 1 disables the penalty."""
+    _fields_ = [
+        ("temperature", ctypes.c_float),
+        ("top_k", ctypes.c_uint32),
+        ("repeat_penalty", ctypes.c_float),
+    ]
+
+
 def declare_synth(lib):
     """Argument types of the lfm3_synth_* entry points (include/lfm3_synth.h)."""
     lib.lfm3_synth_default_config.argtypes = [ctypes.POINTER(Config)]

@@ -27,7 +27,7 @@ CUDA_FLAGS = ARCH + [
 SOURCES = [
     "abi.cu", "attention_decode.cu", "attention_prompt.cu", "conv.cu",
     "device_error.cu", "engine.cpp", "noalloc.cu", "norm.cu", "q8_gemv.cu",
-    "q8_prefill.cu",
+    "q8_prefill.cu", "sampling.cu",
     "tensor_map.cpp",
 ]
 HOST_C = ["host/synth.c"]

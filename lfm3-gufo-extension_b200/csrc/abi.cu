@@ -507,6 +507,87 @@ int lfm3_cuda_batched_rmsnorm(const float* x, const float* weight, float* out,
       Stream(stream), false));
 }
 
+// ---- token selection ------------------------------------------------------------
+namespace {
+
+// Controls and per-row tables checked for `rows` rows of `vocab` logits.
+int SampleArgs(const lfm3_sampler* sampler, int rows, int vocab,
+               const uint32_t* recent, const uint32_t* recent_count,
+               const uint64_t* seeds, lfm3::SampleControls* c) {
+  if (!sampler || rows < 1 || !recent_count || !seeds || !recent)
+    return Fail(LFM3_ERR_INVALID, "sampler, rows and row tables required");
+  if (const char* why = lfm3::sample_controls(
+          sampler->temperature, sampler->top_k, sampler->repeat_penalty,
+          vocab, c))
+    return Fail(LFM3_ERR_INVALID, why);
+  for (int r = 0; r < rows; ++r) {
+    if (recent_count[r] > uint32_t(lfm3::kSampleMaxRecent))
+      return Fail(LFM3_ERR_INVALID, "more than 64 recent tokens in a row");
+    for (uint32_t j = 0; j < recent_count[r]; ++j)
+      if (recent[size_t(r) * lfm3::kSampleMaxRecent + j] >= uint32_t(vocab))
+        return Fail(LFM3_ERR_INVALID, "recent token outside the vocabulary");
+  }
+  return LFM3_OK;
+}
+
+}  // namespace
+
+size_t lfm3_cuda_sample_scratch_bytes(int rows, int vocab, int top_k) {
+  if (rows < 1 || vocab < 1 || top_k < 1)
+    return 0;
+  return lfm3::sample_scratch_bytes(std::min(rows, 8), vocab,
+                                    std::min(top_k, lfm3::kSampleMaxTopK));
+}
+
+int lfm3_cuda_sample(const float* logits, int rows, int vocab, int ld,
+                     const lfm3_sampler* sampler, const uint32_t* recent,
+                     const uint32_t* recent_count, const uint64_t* seeds,
+                     uint32_t* tokens, void* scratch, void* stream) {
+  lfm3::SampleControls c{};
+  if (const int e =
+          SampleArgs(sampler, rows, vocab, recent, recent_count, seeds, &c))
+    return e;
+  if (!logits || !tokens || !scratch || ld < vocab)
+    return Fail(LFM3_ERR_INVALID, "logits, tokens and scratch required");
+  // eight rows per launch pair, reusing the scratch in stream order
+  for (int r0 = 0; r0 < rows; r0 += 8) {
+    lfm3::SampleParams p{};
+    p.rows = std::min(8, rows - r0);
+    p.logits = logits + size_t(r0) * ld;
+    p.vocab = vocab;
+    p.ld = ld;
+    p.segments = (vocab + lfm3::kSampleSegment - 1) / lfm3::kSampleSegment;
+    p.c = c;
+    for (int r = 0; r < p.rows; ++r) {
+      p.recent_count[r] = recent_count[r0 + r];
+      p.seed[r] = seeds[r0 + r];
+      std::memcpy(p.recent[r], recent + size_t(r0 + r) * lfm3::kSampleMaxRecent,
+                  p.recent_count[r] * sizeof(uint32_t));
+    }
+    p.cand_key = static_cast<uint32_t*>(scratch);
+    p.cand_id = p.cand_key + size_t(p.rows) * p.segments * c.top_k;
+    p.out = tokens + r0;
+    if (const int e = Cuda(lfm3::launch_sample(p, Stream(stream))))
+      return e;
+  }
+  return LFM3_OK;
+}
+
+int lfm3_sample_host(const float* logits, int rows, int vocab, int ld,
+                     const lfm3_sampler* sampler, const uint32_t* recent,
+                     const uint32_t* recent_count, const uint64_t* seeds,
+                     uint32_t* tokens) {
+  lfm3::SampleControls c{};
+  if (const int e =
+          SampleArgs(sampler, rows, vocab, recent, recent_count, seeds, &c))
+    return e;
+  if (!logits || !tokens || ld < vocab)
+    return Fail(LFM3_ERR_INVALID, "logits and tokens required");
+  lfm3::sample_host(logits, rows, vocab, size_t(ld), c, recent, recent_count,
+                    seeds, tokens);
+  return LFM3_OK;
+}
+
 // ---- engine ---------------------------------------------------------------------
 struct lfm3_model {
   std::shared_ptr<lfm3::Model> model;
@@ -600,6 +681,40 @@ int lfm3_session_forward_batch(lfm3_session* const* sessions,
           logits ? std::span<const std::span<float>>(outs, count)
                  : std::span<const std::span<float>>(),
           &error)) {
+    bool poisoned = false;
+    for (size_t r = 0; r < count; ++r)
+      poisoned = poisoned || !batch[r]->IsCoherent();
+    if (error.find("device wait") != std::string::npos)
+      return Fail(LFM3_ERR_DEVICE_WAIT, error);
+    return Fail(poisoned ? LFM3_ERR_POISONED : LFM3_ERR_INVALID, error);
+  }
+  return LFM3_OK;
+}
+
+int lfm3_session_forward_batch_sample(lfm3_session* const* sessions,
+                                      const uint32_t* tokens, size_t count,
+                                      const lfm3_sampler* sampler,
+                                      const uint32_t* recent,
+                                      const uint32_t* recent_count,
+                                      const uint64_t* seeds, uint32_t* next) {
+  if (!sessions || !tokens || !count || count > lfm3::kMaxBatch || !next)
+    return Fail(LFM3_ERR_INVALID, "batch must hold 1..8 sessions");
+  lfm3::Session* batch[lfm3::kMaxBatch];
+  for (size_t r = 0; r < count; ++r) {
+    if (!sessions[r])
+      return Fail(LFM3_ERR_INVALID, "null session");
+    batch[r] = sessions[r]->session.get();
+  }
+  lfm3::SampleControls c{};
+  if (const int e = SampleArgs(sampler, int(count),
+                               int(batch[0]->config().vocab), recent,
+                               recent_count, seeds, &c))
+    return e;
+  std::string error;
+  if (!lfm3::Session::ForwardBatchSample(
+          std::span<lfm3::Session* const>(batch, count),
+          std::span<const uint32_t>(tokens, count), c, recent, recent_count,
+          seeds, std::span<uint32_t>(next, count), &error)) {
     bool poisoned = false;
     for (size_t r = 0; r < count; ++r)
       poisoned = poisoned || !batch[r]->IsCoherent();

@@ -294,6 +294,17 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
         4);
     Throw(cudaMallocHost(reinterpret_cast<void**>(&host_rows_),
                          kRowTables * sizeof(DecodeRows)));
+    {
+      const int segments =
+          int((c.vocab + kSampleSegment - 1) / kSampleSegment);
+      const int top_k =
+          std::max(1, std::min(kSampleMaxTopK, kSampleMaxCandidates / segments));
+      sample_scratch_ =
+          DeviceBuffer(sample_scratch_bytes(int(kMaxBatch), int(c.vocab), top_k));
+      sample_out_ = DeviceBuffer(kMaxBatch * sizeof(uint32_t));
+      Throw(cudaMallocHost(reinterpret_cast<void**>(&sample_host_),
+                           kMaxBatch * sizeof(uint32_t)));
+    }
     for (cudaEvent_t& e : rows_copied_)
       Throw(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     Throw(cudaEventCreateWithFlags(&ready_, cudaEventDisableTiming));
@@ -301,6 +312,8 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
   } catch (...) {
     if (host_rows_)
       cudaFreeHost(host_rows_);
+    if (sample_host_)
+      cudaFreeHost(sample_host_);
     cudaStreamDestroy(stream_);
     throw;
   }
@@ -322,6 +335,8 @@ Session::~Session() {
     cudaEventDestroy(ready_);
   if (host_rows_)
     cudaFreeHost(host_rows_);
+  if (sample_host_)
+    cudaFreeHost(sample_host_);
 }
 
 void Session::Check(cudaError_t status) {
@@ -1028,6 +1043,81 @@ bool Session::Batch(std::span<Session* const> sessions,
       sessions[r]->position_ += 1;
       sessions[r]->logits_ready_ = want;
     }
+    return true;
+  } catch (const std::exception& e) {
+    for (Session* s : sessions)
+      s->poisoned_ = true;
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::ForwardBatchSample(std::span<Session* const> sessions,
+                                 std::span<const uint32_t> tokens,
+                                 const SampleControls& controls,
+                                 const uint32_t* recent,
+                                 const uint32_t* recent_count,
+                                 const uint64_t* seeds,
+                                 std::span<uint32_t> next,
+                                 std::string* error) {
+  // the selection's own checks, before the round mutates anything
+  const char* refused = nullptr;
+  if (sessions.empty() || sessions.size() > kMaxBatch || !sessions.front())
+    refused = "batch must hold 1..8 sessions";
+  else if (next.size() != sessions.size() || !recent || !recent_count ||
+           !seeds)
+    refused = "one selected token and one row of tables per session";
+  const int vocab = refused ? 0 : int(sessions.front()->config().vocab);
+  const int segments = (vocab + kSampleSegment - 1) / kSampleSegment;
+  if (!refused && (controls.top_k < 1 || controls.top_k > kSampleMaxTopK ||
+                   segments * controls.top_k > kSampleMaxCandidates))
+    refused = "sampler top_k does not fit this vocabulary";
+  for (size_t r = 0; r < sessions.size() && !refused; ++r) {
+    if (recent_count[r] > uint32_t(kSampleMaxRecent))
+      refused = "more than 64 recent tokens in a row";
+    for (uint32_t j = 0; j < recent_count[r] && !refused; ++j)
+      if (recent[r * kSampleMaxRecent + j] >= uint32_t(vocab))
+        refused = "recent token outside the vocabulary";
+  }
+  if (refused) {
+    if (error)
+      *error = refused;
+    return false;
+  }
+  if (!Batch(sessions, tokens, {}, true, error))
+    return false;
+  Session* front = sessions.front();
+  const int B = int(sessions.size());
+  try {
+    SampleParams p{};
+    p.rows = B;
+    p.logits = front->batch_logits_.as<float>();
+    p.vocab = vocab;
+    p.ld = vocab;
+    p.segments = segments;
+    p.c = controls;
+    for (int r = 0; r < B; ++r) {
+      p.recent_count[r] = recent_count[r];
+      p.seed[r] = seeds[r];
+      std::copy(recent + size_t(r) * kSampleMaxRecent,
+                recent + size_t(r) * kSampleMaxRecent + recent_count[r],
+                p.recent[r]);
+    }
+    p.cand_key = front->sample_scratch_.as<uint32_t>();
+    p.cand_id = p.cand_key + size_t(B) * segments * controls.top_k;
+    p.out = front->sample_out_.as<uint32_t>();
+    front->Timed(kRowKernels,
+                 [&] { front->Check(launch_sample(p, front->stream_)); });
+    front->Check(cudaMemcpyAsync(front->sample_host_, p.out,
+                                 size_t(B) * sizeof(uint32_t),
+                                 cudaMemcpyDeviceToHost, front->stream_));
+    front->Check(cudaStreamSynchronize(front->stream_));
+    if (const unsigned e = take_device_error())
+      throw std::runtime_error("device wait gave up, code " +
+                               std::to_string(e));
+    front->CollectProfile();
+    std::copy(front->sample_host_, front->sample_host_ + B, next.begin());
     return true;
   } catch (const std::exception& e) {
     for (Session* s : sessions)

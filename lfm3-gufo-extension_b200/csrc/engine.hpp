@@ -17,6 +17,7 @@
 
 #include "../../include/lfm3_types.h"
 #include "decode_types.cuh"
+#include "sampling.cuh"
 
 namespace lfm3 {
 
@@ -127,6 +128,20 @@ public:
   static bool ForwardBatchInputs(std::span<Session* const> sessions,
                                  std::span<const uint32_t> tokens, bool logits,
                                  std::string* error = nullptr);
+  // A round followed by token selection on the device (sampling.cuh): the
+  // runner's AdvanceBatch + SelectNext (runner.cpp:268-351) without the
+  // logits' trip to the host. next[i] is the token selected from session
+  // i's new logits with row i of the host tables (recent[i * 64 + j] for
+  // j < recent_count[i], seeds[i]); the logits stay readable by ReadLogits.
+  // Returns once the tokens are on the host.
+  static bool ForwardBatchSample(std::span<Session* const> sessions,
+                                 std::span<const uint32_t> tokens,
+                                 const SampleControls& controls,
+                                 const uint32_t* recent,
+                                 const uint32_t* recent_count,
+                                 const uint64_t* seeds,
+                                 std::span<uint32_t> next,
+                                 std::string* error = nullptr);
   // The final-normed hidden state / logits of the last advanced row.
   bool ReadHidden(std::span<float> hidden, std::string* error = nullptr);
   bool ReadLogits(std::span<float> logits, std::string* error = nullptr);
@@ -198,6 +213,10 @@ private:
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
       attn_tickets_, prompt_scratch_, split_partial_, zf_;
+  // token selection of the rounds this session leads: candidates, the
+  // selected tokens, and their pinned host copy
+  DeviceBuffer sample_scratch_, sample_out_;
+  uint32_t* sample_host_ = nullptr;
   // the rows of the rounds this session leads: kRowTables pinned tables in
   // turn, each reused once its copy to the device is done
   static constexpr int kRowTables = 4;

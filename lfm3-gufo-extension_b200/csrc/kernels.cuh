@@ -8,6 +8,7 @@
 #include "norm.cuh"
 #include "q8_gemv.cuh"
 #include "q8_prefill.cuh"
+#include "sampling.cuh"
 
 namespace lfm3 {
 
