@@ -755,9 +755,9 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = max(1, min(SESSIONS, os.cpu_count() or 1))
-        rate, elapsed, kind = cpu_decode_rate(weights.weights, threads, 2, 3)
+        rate, elapsed, kind = cpu_decode_rate(weights.weights, threads, 6, 3)
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": kind,
-               "sample": f"{threads} sessions x 2 decode tokens at depth 3, one session "
+               "sample": f"{threads} sessions x 6 decode tokens at depth 3, one session "
                          f"per host thread ({elapsed:.1f} s)"}
 
     # ---- BASELINE config 3 as a whole job (arrivals, passes between rounds)
