@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="no timing: a fixed launch sequence for ncu captures "
                          "(see profile_sequence)")
+    ap.add_argument("--configs", action="store_true",
+                    help="BASELINE configs 2, 4 and a one-GPU slice of 5, one JSON "
+                         "line each (see config_runs); not the headline")
     ap.add_argument("--profile-workload", action="store_true",
                     help="no timing: the bench's own sessions, then decode rounds "
                          "for ncu captures (see profile_workload)")
@@ -90,13 +93,13 @@ def small_tensor_bytes(cfg):
     return total
 
 
-def decode_round_bytes(cfg, depths):
+def decode_round_bytes(cfg, depths, bf16=False):
     """Algorithmic HBM bytes of one decode round whose rows sit at `depths`
-    keys before them: Q8 weights once, plus per row the K/V rows attention
-    reads, the new K/V row, convolution state read+write, logits and the
-    embedding row."""
+    keys before them: Q8 (or BF16) weights once, plus per row the K/V rows
+    attention reads, the new K/V row, convolution state read+write, logits
+    and the embedding row."""
     conv, full, sliding = layer_counts(cfg)
-    W = matrix_elements(cfg) * 34 // 32
+    W = matrix_elements(cfg) * 2 if bf16 else matrix_elements(cfg) * 34 // 32
     kv_key = {i: 2 * cfg.kv_heads[i] * 128 * 2 for i in range(cfg.n_layers)}
     per_key = max(kv_key.values()) if kv_key else 0
     total = W + small_tensor_bytes(cfg)
@@ -110,7 +113,7 @@ def decode_round_bytes(cfg, depths):
                 total += kv_key[i] * min(keys, cfg.window) + kv_key[i]
             else:
                 total += 2 * cfg.hidden * (cfg.conv_width - 1) * 4
-        total += cfg.vocab * 4 + cfg.hidden * 34 // 32
+        total += cfg.vocab * 4 + (cfg.hidden * 2 if bf16 else cfg.hidden * 34 // 32)
     del per_key
     return total
 
@@ -605,8 +608,144 @@ def profile_workload(prompt_max):
 
 
 # ---- our arm ---------------------------------------------------------------------------------
+def config_runs():
+    """The BASELINE configs besides the headline, on one GPU, one JSON line
+    each (printed as each finishes):
+      config2: Q8_0, one session, 2048-token prompt in four 512-row passes,
+        then 128 greedy tokens through Forward (host logits, host argmax);
+      config5: a one-GPU slice of the box-scale config, 8 sessions with
+        prompts log-uniform in [512, 32768] (seed 5), prefilled in 512-row
+        passes, then 512 decode rounds of the 8 rows with logits on the device;
+      config4: BF16 weights, 8 sessions at depth 8192, 128 decode rounds with
+        logits on the device. One session is prefilled from 8192 random
+        tokens; the other seven restore its snapshot (the same state, without
+        seven more prefills of the CUDA-core BF16 prompt path).
+    Device time with CUDA events on the session streams (max with the host's
+    wall time for calls that return to the host)."""
+    import torch
+    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
+    hbm_peak, tensor_peak, _, peak_source = measured_peaks()
+
+    def timed(stream, fn):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        start.record(stream)
+        fn()
+        end.record(stream)
+        end.synchronize()
+        return max(start.elapsed_time(end), (time.perf_counter() - t0) * 1e3)
+
+    def emit(line):
+        line["peak_source"] = peak_source
+        print(json.dumps(line), flush=True)
+
+    w = lfm3.SyntheticWeights(seed=0)
+    cfg = w.config
+    model = lfm3.Model(w.weights)
+    rng = np.random.default_rng(2)
+
+    # ---- config 2
+    prompt = rng.integers(0, cfg.vocab, 2048).astype(np.uint32)
+    warm = model.session(600)
+    warm.forward(prompt[:512])
+    warm.forward(prompt[512:513])
+    warm.close()
+    s = model.session(2048 + 128 + 8)
+    st = torch.cuda.ExternalStream(s.stream)
+    state = {}
+    prefill_ms = timed(st, lambda: state.update(logits=s.forward(prompt)))
+
+    def greedy():
+        tok = int(np.argmax(state["logits"]))
+        for _ in range(128):
+            tok = int(np.argmax(s.forward([tok])))
+
+    decode_ms = timed(st, greedy)
+    flops = sum(prefill_flops(cfg, 512, 512 * i, logits=i == 3) for i in range(4))
+    per_token = decode_ms / 128
+    emit({"config": "config2", "prefill_tok_s": 2048 / (prefill_ms / 1e3),
+          "prefill_tflops": flops / (prefill_ms * 1e-3) / 1e12,
+          "prefill_frac_of_tensor_peak": flops / (prefill_ms * 1e-3) / 1e12 / tensor_peak,
+          "decode_tok_s": 128 / (decode_ms / 1e3), "decode_ms_per_token": per_token,
+          "decode_frac_of_hbm_peak": decode_round_bytes(cfg, [2048 + 64])
+          / (per_token * 1e-3) / 1e9 / hbm_peak,
+          "path": "Forward: four 512-row passes, then 128 one-token calls with host "
+                  "logits and host argmax"})
+    s.close()
+
+    # ---- config 5, one GPU's share
+    lengths = np.exp(rng.uniform(np.log(512), np.log(32768), SESSIONS)).astype(int)
+    prompts = [rng.integers(0, cfg.vocab, int(n)).astype(np.uint32) for n in lengths]
+    sessions = [model.session(int(n) + 512 + 16) for n in lengths]
+    prefill_ms = 0.0
+    flops = 0.0
+    for sess, p in zip(sessions, prompts):
+        prefill_ms += timed(torch.cuda.ExternalStream(sess.stream),
+                            lambda: sess.forward(p, logits=False))
+        flops += sum(prefill_flops(cfg, min(512, len(p) - a), a, logits=False)
+                     for a in range(0, len(p), 512))
+    tokens = [int(t) for t in rng.integers(0, cfg.vocab, SESSIONS)]
+    fst = torch.cuda.ExternalStream(sessions[0].stream)
+
+    def rounds(k):
+        for step in range(k):
+            lfm3.Session.forward_batch_inputs(
+                sessions, [(t + step) % cfg.vocab for t in tokens], logits=True)
+
+    rounds(3)
+    depths = [sess.position for sess in sessions]
+    decode_ms = timed(fst, lambda: rounds(512))
+    per_round = decode_ms / 512
+    bytes_round = decode_round_bytes(cfg, [d + 256 for d in depths])
+    emit({"config": "config5_one_gpu", "prompt_lengths": [int(n) for n in lengths],
+          "prefill_tok_s": int(lengths.sum()) / (prefill_ms / 1e3),
+          "prefill_tflops": flops / (prefill_ms * 1e-3) / 1e12,
+          "decode_tok_s": SESSIONS * 512 / (decode_ms / 1e3),
+          "decode_ms_per_round": per_round,
+          "decode_frac_of_hbm_peak": bytes_round / (per_round * 1e-3) / 1e9 / hbm_peak,
+          "path": "Forward 512-row passes per session, then 512 ForwardBatchInputs "
+                  "rounds of the 8 rows (logits on the device)"})
+    for sess in sessions:
+        sess.close()
+    model.close()
+    w.close()
+
+    # ---- config 4
+    wb = lfm3.SyntheticWeights(seed=0, matrix_type=lfm3.abi.BF16)
+    mb = lfm3.Model(wb.weights)
+    depth = 8192
+    sessions = [mb.session(depth + 128 + 16) for _ in range(SESSIONS)]
+    first = sessions[0]
+    prompt = rng.integers(0, cfg.vocab, depth).astype(np.uint32)
+    prefill_ms = timed(torch.cuda.ExternalStream(first.stream),
+                       lambda: first.forward(prompt, logits=False))
+    snap = first.save_snapshot()
+    for sess in sessions[1:]:
+        sess.restore_snapshot(snap)
+    tokens = [int(t) for t in rng.integers(0, cfg.vocab, SESSIONS)]
+    fst = torch.cuda.ExternalStream(first.stream)
+    rounds(3)
+    decode_ms = timed(fst, lambda: rounds(128))
+    per_round = decode_ms / 128
+    bytes_round = decode_round_bytes(cfg, [depth + 3 + 64] * SESSIONS, bf16=True)
+    emit({"config": "config4", "depth": depth,
+          "prefill_tok_s": depth / (prefill_ms / 1e3),
+          "decode_tok_s": SESSIONS * 128 / (decode_ms / 1e3),
+          "decode_ms_per_round": per_round, "bytes_per_round": bytes_round,
+          "decode_frac_of_hbm_peak": bytes_round / (per_round * 1e-3) / 1e9 / hbm_peak,
+          "path": "one session prefilled (BF16 prompt passes on the CUDA cores), seven "
+                  "restored from its snapshot; 128 ForwardBatchInputs rounds"})
+    for sess in sessions:
+        sess.close()
+    mb.close()
+    wb.close()
+
+
 def main():
     args = parse()
+    if args.configs:
+        config_runs()
+        return
     if args.impl == "reference":
         reference_arm(args)
         return
