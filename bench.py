@@ -55,9 +55,10 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="no timing: a fixed launch sequence for ncu captures "
                          "(see profile_sequence)")
-    ap.add_argument("--configs", action="store_true",
-                    help="BASELINE configs 2, 4 and a one-GPU slice of 5, one JSON "
-                         "line each (see config_runs); not the headline")
+    ap.add_argument("--configs", nargs="?", const="2,5,4", default=None,
+                    help="BASELINE configs 2, 4 and a one-GPU slice of 5 (a comma "
+                         "list selects), one JSON line each (see config_runs); not "
+                         "the headline")
     ap.add_argument("--profile-workload", action="store_true",
                     help="no timing: the bench's own sessions, then decode rounds "
                          "for ncu captures (see profile_workload)")
@@ -608,7 +609,7 @@ def profile_workload(prompt_max):
 
 
 # ---- our arm ---------------------------------------------------------------------------------
-def config_runs():
+def config_runs(which="2,5,4"):
     """The BASELINE configs besides the headline, on one GPU, one JSON line
     each (printed as each finishes):
       config2: Q8_0, one session, 2048-token prompt in four 512-row passes,
@@ -639,12 +640,28 @@ def config_runs():
         line["peak_source"] = peak_source
         print(json.dumps(line), flush=True)
 
-    w = lfm3.SyntheticWeights(seed=0)
-    cfg = w.config
-    model = lfm3.Model(w.weights)
+    chosen = {c.strip() for c in which.split(",")}
     rng = np.random.default_rng(2)
+    if chosen & {"2", "5"}:
+        w = lfm3.SyntheticWeights(seed=0)
+        model = lfm3.Model(w.weights)
+        if "2" in chosen:
+            config2_run(lfm3, w.config, model, rng, timed, emit, tensor_peak, hbm_peak)
+        if "5" in chosen:
+            config5_run(lfm3, w.config, model, rng, timed, emit, hbm_peak)
+        model.close()
+        w.close()
+    if "4" in chosen:
+        wb = lfm3.SyntheticWeights(seed=0, matrix_type=lfm3.abi.BF16)
+        mb = lfm3.Model(wb.weights)
+        config4_run(lfm3, wb.config, mb, rng, timed, emit, hbm_peak)
+        mb.close()
+        wb.close()
 
-    # ---- config 2
+
+def config2_run(lfm3, cfg, model, rng, timed, emit, tensor_peak, hbm_peak):
+    """Config 2 (see config_runs)."""
+    import torch
     prompt = rng.integers(0, cfg.vocab, 2048).astype(np.uint32)
     warm = model.session(600)
     warm.forward(prompt[:512])
@@ -673,7 +690,10 @@ def config_runs():
                   "logits and host argmax"})
     s.close()
 
-    # ---- config 5, one GPU's share
+
+def config5_run(lfm3, cfg, model, rng, timed, emit, hbm_peak):
+    """One GPU's share of config 5 (see config_runs)."""
+    import torch
     lengths = np.exp(rng.uniform(np.log(512), np.log(32768), SESSIONS)).astype(int)
     prompts = [rng.integers(0, cfg.vocab, int(n)).astype(np.uint32) for n in lengths]
     sessions = [model.session(int(n) + 512 + 16) for n in lengths]
@@ -707,12 +727,11 @@ def config_runs():
                   "rounds of the 8 rows (logits on the device)"})
     for sess in sessions:
         sess.close()
-    model.close()
-    w.close()
 
-    # ---- config 4
-    wb = lfm3.SyntheticWeights(seed=0, matrix_type=lfm3.abi.BF16)
-    mb = lfm3.Model(wb.weights)
+
+def config4_run(lfm3, cfg, mb, rng, timed, emit, hbm_peak):
+    """Config 4 (see config_runs)."""
+    import torch
     depth = 8192
     sessions = [mb.session(depth + 128 + 16) for _ in range(SESSIONS)]
     first = sessions[0]
@@ -724,6 +743,12 @@ def config_runs():
         sess.restore_snapshot(snap)
     tokens = [int(t) for t in rng.integers(0, cfg.vocab, SESSIONS)]
     fst = torch.cuda.ExternalStream(first.stream)
+
+    def rounds(k):
+        for step in range(k):
+            lfm3.Session.forward_batch_inputs(
+                sessions, [(t + step) % cfg.vocab for t in tokens], logits=True)
+
     rounds(3)
     decode_ms = timed(fst, lambda: rounds(128))
     per_round = decode_ms / 128
@@ -737,14 +762,12 @@ def config_runs():
                   "restored from its snapshot; 128 ForwardBatchInputs rounds"})
     for sess in sessions:
         sess.close()
-    mb.close()
-    wb.close()
 
 
 def main():
     args = parse()
     if args.configs:
-        config_runs()
+        config_runs(args.configs)
         return
     if args.impl == "reference":
         reference_arm(args)
