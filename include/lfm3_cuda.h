@@ -260,8 +260,9 @@ int lfm3_session_forward_batch(lfm3_session* const* sessions,
                                const uint32_t* tokens, size_t count,
                                float* const* logits);
 /* Session::ForwardBatchInputs (engine.hpp:107-114): one row per session;
- * rows[i] (device embedding rows) must be NULL in this build (tokens[i] is
- * the input). With logits set, each session's logits are computed into its
+ * rows (may be NULL) holds per session NULL (tokens[i] is the input) or a
+ * device row of hidden input-embedding floats, ready in the calling
+ * sessions' stream order (tokens[i] is then ignored). With logits set, each session's logits are computed into its
  * device buffer (lfm3_session_continuation_data tensor 0) without a copy to
  * the host. Returns once the round is queued: work queued on a session's
  * lfm3_session_stream runs after it, the session's reads wait for it, and a
@@ -282,6 +283,32 @@ int lfm3_session_forward_batch_sample(lfm3_session* const* sessions,
                                       const uint32_t* recent,
                                       const uint32_t* recent_count,
                                       const uint64_t* seeds, uint32_t* next);
+/* Session::ForwardEmbeddings (engine.hpp:115-120): n rows of hidden
+ * input-embedding floats, in host memory, or in device memory read in this
+ * session's stream order when on_device is nonzero; logits (host, vocab
+ * floats) may be NULL. */
+int lfm3_session_forward_embeddings(lfm3_session* session, const float* rows,
+                                    size_t n, int on_device, float* logits);
+/* Session::Input / ForwardInputs (engine.hpp:121-131): runs of token ids or
+ * of host embedding rows (one of the two per run), advanced in order with
+ * adjacent runs sharing their 512-row passes. */
+typedef struct lfm3_input {
+  const uint32_t* tokens;
+  size_t n_tokens;
+  const float* rows; /* n_rows x hidden floats, host memory */
+  size_t n_rows;
+} lfm3_input;
+int lfm3_session_forward_inputs(lfm3_session* session,
+                                const lfm3_input* inputs, size_t count,
+                                float* logits);
+/* Session::Speculate (engine.hpp:71-73): the reference starts an NPU decode
+ * early; the GPU has nothing to start, so this only checks the session. */
+int lfm3_session_speculate(lfm3_session* session, uint32_t token);
+/* Session::ForwardDecision / ForwardDecisions (engine.hpp:54-70, d1 models
+ * with bidirectional attention): not built; returns LFM3_ERR_UNSUPPORTED. */
+int lfm3_session_forward_decision(lfm3_session* session,
+                                  const uint32_t* tokens, size_t n,
+                                  float* logits);
 int lfm3_session_read_logits(lfm3_session* session, float* logits);
 int lfm3_session_read_hidden(lfm3_session* session, float* hidden);
 int lfm3_session_reset(lfm3_session* session);
@@ -294,6 +321,29 @@ void* lfm3_session_continuation_data(const lfm3_session* session, int tensor,
                                      size_t layer);
 uint32_t lfm3_session_ring_capacity(const lfm3_session* session,
                                     size_t layer);
+/* ContinuationHooks (continuation_hooks.hpp:5-16) as C callbacks: each
+ * runs on the calling thread before the session changes state or submits
+ * device work, and refuses it by returning nonzero (the call then fails
+ * with LFM3_ERR_INVALID and changes nothing). before_write gets the rows
+ * [first, end) about to be written. SetContinuationHooks
+ * (engine.hpp:146): hooks is copied; NULL removes them. */
+typedef struct lfm3_continuation_hooks {
+  void* user;
+  int (*before_write)(void* user, uint32_t first, uint32_t end);
+  int (*before_reset)(void* user);
+  int (*before_restore)(void* user);
+} lfm3_continuation_hooks;
+int lfm3_session_set_continuation_hooks(lfm3_session* session,
+                                        const lfm3_continuation_hooks* hooks);
+/* PrepareLogits (engine.hpp:153-154): computes the frontier's logits on the
+ * session's stream when the last advance did not. BeginRestore /
+ * FinishRestore (engine.hpp:155-156): around direct writes to the
+ * continuation buffers; BeginRestore waits for queued work and marks the
+ * session incoherent, FinishRestore(position) makes it coherent at
+ * `position` with the written frontier and logits. */
+int lfm3_session_prepare_logits(lfm3_session* session);
+int lfm3_session_begin_restore(lfm3_session* session);
+int lfm3_session_finish_restore(lfm3_session* session, uint32_t position);
 /* Snapshot v2 (engine.hpp:127-131). */
 size_t lfm3_session_snapshot_bytes(const lfm3_session* session);
 int lfm3_session_save_snapshot(lfm3_session* session, uint8_t* out,

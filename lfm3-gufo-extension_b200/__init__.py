@@ -93,6 +93,15 @@ def library():
         "lfm3_session_set_profiling": ([P, I], I),
         "lfm3_session_take_profile": ([P, P, P], I),
         "lfm3_cuda_launch_count": ([], ctypes.c_ulonglong),
+        "lfm3_session_forward_embeddings": ([P, P, SZ, I, P], I),
+        "lfm3_session_forward_inputs": ([P, ctypes.POINTER(abi.Input), SZ, P], I),
+        "lfm3_session_speculate": ([P, U32], I),
+        "lfm3_session_forward_decision": ([P, P, SZ, P], I),
+        "lfm3_session_set_continuation_hooks": (
+            [P, ctypes.POINTER(abi.ContinuationHooks)], I),
+        "lfm3_session_prepare_logits": ([P], I),
+        "lfm3_session_begin_restore": ([P], I),
+        "lfm3_session_finish_restore": ([P, U32], I),
         "lfm3_cuda_sample_scratch_bytes": ([I, I, I], SZ),
         "lfm3_cuda_sample": ([P, I, I, I, ctypes.POINTER(abi.Sampler), P, P,
                               P, P, P, P], I),
@@ -296,14 +305,79 @@ class Session:
         return out
 
     @staticmethod
-    def forward_batch_inputs(sessions, tokens, logits=True):
+    def forward_batch_inputs(sessions, tokens, logits=True, rows=None):
         """ForwardBatchInputs: one token per session, logits left on the
-        device."""
+        device; rows[i], when given and not None, is the device address of
+        session i's input embedding row (used instead of tokens[i])."""
         n = len(sessions)
         handles = (ctypes.c_void_p * n)(*[s.handle for s in sessions])
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        ptrs = (ctypes.c_void_p * n)(*rows) if rows is not None else None
         check(library().lfm3_session_forward_batch_inputs(
-            handles, _ptr(toks), None, n, int(bool(logits))))
+            handles, _ptr(toks), ptrs, n, int(bool(logits))))
+
+    def forward_embeddings(self, rows, logits=True, device_rows=None):
+        """ForwardEmbeddings: host rows (float32 [n][hidden]), or with
+        device_rows=(address, n) rows in device memory; returns the last
+        row's logits (or None)."""
+        out = np.empty(self.vocab, np.float32) if logits else None
+        if device_rows is not None:
+            address, n = device_rows
+            check(library().lfm3_session_forward_embeddings(
+                self.handle, ctypes.c_void_p(address), n, 1, _ptr(out)))
+        else:
+            x = np.ascontiguousarray(np.asarray(rows, np.float32))
+            check(library().lfm3_session_forward_embeddings(
+                self.handle, _ptr(x), x.size // self.hidden, 0, _ptr(out)))
+        return out
+
+    def forward_inputs(self, runs, logits=True):
+        """ForwardInputs over runs [("tokens", ids) | ("rows", floats
+        [n][hidden])]; returns the last row's logits (or None)."""
+        keep, structs = [], []
+        for kind, data in runs:
+            if kind == "tokens":
+                a = np.ascontiguousarray(np.asarray(data, np.uint32))
+                structs.append(abi.Input(a.ctypes.data, a.size, None, 0))
+            else:
+                a = np.ascontiguousarray(np.asarray(data, np.float32))
+                structs.append(abi.Input(None, 0, a.ctypes.data,
+                                         a.size // self.hidden))
+            keep.append(a)
+        arr = (abi.Input * len(structs))(*structs)
+        out = np.empty(self.vocab, np.float32) if logits else None
+        check(library().lfm3_session_forward_inputs(
+            self.handle, arr, len(structs), _ptr(out)))
+        return out
+
+    def set_continuation_hooks(self, before_write=None, before_reset=None,
+                               before_restore=None):
+        """Installs Python callables as ContinuationHooks (a truthy return
+        refuses the change); no arguments removes them."""
+        lib = library()
+        if before_write is None and before_reset is None and before_restore is None:
+            self._hooks = None
+            check(lib.lfm3_session_set_continuation_hooks(self.handle, None))
+            return
+        h = abi.ContinuationHooks(
+            None,
+            abi.HOOK_WRITE(lambda u, a, b: int(bool(before_write and before_write(a, b)))),
+            abi.HOOK_EVENT(lambda u: int(bool(before_reset and before_reset()))),
+            abi.HOOK_EVENT(lambda u: int(bool(before_restore and before_restore()))))
+        self._hooks = h  # the callbacks must outlive the session's use of them
+        check(lib.lfm3_session_set_continuation_hooks(self.handle, ctypes.byref(h)))
+
+    def prepare_logits(self):
+        check(library().lfm3_session_prepare_logits(self.handle))
+
+    def begin_restore(self):
+        check(library().lfm3_session_begin_restore(self.handle))
+
+    def finish_restore(self, position):
+        check(library().lfm3_session_finish_restore(self.handle, position))
+
+    def speculate(self, token):
+        check(library().lfm3_session_speculate(self.handle, token))
 
     def read_logits(self):
         out = np.empty(self.vocab, np.float32)

@@ -77,6 +77,31 @@ class SynthModel(ctypes.Structure):
     ]
 
 
+class Input(ctypes.Structure):
+    """lfm3_input: a run of token ids or of host embedding rows."""
+    _fields_ = [
+        ("tokens", ctypes.c_void_p),
+        ("n_tokens", ctypes.c_size_t),
+        ("rows", ctypes.c_void_p),
+        ("n_rows", ctypes.c_size_t),
+    ]
+
+
+HOOK_WRITE = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint32,
+                              ctypes.c_uint32)
+HOOK_EVENT = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+
+
+class ContinuationHooks(ctypes.Structure):
+    """lfm3_continuation_hooks: nonzero from a callback refuses the change."""
+    _fields_ = [
+        ("user", ctypes.c_void_p),
+        ("before_write", HOOK_WRITE),
+        ("before_reset", HOOK_EVENT),
+        ("before_restore", HOOK_EVENT),
+    ]
+
+
 SAMPLE_MAX_TOP_K = 64
 SAMPLE_MAX_RECENT = 64
 

@@ -592,8 +592,31 @@ int lfm3_sample_host(const float* logits, int rows, int vocab, int ld,
 struct lfm3_model {
   std::shared_ptr<lfm3::Model> model;
 };
+// C callbacks behind the engine's ContinuationHooks: a nonzero return
+// refuses the change (the engine call fails before touching the session).
+class CHooks final : public lfm3::ContinuationHooks {
+public:
+  explicit CHooks(const lfm3_continuation_hooks& c) : c_(c) {}
+  void BeforeWrite(uint32_t first, uint32_t end) override {
+    if (c_.before_write && c_.before_write(c_.user, first, end))
+      throw std::runtime_error("continuation hook refused the write");
+  }
+  void BeforeReset() override {
+    if (c_.before_reset && c_.before_reset(c_.user))
+      throw std::runtime_error("continuation hook refused the reset");
+  }
+  void BeforeRestore() override {
+    if (c_.before_restore && c_.before_restore(c_.user))
+      throw std::runtime_error("continuation hook refused the restore");
+  }
+
+private:
+  lfm3_continuation_hooks c_;
+};
+
 struct lfm3_session {
   std::unique_ptr<lfm3::Session> session;
+  std::unique_ptr<CHooks> hooks;
 };
 
 lfm3_model* lfm3_model_load(const lfm3_weights* host) {
@@ -632,7 +655,7 @@ lfm3_session* lfm3_session_create(lfm3_model* model, uint32_t context) {
       Fail(LFM3_ERR_INVALID, error);
       return nullptr;
     }
-    return new lfm3_session{std::move(s)};
+    return new lfm3_session{std::move(s), nullptr};
   } catch (const std::exception& e) {
     Fail(LFM3_ERR_CUDA, e.what());
     return nullptr;
@@ -731,11 +754,6 @@ int lfm3_session_forward_batch_inputs(lfm3_session* const* sessions,
                                       int logits) {
   if (!sessions || !tokens || !count || count > lfm3::kMaxBatch)
     return Fail(LFM3_ERR_INVALID, "batch must hold 1..8 sessions");
-  if (rows)
-    for (size_t r = 0; r < count; ++r)
-      if (rows[r])
-        return Fail(LFM3_ERR_UNSUPPORTED,
-                    "embedding-row inputs are not built; pass tokens");
   lfm3::Session* batch[lfm3::kMaxBatch];
   for (size_t r = 0; r < count; ++r) {
     if (!sessions[r])
@@ -745,7 +763,10 @@ int lfm3_session_forward_batch_inputs(lfm3_session* const* sessions,
   std::string error;
   if (!lfm3::Session::ForwardBatchInputs(
           std::span<lfm3::Session* const>(batch, count),
-          std::span<const uint32_t>(tokens, count), logits != 0, &error)) {
+          std::span<const uint32_t>(tokens, count),
+          rows ? std::span<const float* const>(rows, count)
+               : std::span<const float* const>(),
+          logits != 0, &error)) {
     bool poisoned = false;
     for (size_t r = 0; r < count; ++r)
       poisoned = poisoned || !batch[r]->IsCoherent();
@@ -753,6 +774,100 @@ int lfm3_session_forward_batch_inputs(lfm3_session* const* sessions,
       return Fail(LFM3_ERR_DEVICE_WAIT, error);
     return Fail(poisoned ? LFM3_ERR_POISONED : LFM3_ERR_INVALID, error);
   }
+  return LFM3_OK;
+}
+
+int lfm3_session_forward_embeddings(lfm3_session* session, const float* rows,
+                                    size_t n, int on_device, float* logits) {
+  if (!session || !rows || !n)
+    return Fail(LFM3_ERR_INVALID, "null argument");
+  auto& s = *session->session;
+  const auto& c = s.config();
+  std::string error;
+  if (!s.ForwardEmbeddings(
+          std::span<const float>(rows, n * c.hidden), on_device != 0,
+          logits ? std::span<float>(logits, c.vocab) : std::span<float>(),
+          &error))
+    return SessionStatus(s, error);
+  return LFM3_OK;
+}
+
+int lfm3_session_forward_inputs(lfm3_session* session,
+                                const lfm3_input* inputs, size_t count,
+                                float* logits) {
+  if (!session || (!inputs && count))
+    return Fail(LFM3_ERR_INVALID, "null argument");
+  auto& s = *session->session;
+  const auto& c = s.config();
+  std::vector<lfm3::Session::Input> runs(count);
+  for (size_t i = 0; i < count; ++i) {
+    const lfm3_input& in = inputs[i];
+    if ((in.n_tokens && !in.tokens) || (in.n_rows && !in.rows))
+      return Fail(LFM3_ERR_INVALID, "null input run");
+    runs[i].tokens = std::span<const uint32_t>(in.tokens, in.n_tokens);
+    runs[i].rows = std::span<const float>(in.rows, in.n_rows * c.hidden);
+  }
+  std::string error;
+  if (!s.ForwardInputs(
+          runs, logits ? std::span<float>(logits, c.vocab) : std::span<float>(),
+          &error))
+    return SessionStatus(s, error);
+  return LFM3_OK;
+}
+
+int lfm3_session_speculate(lfm3_session* session, uint32_t token) {
+  if (!session)
+    return Fail(LFM3_ERR_INVALID, "null session");
+  session->session->Speculate(token);
+  return LFM3_OK;
+}
+
+int lfm3_session_forward_decision(lfm3_session* session,
+                                  const uint32_t* tokens, size_t n,
+                                  float* logits) {
+  (void)tokens;
+  (void)n;
+  (void)logits;
+  if (!session)
+    return Fail(LFM3_ERR_INVALID, "null session");
+  return Fail(LFM3_ERR_UNSUPPORTED,
+              "d1 decision passes (bidirectional attention) are not built");
+}
+
+int lfm3_session_set_continuation_hooks(lfm3_session* session,
+                                        const lfm3_continuation_hooks* hooks) {
+  if (!session)
+    return Fail(LFM3_ERR_INVALID, "null session");
+  session->session->SetContinuationHooks(nullptr);
+  session->hooks = hooks ? std::make_unique<CHooks>(*hooks) : nullptr;
+  session->session->SetContinuationHooks(session->hooks.get());
+  return LFM3_OK;
+}
+
+int lfm3_session_prepare_logits(lfm3_session* session) {
+  if (!session)
+    return Fail(LFM3_ERR_INVALID, "null session");
+  std::string error;
+  if (!session->session->PrepareLogits(&error))
+    return SessionStatus(*session->session, error);
+  return LFM3_OK;
+}
+
+int lfm3_session_begin_restore(lfm3_session* session) {
+  if (!session)
+    return Fail(LFM3_ERR_INVALID, "null session");
+  std::string error;
+  if (!session->session->BeginRestore(&error))
+    return Fail(LFM3_ERR_CUDA, error);
+  return LFM3_OK;
+}
+
+int lfm3_session_finish_restore(lfm3_session* session, uint32_t position) {
+  if (!session)
+    return Fail(LFM3_ERR_INVALID, "null session");
+  std::string error;
+  if (!session->session->FinishRestore(position, &error))
+    return Fail(LFM3_ERR_INVALID, error);
   return LFM3_OK;
 }
 

@@ -423,7 +423,8 @@ void Session::LaunchLmHead(const void* split_rows, int rows, float* out) {
 }
 
 void Session::DecodeRound(std::span<Session* const> batch,
-                          std::span<const uint32_t> tokens, bool logits) {
+                          std::span<const uint32_t> tokens, bool logits,
+                          const float* const* input_rows, bool rows_on_host) {
   const auto& w = model_->weights();
   const auto& c = w.config;
   const int B = int(batch.size());
@@ -468,6 +469,23 @@ void Session::DecodeRound(std::span<Session* const> batch,
                             NormOut{nullptr, z, nullptr, nullptr}, B, H, c.eps,
                             s, /*pdl=*/false));  // after all earlier work
   });
+  // rows given as input embeddings replace their token rows in x, then the
+  // first norm runs again over every row
+  bool embedded = false;
+  for (int r = 0; input_rows && r < B; ++r)
+    if (input_rows[r]) {
+      Check(cudaMemcpyAsync(x + size_t(r) * H, input_rows[r], size_t(H) * 4,
+                            rows_on_host ? cudaMemcpyHostToDevice
+                                         : cudaMemcpyDeviceToDevice,
+                            s));
+      embedded = true;
+    }
+  if (embedded)
+    Timed(kRowKernels, [&] {
+      Check(launch_residual_norm(
+          nullptr, nullptr, x, static_cast<const float*>(w.layers[0].norm.data),
+          NormOut{nullptr, z, nullptr, nullptr}, B, H, c.eps, s, false));
+    });
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     const auto& l = w.layers[i];
     if (c.layer_type[i] == LFM3_CONV) {
@@ -614,7 +632,8 @@ void Session::DecodeRound(std::span<Session* const> batch,
 }
 
 // ---- prompt pass --------------------------------------------------------------
-void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
+void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
+                     std::span<const RowRun> runs, bool on_device) {
   const auto& w = model_->weights();
   const auto& c = w.config;
   const int n = int(tokens.size());
@@ -731,6 +750,12 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits) {
                               ids_.as<uint32_t>(), nullptr, x, nullptr,
                               NormOut{}, n, H, c.eps, s, kPdl));
     });
+    // rows given as input embeddings replace their token rows
+    for (const RowRun& run : runs)
+      Check(cudaMemcpyAsync(x + run.first * H, run.data, run.count * H * 4,
+                            on_device ? cudaMemcpyDeviceToDevice
+                                      : cudaMemcpyHostToDevice,
+                            s));
     rows([&] {
       Check(launch_residual_norm(
           nullptr, nullptr, x + size_t(o_in) * H,
@@ -909,16 +934,42 @@ bool Session::Forward(std::span<const uint32_t> tokens, std::span<float> logits,
       *error = e.what();
     return false;
   }
+  return Advance(tokens, {}, false, logits, error);
+}
+
+bool Session::Advance(std::span<const uint32_t> ids,
+                      std::span<const RowRun> runs, bool on_device,
+                      std::span<float> logits, std::string* error) {
   try {
-    for (size_t first = 0; first < tokens.size(); first += kPrefillChunk) {
-      const auto chunk = tokens.subspan(
-          first, std::min(kPrefillChunk, tokens.size() - first));
-      const bool last = first + chunk.size() == tokens.size();
+    if (hooks_)
+      hooks_->BeforeWrite(position_, position_ + uint32_t(ids.size()));
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+  const auto& c = model_->config();
+  try {
+    for (size_t first = 0; first < ids.size(); first += kPrefillChunk) {
+      const auto chunk =
+          ids.subspan(first, std::min(kPrefillChunk, ids.size() - first));
+      const bool last = first + chunk.size() == ids.size();
+      // the embedding runs inside this chunk, relative to its first row
+      std::vector<RowRun> in_chunk;
+      for (const RowRun& run : runs) {
+        const size_t a = std::max(run.first, first);
+        const size_t b = std::min(run.first + run.count, first + chunk.size());
+        if (a < b)
+          in_chunk.push_back(
+              {a - first, b - a, run.data + (a - run.first) * c.hidden});
+      }
       if (chunk.size() == 1) {
         Session* self = this;
-        DecodeRound({&self, 1}, chunk, last && !logits.empty());
+        const float* row = in_chunk.empty() ? nullptr : in_chunk[0].data;
+        DecodeRound({&self, 1}, chunk, last && !logits.empty(), &row,
+                    !on_device);
       } else {
-        Prompt(chunk, last && !logits.empty());
+        Prompt(chunk, last && !logits.empty(), in_chunk, on_device);
       }
       // the chunks queue back to back; the last one (every one when
       // profiling) is waited for and its device waits checked
@@ -944,6 +995,64 @@ bool Session::Forward(std::span<const uint32_t> tokens, std::span<float> logits,
   }
 }
 
+bool Session::ForwardEmbeddings(std::span<const float> rows, bool on_device,
+                                std::span<float> logits, std::string* error) {
+  const auto& c = model_->config();
+  const size_t n = rows.size() / c.hidden;
+  try {
+    if (poisoned_)
+      throw std::runtime_error("session is poisoned; Reset it first");
+    if (!logits.empty() && logits.size() != c.vocab)
+      throw std::invalid_argument("logits must hold vocab floats");
+    if (!n || rows.size() % c.hidden || !rows.data())
+      throw std::invalid_argument("embedding rows must be hidden floats each");
+    if (size_t(position_) + n > context_)
+      throw std::invalid_argument("LFM3 context overflow");
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+  const std::vector<uint32_t> ids(n, 0);
+  const RowRun all{0, n, rows.data()};
+  return Advance(ids, {&all, 1}, on_device, logits, error);
+}
+
+bool Session::ForwardInputs(std::span<const Input> inputs,
+                            std::span<float> logits, std::string* error) {
+  const auto& c = model_->config();
+  std::vector<uint32_t> ids;
+  std::vector<RowRun> runs;
+  try {
+    if (poisoned_)
+      throw std::runtime_error("session is poisoned; Reset it first");
+    if (!logits.empty() && logits.size() != c.vocab)
+      throw std::invalid_argument("logits must hold vocab floats");
+    for (const Input& in : inputs) {
+      if (!in.tokens.empty() && !in.rows.empty())
+        throw std::invalid_argument("an input run holds tokens or rows");
+      for (uint32_t t : in.tokens)
+        if (t >= c.vocab)
+          throw std::invalid_argument("invalid LFM3 token");
+      if (in.rows.size() % c.hidden)
+        throw std::invalid_argument("embedding rows must be hidden floats each");
+      if (!in.rows.empty())
+        runs.push_back({ids.size(), in.rows.size() / c.hidden, in.rows.data()});
+      ids.insert(ids.end(), in.tokens.begin(), in.tokens.end());
+      ids.resize(ids.size() + in.rows.size() / c.hidden, 0);
+    }
+    if (ids.empty())
+      throw std::invalid_argument("no inputs");
+    if (size_t(position_) + ids.size() > context_)
+      throw std::invalid_argument("LFM3 context overflow");
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+  return Advance(ids, runs, false, logits, error);
+}
+
 bool Session::ForwardBatch(std::span<Session* const> sessions,
                            std::span<const uint32_t> tokens,
                            std::span<const std::span<float>> logits,
@@ -957,10 +1066,21 @@ bool Session::ForwardBatchInputs(std::span<Session* const> sessions,
   return Batch(sessions, tokens, {}, logits, error);
 }
 
+bool Session::ForwardBatchInputs(std::span<Session* const> sessions,
+                                 std::span<const uint32_t> tokens,
+                                 std::span<const float* const> rows,
+                                 bool logits, std::string* error) {
+  return Batch(sessions, tokens, {}, logits, error, rows);
+}
+
 bool Session::Batch(std::span<Session* const> sessions,
                     std::span<const uint32_t> tokens,
                     std::span<const std::span<float>> logits,
-                    bool device_logits, std::string* error) {
+                    bool device_logits, std::string* error,
+                    std::span<const float* const> rows) {
+  // an embedding row stands in for its session's token
+  const auto embedded = [&](size_t r) { return r < rows.size() && rows[r]; };
+  uint32_t ids[kMaxBatch] = {};
   // every check before any mutation (engine.cpp:1178-1199)
   try {
     if (sessions.empty() || sessions.size() > kMaxBatch)
@@ -980,12 +1100,18 @@ bool Session::Batch(std::span<Session* const> sessions,
         throw std::runtime_error("batch session is poisoned");
       if (s->position_ >= s->context_)
         throw std::invalid_argument("LFM3 context overflow");
-      if (tokens[r] >= model->config().vocab)
+      if (!embedded(r) && tokens[r] >= model->config().vocab)
         throw std::invalid_argument("invalid LFM3 token");
+      ids[r] = embedded(r) ? 0 : tokens[r];
       if (!logits.empty() && !logits[r].empty() &&
           logits[r].size() != model->config().vocab)
         throw std::invalid_argument("logits must hold vocab floats");
     }
+    if (!rows.empty() && rows.size() != sessions.size())
+      throw std::invalid_argument("one input row (or null) per session");
+    for (Session* s : sessions)
+      if (s->hooks_)
+        s->hooks_->BeforeWrite(s->position_, s->position_ + 1);
   } catch (const std::exception& e) {
     if (error)
       *error = e.what();
@@ -1003,7 +1129,8 @@ bool Session::Batch(std::span<Session* const> sessions,
         front->Check(cudaEventRecord(s->ready_, s->stream_));
         front->Check(cudaStreamWaitEvent(front->stream_, s->ready_, 0));
       }
-    front->DecodeRound(sessions, tokens, want);
+    front->DecodeRound(sessions, std::span<const uint32_t>(ids, sessions.size()),
+                       want, rows.empty() ? nullptr : rows.data());
     // logits spans that are consecutive rows of one block take one copy of
     // the round's logits; otherwise one copy per session
     bool block = !logits.empty();
@@ -1165,6 +1292,8 @@ bool Session::ReadLogits(std::span<float> logits, std::string* error) {
 
 bool Session::Reset(std::string* error) {
   try {
+    if (hooks_)
+      hooks_->BeforeReset();
     Throw(cudaStreamSynchronize(stream_));
     const auto& c = model_->config();
     for (size_t i = 0; i < states_.size(); ++i)
@@ -1183,6 +1312,50 @@ bool Session::Reset(std::string* error) {
       *error = e.what();
     return false;
   }
+}
+
+bool Session::PrepareLogits(std::string* error) {
+  try {
+    if (poisoned_)
+      throw std::runtime_error("session is poisoned; Reset it first");
+    if (!position_)
+      throw std::invalid_argument("no row advanced yet");
+    EnsureLogits();
+    return true;
+  } catch (const std::exception& e) {
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::BeginRestore(std::string* error) {
+  // engine.cpp:1374-1379: queued work ends before the adapter writes the
+  // state; the session stays incoherent until FinishRestore
+  try {
+    Throw(cudaStreamSynchronize(stream_));
+    poisoned_ = true;
+    return true;
+  } catch (const std::exception& e) {
+    poisoned_ = true;
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
+bool Session::FinishRestore(uint32_t position, std::string* error) {
+  // engine.cpp:1380-1386: the adapter wrote frontier, logits and every
+  // layer's state for `position` rows
+  if (position > context_) {
+    if (error)
+      *error = "restored position exceeds the session context";
+    return false;
+  }
+  position_ = position;
+  logits_ready_ = true;
+  poisoned_ = false;
+  return true;
 }
 
 void* Session::ContinuationData(ContinuationTensor tensor, size_t layer) const {
@@ -1303,6 +1476,8 @@ bool Session::RestoreSnapshot(std::span<const uint8_t> payload,
                               std::string* error) {
   const auto& c = model_->config();
   try {
+    if (hooks_)
+      hooks_->BeforeRestore();
     // nothing queued may still write this session's state
     Throw(cudaStreamSynchronize(stream_));
     if (payload.size() < kSnapshotHeaderBytes)

@@ -23,6 +23,18 @@ namespace lfm3 {
 
 class Session;
 
+// Installed by the continuation (component cache) adapter
+// (continuation_hooks.hpp:5-16): every callback runs on the host before the
+// session changes state or submits device work, and may throw to refuse it.
+class ContinuationHooks {
+public:
+  virtual ~ContinuationHooks() = default;
+  // Rows [first, end) are about to be written.
+  virtual void BeforeWrite(uint32_t first, uint32_t end) = 0;
+  virtual void BeforeReset() = 0;
+  virtual void BeforeRestore() = 0;
+};
+
 // Owns one device allocation.
 class DeviceBuffer {
 public:
@@ -128,6 +140,42 @@ public:
   static bool ForwardBatchInputs(std::span<Session* const> sessions,
                                  std::span<const uint32_t> tokens, bool logits,
                                  std::string* error = nullptr);
+  // The same with input embeddings: rows[i], when set, is session i's input
+  // row (hidden floats in device memory, ready in this call's stream order),
+  // otherwise tokens[i] is (engine.hpp:107-114).
+  static bool ForwardBatchInputs(std::span<Session* const> sessions,
+                                 std::span<const uint32_t> tokens,
+                                 std::span<const float* const> rows,
+                                 bool logits, std::string* error = nullptr);
+  // Advances rows of input embeddings (hidden floats each) instead of token
+  // ids: host memory, or device memory read in this session's stream order
+  // when on_device (engine.hpp:115-120).
+  bool ForwardEmbeddings(std::span<const float> rows, bool on_device = false,
+                         std::span<float> logits = {},
+                         std::string* error = nullptr);
+  // A run of token ids or of host embedding rows (engine.hpp:121-125).
+  struct Input {
+    std::span<const uint32_t> tokens;
+    std::span<const float> rows;
+  };
+  // Advances runs in order; adjacent runs share their passes, so a prompt
+  // mixing text and embeddings reads the weights once per 512 rows
+  // (engine.hpp:126-131).
+  bool ForwardInputs(std::span<const Input> inputs,
+                     std::span<float> logits = {},
+                     std::string* error = nullptr);
+  // The reference starts an NPU decode early; on the GPU there is nothing to
+  // start before the token is advanced (engine.hpp:71-73).
+  void Speculate(uint32_t) {}
+  // Continuation components (engine.hpp:144-158): the hooks (not owned; null
+  // removes them), the frontier's logits completed on this session's stream,
+  // and a restore by direct writes to ContinuationData between BeginRestore
+  // (waits for queued work, marks the session incoherent) and
+  // FinishRestore(position).
+  void SetContinuationHooks(ContinuationHooks* hooks) { hooks_ = hooks; }
+  bool PrepareLogits(std::string* error = nullptr);
+  bool BeginRestore(std::string* error = nullptr);
+  bool FinishRestore(uint32_t position, std::string* error = nullptr);
   // A round followed by token selection on the device (sampling.cuh): the
   // runner's AdvanceBatch + SelectNext (runner.cpp:268-351) without the
   // logits' trip to the host. next[i] is the token selected from session
@@ -185,21 +233,37 @@ public:
 private:
   Session(std::shared_ptr<Model> model, uint32_t context);
   void Check(cudaError_t status);
-  void Prompt(std::span<const uint32_t> tokens, bool logits);
+  // Rows [first, first + count) of a pass taken from input embeddings.
+  struct RowRun {
+    size_t first, count;
+    const float* data;
+  };
+  // Validated rows: ids (any valid id where a run supplies the row) and the
+  // runs of embedding rows (host, or device when on_device).
+  bool Advance(std::span<const uint32_t> ids, std::span<const RowRun> runs,
+               bool on_device, std::span<float> logits, std::string* error);
+  void Prompt(std::span<const uint32_t> tokens, bool logits,
+              std::span<const RowRun> runs = {}, bool on_device = false);
+  // rows[r], when set, replaces row r's token (hidden floats, device memory
+  // unless rows_on_host)
   void DecodeRound(std::span<Session* const> batch,
-                   std::span<const uint32_t> tokens, bool logits);
+                   std::span<const uint32_t> tokens, bool logits,
+                   const float* const* rows = nullptr,
+                   bool rows_on_host = false);
   void EnsureLogits();
   void Settle();
   static bool Batch(std::span<Session* const> sessions,
                     std::span<const uint32_t> tokens,
                     std::span<const std::span<float>> logits,
-                    bool device_logits, std::string* error);
+                    bool device_logits, std::string* error,
+                    std::span<const float* const> rows = {});
   void LaunchLmHead(const void* split_rows, int rows, float* out);
 
   std::shared_ptr<Model> model_;
   cudaStream_t stream_ = nullptr;
   uint32_t context_ = 0, position_ = 0;
   bool poisoned_ = false, logits_ready_ = false;
+  ContinuationHooks* hooks_ = nullptr;
   int inject_after_ = 0;
   struct State {
     DeviceBuffer conv, k, v;
