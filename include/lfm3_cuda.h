@@ -191,6 +191,31 @@ int lfm3_cuda_pack_kv(const float* k, const float* v, uint16_t* k16,
 int lfm3_cuda_select_rows(const lfm3_tensor* source, const uint32_t* rows,
                           void* out, int count, void* stream);
 
+/* SharesSplit (hip/ops.hpp:41-43): 1 when these projections of n rows read
+ * one FP16 prompt input (n >= kPromptRows, Q8_0 weights of one width and a
+ * workspace to hold it), else 0. Host only. */
+int lfm3_cuda_shares_split(const lfm3_output* outputs, int count, int n,
+                           const lfm3_dense_workspace* workspace);
+/* LaunchBatchedResidualAdd (hip/ops.hpp:156-158): out = a + b over batch x
+ * dim floats (out may be a); dim a multiple of 8, at most 8192. */
+int lfm3_cuda_batched_residual_add(const float* a, const float* b, float* out,
+                                   size_t batch, size_t dim, void* stream);
+/* LaunchGEMV (hip/ops.hpp:163-164), LaunchBatchedQuantGEMMFp32
+ * (hip/ops.hpp:165-168) and LaunchExactBf16GEMMFp32SmallBatch
+ * (hip/ops.hpp:169-171): y[r] = W x[r] for rows of FP32 x ([rows][K]) and a
+ * [M][K] matrix (Q8_0 with K a multiple of 512, or BF16 with K a multiple
+ * of 256), the results of lfm3_cuda_dense. They take no workspace: the Q8_0
+ * input conversion uses stream-ordered memory (cudaMallocAsync /
+ * cudaFreeAsync on `stream`). */
+int lfm3_cuda_gemv(const void* A, uint32_t a_type, const float* x, float* y,
+                   size_t M, size_t K, void* stream);
+int lfm3_cuda_batched_quant_gemm_fp32(uint32_t type, const void* w,
+                                      const float* x, float* y, size_t batch,
+                                      size_t m, size_t k, void* stream);
+int lfm3_cuda_exact_bf16_gemm_fp32_small_batch(const void* A, const float* X,
+                                               float* Y, size_t batch, size_t M,
+                                               size_t K, void* stream);
+
 /* LaunchBatchedRMSNorm (hip/ops.hpp:148-150): out = x * rsqrt(mean x^2 +
  * eps) * weight per row (bf16 output not supported: out_bf16 must be NULL). */
 int lfm3_cuda_batched_rmsnorm(const float* x, const float* weight, float* out,

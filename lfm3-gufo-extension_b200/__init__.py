@@ -102,6 +102,11 @@ def library():
         "lfm3_session_prepare_logits": ([P], I),
         "lfm3_session_begin_restore": ([P], I),
         "lfm3_session_finish_restore": ([P, U32], I),
+        "lfm3_cuda_shares_split": ([P, I, I, P], I),
+        "lfm3_cuda_batched_residual_add": ([P, P, P, SZ, SZ, P], I),
+        "lfm3_cuda_gemv": ([P, U32, P, P, SZ, SZ, P], I),
+        "lfm3_cuda_batched_quant_gemm_fp32": ([U32, P, P, P, SZ, SZ, SZ, P], I),
+        "lfm3_cuda_exact_bf16_gemm_fp32_small_batch": ([P, P, P, SZ, SZ, SZ, P], I),
         "lfm3_cuda_sample_scratch_bytes": ([I, I, I], SZ),
         "lfm3_cuda_sample": ([P, I, I, I, ctypes.POINTER(abi.Sampler), P, P,
                               P, P, P, P], I),

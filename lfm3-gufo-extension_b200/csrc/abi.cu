@@ -507,6 +507,93 @@ int lfm3_cuda_batched_rmsnorm(const float* x, const float* weight, float* out,
       Stream(stream), false));
 }
 
+// ---- launch-level operators ---------------------------------------------------------
+namespace {
+
+// One matrix times rows of FP32 x through the Dense path, with the Q8_0
+// input workspace in stream-ordered memory.
+int MatrixRows(const void* w, uint32_t type, const float* x, float* y,
+               size_t rows, size_t M, size_t K, cudaStream_t s) {
+  if (!w || !x || !y || !rows || !M || !K || rows > size_t(1) << 24 ||
+      M > UINT32_MAX || K > UINT32_MAX)
+    return Fail(LFM3_ERR_INVALID, "invalid matrix arguments");
+  const size_t row_bytes =
+      type == LFM3_Q8_0 ? K / 32 * 34 : type == LFM3_BF16 ? K * 2 : 0;
+  if (!row_bytes)
+    return Fail(LFM3_ERR_UNSUPPORTED, "matrices must be Q8_0 or BF16");
+  const lfm3_tensor t{w, type, uint32_t(K), uint32_t(M), M * row_bytes};
+  const lfm3_output o{&t, y};
+  lfm3_dense_workspace ws{};
+  if (type == LFM3_BF16 && !Bf16Matrix(&t))
+    return Fail(LFM3_ERR_UNSUPPORTED, "BF16 width must be a multiple of 256");
+  if (type == LFM3_Q8_0) {
+    if (!Q8Matrix(&t))
+      return Fail(LFM3_ERR_UNSUPPORTED, "Q8_0 width must be a multiple of 512");
+    if (const int e = Cuda(cudaMallocAsync(
+            &ws.quantized, lfm3_cuda_dense_workspace_bytes(rows, K), s)))
+      return e;
+  }
+  int rc = ProjectImpl(&o, 1, x, int(rows), s, &ws, false);
+  if (ws.quantized) {
+    const int e = Cuda(cudaFreeAsync(ws.quantized, s));
+    if (rc == LFM3_OK)
+      rc = e;
+  }
+  return rc;
+}
+
+}  // namespace
+
+int lfm3_cuda_shares_split(const lfm3_output* outputs, int count, int n,
+                           const lfm3_dense_workspace* workspace) {
+  if (!outputs || count < 1 || count > 4 || n < kPromptRows || !workspace ||
+      !workspace->quantized)
+    return 0;
+  for (int j = 0; j < count; ++j)
+    if (!Q8Matrix(outputs[j].weight) ||
+        outputs[j].weight->cols != outputs[0].weight->cols)
+      return 0;
+  return 1;
+}
+
+int lfm3_cuda_batched_residual_add(const float* a, const float* b, float* out,
+                                   size_t batch, size_t dim, void* stream) {
+  if (!a || !b || !out)
+    return Fail(LFM3_ERR_INVALID, "null argument");
+  if (dim % 8 || dim > 8192 || batch > size_t(INT32_MAX))
+    return Fail(LFM3_ERR_UNSUPPORTED, "residual add width must be a multiple of 8, <= 8192");
+  if (!batch || !dim)
+    return LFM3_OK;
+  if (out != a)
+    if (const int e = Cuda(cudaMemcpyAsync(out, a, batch * dim * 4,
+                                           cudaMemcpyDeviceToDevice,
+                                           Stream(stream))))
+      return e;
+  // the residual-norm kernel's plain add (no branch norm, no output norm)
+  return Cuda(lfm3::launch_residual_norm(b, nullptr, out, nullptr,
+                                         lfm3::NormOut{}, int(batch), int(dim),
+                                         0.0F, Stream(stream), false));
+}
+
+int lfm3_cuda_gemv(const void* A, uint32_t a_type, const float* x, float* y,
+                   size_t M, size_t K, void* stream) {
+  return MatrixRows(A, a_type, x, y, 1, M, K, Stream(stream));
+}
+
+int lfm3_cuda_batched_quant_gemm_fp32(uint32_t type, const void* w,
+                                      const float* x, float* y, size_t batch,
+                                      size_t m, size_t k, void* stream) {
+  if (type != LFM3_Q8_0)
+    return Fail(LFM3_ERR_UNSUPPORTED, "quantized matrices must be Q8_0");
+  return MatrixRows(w, type, x, y, batch, m, k, Stream(stream));
+}
+
+int lfm3_cuda_exact_bf16_gemm_fp32_small_batch(const void* A, const float* X,
+                                               float* Y, size_t batch, size_t M,
+                                               size_t K, void* stream) {
+  return MatrixRows(A, LFM3_BF16, X, Y, batch, M, K, Stream(stream));
+}
+
 // ---- token selection ------------------------------------------------------------
 namespace {
 
