@@ -193,6 +193,58 @@ __global__ void copy_rows_kernel(const unsigned char* source,
     out[row * bytes + i] = source[size_t(rows[row]) * bytes + i];
 }
 
+// One matrix times rows of FP32 x through the Dense path, with the Q8_0
+// input workspace in stream-ordered memory.
+int MatrixRows(const void* w, uint32_t type, const float* x, float* y,
+               size_t rows, size_t M, size_t K, cudaStream_t s) {
+  if (!w || !x || !y || !rows || !M || !K || rows > size_t(1) << 24 ||
+      M > UINT32_MAX || K > UINT32_MAX)
+    return Fail(LFM3_ERR_INVALID, "invalid matrix arguments");
+  const size_t row_bytes =
+      type == LFM3_Q8_0 ? K / 32 * 34 : type == LFM3_BF16 ? K * 2 : 0;
+  if (!row_bytes)
+    return Fail(LFM3_ERR_UNSUPPORTED, "matrices must be Q8_0 or BF16");
+  const lfm3_tensor t{w, type, uint32_t(K), uint32_t(M), M * row_bytes};
+  const lfm3_output o{&t, y};
+  lfm3_dense_workspace ws{};
+  if (type == LFM3_BF16 && !Bf16Matrix(&t))
+    return Fail(LFM3_ERR_UNSUPPORTED, "BF16 width must be a multiple of 256");
+  if (type == LFM3_Q8_0) {
+    if (!Q8Matrix(&t))
+      return Fail(LFM3_ERR_UNSUPPORTED, "Q8_0 width must be a multiple of 512");
+    if (const int e = Cuda(cudaMallocAsync(
+            &ws.quantized, lfm3_cuda_dense_workspace_bytes(rows, K), s)))
+      return e;
+  }
+  int rc = ProjectImpl(&o, 1, x, int(rows), s, &ws, false);
+  if (ws.quantized) {
+    const int e = Cuda(cudaFreeAsync(ws.quantized, s));
+    if (rc == LFM3_OK)
+      rc = e;
+  }
+  return rc;
+}
+
+// Controls and per-row tables checked for `rows` rows of `vocab` logits.
+int SampleArgs(const lfm3_sampler* sampler, int rows, int vocab,
+               const uint32_t* recent, const uint32_t* recent_count,
+               const uint64_t* seeds, lfm3::SampleControls* c) {
+  if (!sampler || rows < 1 || !recent_count || !seeds || !recent)
+    return Fail(LFM3_ERR_INVALID, "sampler, rows and row tables required");
+  if (const char* why = lfm3::sample_controls(
+          sampler->temperature, sampler->top_k, sampler->repeat_penalty,
+          vocab, c))
+    return Fail(LFM3_ERR_INVALID, why);
+  for (int r = 0; r < rows; ++r) {
+    if (recent_count[r] > uint32_t(lfm3::kSampleMaxRecent))
+      return Fail(LFM3_ERR_INVALID, "more than 64 recent tokens in a row");
+    for (uint32_t j = 0; j < recent_count[r]; ++j)
+      if (recent[size_t(r) * lfm3::kSampleMaxRecent + j] >= uint32_t(vocab))
+        return Fail(LFM3_ERR_INVALID, "recent token outside the vocabulary");
+  }
+  return LFM3_OK;
+}
+
 }  // namespace
 
 int lfm3::set_last_error(int code, const char* message) {
@@ -508,42 +560,6 @@ int lfm3_cuda_batched_rmsnorm(const float* x, const float* weight, float* out,
 }
 
 // ---- launch-level operators ---------------------------------------------------------
-namespace {
-
-// One matrix times rows of FP32 x through the Dense path, with the Q8_0
-// input workspace in stream-ordered memory.
-int MatrixRows(const void* w, uint32_t type, const float* x, float* y,
-               size_t rows, size_t M, size_t K, cudaStream_t s) {
-  if (!w || !x || !y || !rows || !M || !K || rows > size_t(1) << 24 ||
-      M > UINT32_MAX || K > UINT32_MAX)
-    return Fail(LFM3_ERR_INVALID, "invalid matrix arguments");
-  const size_t row_bytes =
-      type == LFM3_Q8_0 ? K / 32 * 34 : type == LFM3_BF16 ? K * 2 : 0;
-  if (!row_bytes)
-    return Fail(LFM3_ERR_UNSUPPORTED, "matrices must be Q8_0 or BF16");
-  const lfm3_tensor t{w, type, uint32_t(K), uint32_t(M), M * row_bytes};
-  const lfm3_output o{&t, y};
-  lfm3_dense_workspace ws{};
-  if (type == LFM3_BF16 && !Bf16Matrix(&t))
-    return Fail(LFM3_ERR_UNSUPPORTED, "BF16 width must be a multiple of 256");
-  if (type == LFM3_Q8_0) {
-    if (!Q8Matrix(&t))
-      return Fail(LFM3_ERR_UNSUPPORTED, "Q8_0 width must be a multiple of 512");
-    if (const int e = Cuda(cudaMallocAsync(
-            &ws.quantized, lfm3_cuda_dense_workspace_bytes(rows, K), s)))
-      return e;
-  }
-  int rc = ProjectImpl(&o, 1, x, int(rows), s, &ws, false);
-  if (ws.quantized) {
-    const int e = Cuda(cudaFreeAsync(ws.quantized, s));
-    if (rc == LFM3_OK)
-      rc = e;
-  }
-  return rc;
-}
-
-}  // namespace
-
 int lfm3_cuda_shares_split(const lfm3_output* outputs, int count, int n,
                            const lfm3_dense_workspace* workspace) {
   if (!outputs || count < 1 || count > 4 || n < kPromptRows || !workspace ||
@@ -595,30 +611,6 @@ int lfm3_cuda_exact_bf16_gemm_fp32_small_batch(const void* A, const float* X,
 }
 
 // ---- token selection ------------------------------------------------------------
-namespace {
-
-// Controls and per-row tables checked for `rows` rows of `vocab` logits.
-int SampleArgs(const lfm3_sampler* sampler, int rows, int vocab,
-               const uint32_t* recent, const uint32_t* recent_count,
-               const uint64_t* seeds, lfm3::SampleControls* c) {
-  if (!sampler || rows < 1 || !recent_count || !seeds || !recent)
-    return Fail(LFM3_ERR_INVALID, "sampler, rows and row tables required");
-  if (const char* why = lfm3::sample_controls(
-          sampler->temperature, sampler->top_k, sampler->repeat_penalty,
-          vocab, c))
-    return Fail(LFM3_ERR_INVALID, why);
-  for (int r = 0; r < rows; ++r) {
-    if (recent_count[r] > uint32_t(lfm3::kSampleMaxRecent))
-      return Fail(LFM3_ERR_INVALID, "more than 64 recent tokens in a row");
-    for (uint32_t j = 0; j < recent_count[r]; ++j)
-      if (recent[size_t(r) * lfm3::kSampleMaxRecent + j] >= uint32_t(vocab))
-        return Fail(LFM3_ERR_INVALID, "recent token outside the vocabulary");
-  }
-  return LFM3_OK;
-}
-
-}  // namespace
-
 size_t lfm3_cuda_sample_scratch_bytes(int rows, int vocab, int top_k) {
   if (rows < 1 || vocab < 1 || top_k < 1)
     return 0;
