@@ -531,15 +531,10 @@ cudaError_t launch_group(const DecodeAttentionParams& p, int rows,
   const int spans = p.span_grid > 0 && p.span_grid < kMaxDecodeSplits
                         ? p.span_grid
                         : kMaxDecodeSplits;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        decode_attention_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        int(sizeof(DecodeSmem)));
-    if (e != cudaSuccess)
-      return e;
-    configured = true;
-  }
+  if (const cudaError_t e = ensure_dynamic_smem(
+          reinterpret_cast<const void*>(decode_attention_kernel<G>),
+          int(sizeof(DecodeSmem))))
+    return e;
   config.gridDim = dim3(p.kv_heads, spans, rows);
   config.blockDim = dim3(kThreads);
   config.dynamicSmemBytes = sizeof(DecodeSmem);

@@ -429,19 +429,15 @@ cudaError_t launch_prompt_attention(const float* q, int ldq, const __half* k16,
     return cudaErrorInvalidValue;
   const dim3 grid((n + kQ - 1) / kQ, kv_heads, a.spans);
   constexpr int kSmem = 4 * kKeys * 256;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(prompt_attention_kernel<2>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    cudaFuncSetAttribute(prompt_attention_kernel<4>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    cudaFuncSetAttribute(prompt_attention_kernel<8>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    configured = true;
-  }
   const int group = heads / kv_heads;
   if (group != 2 && group != 4 && group != 8)
     return cudaErrorInvalidValue;
+  for (const void* kernel :
+       {reinterpret_cast<const void*>(prompt_attention_kernel<2>),
+        reinterpret_cast<const void*>(prompt_attention_kernel<4>),
+        reinterpret_cast<const void*>(prompt_attention_kernel<8>)})
+    if (const cudaError_t e = ensure_dynamic_smem(kernel, kSmem))
+      return e;
   cudaError_t e = launch_kernel(
       group == 2   ? prompt_attention_kernel<2>
       : group == 4 ? prompt_attention_kernel<4>

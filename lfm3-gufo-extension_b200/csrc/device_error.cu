@@ -3,6 +3,9 @@
 #include "kernels.cuh"
 
 #include <atomic>
+#include <mutex>
+#include <set>
+#include <tuple>
 
 namespace lfm3 {
 
@@ -13,6 +16,23 @@ std::atomic<unsigned long long> g_launches{0};
 }
 void note_launch(int kernels) { g_launches += kernels; }
 unsigned long long launch_count() { return g_launches.load(); }
+
+cudaError_t ensure_dynamic_smem(const void* kernel, int bytes) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess)
+    return e;
+  static std::mutex mutex;
+  static std::set<std::tuple<const void*, int, int>> done;
+  const std::lock_guard<std::mutex> lock(mutex);
+  if (done.count({kernel, device, bytes}))
+    return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           bytes);
+  if (e == cudaSuccess)
+    done.insert({kernel, device, bytes});
+  return e;
+}
 
 namespace {
 // One thread waits on an mbarrier that nothing arrives at: the bounded wait

@@ -24,6 +24,11 @@ cudaError_t launch_wait_probe(uint64_t limit_ns, cudaStream_t stream);
 // Records the message lfm3_last_error() returns on this thread; returns code.
 int set_last_error(int code, const char* message);
 
+// Raises a kernel's dynamic shared memory limit to `bytes` on the current
+// device, once per (kernel, device, bytes): function attributes belong to
+// each device's context. Thread-safe.
+cudaError_t ensure_dynamic_smem(const void* kernel, int bytes);
+
 // Process-wide count of kernels this library has launched.
 void note_launch(int kernels = 1);
 unsigned long long launch_count();

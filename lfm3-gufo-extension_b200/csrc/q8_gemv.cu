@@ -657,15 +657,9 @@ cudaError_t launch_bf16_gemv(const GemvParams& p, const float* x32, int x_ld,
 
 cudaError_t launch_q8_gemv(const GemvParams& p, int grid, cudaStream_t stream,
                            bool pdl) {
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        q8_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        int(sizeof(GemvSmem)));
-    if (e != cudaSuccess)
-      return e;
-    configured = true;
-  }
+  if (const cudaError_t e = ensure_dynamic_smem(
+          reinterpret_cast<const void*>(q8_gemv_kernel), int(sizeof(GemvSmem))))
+    return e;
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(grid);
   config.blockDim = dim3(kGemvThreads);

@@ -555,16 +555,10 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
     return e;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   const int smem = int(sizeof(PrefillSmem)) + 1024;
-  static bool configured[64] = {};
-  if (device < 0 || device >= 64)
-    return cudaErrorInvalidDevice;
-  if (!configured[device]) {
-    e = cudaFuncSetAttribute(q8_prefill_tc_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess)
-      return e;
-    configured[device] = true;
-  }
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(q8_prefill_tc_kernel),
+                          smem);
+  if (e != cudaSuccess)
+    return e;
   if (p.K <= 0 || p.K % 256 || p.tokens <= 0 || !x || !p.scale ||
       x_rows < p.x_row0 + p.tokens)
     return cudaErrorInvalidValue;
