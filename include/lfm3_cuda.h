@@ -90,21 +90,27 @@ typedef struct lfm3_output {
 } lfm3_output;
 
 /* Project (hip/ops.hpp:46-48): up to four weights with the same column
- * count read one input. */
+ * count read one input. split_ready (hip/ops.hpp:44-45): the workspace
+ * already holds this input as FP16 prompt activations (written by
+ * lfm3_cuda_residual_norm with split set, for the same n rows and width), so
+ * x is not read; it applies to Q8_0 prompt rows (n >= kPromptRows) and is
+ * ignored otherwise. */
 int lfm3_cuda_project(const lfm3_output* outputs, int count, const float* x,
                       int n, void* stream,
-                      const lfm3_dense_workspace* workspace);
+                      const lfm3_dense_workspace* workspace, int split_ready);
 /* ProjectSwiGLU (hip/ops.hpp:51-53): out = silu(gate x) * (up x). */
 int lfm3_cuda_project_swiglu(const lfm3_tensor* gate, const lfm3_tensor* up,
                              const float* x, float* out, float* up_scratch,
                              int n, void* stream,
-                             const lfm3_dense_workspace* workspace);
+                             const lfm3_dense_workspace* workspace,
+                             int split_ready);
 /* ProjectFfn (hip/ops.hpp:55-58): out = down(silu(gate x) * (up x)), the
- * activation left in hidden. */
+ * activation left in hidden; split_ready applies to the gate/up input. */
 int lfm3_cuda_project_ffn(const lfm3_tensor* gate, const lfm3_tensor* up,
                           const lfm3_tensor* down, const float* x,
                           float* hidden, float* up_scratch, float* out, int n,
-                          void* stream, const lfm3_dense_workspace* workspace);
+                          void* stream, const lfm3_dense_workspace* workspace,
+                          int split_ready);
 
 /* ResidualNorm (hip/ops.hpp:62-65): x += post_norm(branch) (branch and
  * post_norm may be NULL), then z = norm(x) unless norm is NULL. With split

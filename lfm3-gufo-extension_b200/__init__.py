@@ -49,9 +49,9 @@ def library():
         "lfm3_cuda_prompt_rows": ([], I),
         "lfm3_cuda_embed": ([P, P, P, I, P], I),
         "lfm3_cuda_dense": ([P, P, P, I, P, P], I),
-        "lfm3_cuda_project": ([P, I, P, I, P, P], I),
-        "lfm3_cuda_project_swiglu": ([P, P, P, P, P, I, P, P], I),
-        "lfm3_cuda_project_ffn": ([P, P, P, P, P, P, P, I, P, P], I),
+        "lfm3_cuda_project": ([P, I, P, I, P, P, I], I),
+        "lfm3_cuda_project_swiglu": ([P, P, P, P, P, I, P, P, I], I),
+        "lfm3_cuda_project_ffn": ([P, P, P, P, P, P, P, I, P, P, I], I),
         "lfm3_cuda_residual_norm": ([P, P, P, P, P, I, I, F, I, P, P], I),
         "lfm3_cuda_short_conv": ([P, P, P, P, I, I, I, P, I], I),
         "lfm3_cuda_rope_frequencies": ([P, I, F, P], I),

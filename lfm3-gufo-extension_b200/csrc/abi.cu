@@ -294,14 +294,15 @@ int lfm3_cuda_dense(const lfm3_tensor* weight, const float* x, float* out,
 
 int lfm3_cuda_project(const lfm3_output* outputs, int count, const float* x,
                       int n, void* stream,
-                      const lfm3_dense_workspace* workspace) {
-  return ProjectImpl(outputs, count, x, n, Stream(stream), workspace, false);
+                      const lfm3_dense_workspace* workspace, int split_ready) {
+  return ProjectImpl(outputs, count, x, n, Stream(stream), workspace,
+                     split_ready != 0);
 }
 
 int lfm3_cuda_project_swiglu(const lfm3_tensor* gate, const lfm3_tensor* up,
                              const float* x, float* out, float* up_scratch,
                              int n, void* stream,
-                             const lfm3_dense_workspace* ws) {
+                             const lfm3_dense_workspace* ws, int split_ready) {
   (void)up_scratch;  // the fused kernels keep up x in registers
   const bool bf16 = Bf16Matrix(gate) && Bf16Matrix(up);
   if (!(bf16 || (Q8Matrix(gate) && Q8Matrix(up))) || gate->rows != up->rows ||
@@ -341,18 +342,19 @@ int lfm3_cuda_project_swiglu(const lfm3_tensor* gate, const lfm3_tensor* up,
             int(gate->rows)};
   p.o[1] = {static_cast<const uint8_t*>(up->data), nullptr, int(up->rows), 0};
   p.row_max = ws->row_max;
-  return PrefillRows(p, x, n, K, *ws, s, false);
+  return PrefillRows(p, x, n, K, *ws, s, split_ready != 0);
 }
 
 int lfm3_cuda_project_ffn(const lfm3_tensor* gate, const lfm3_tensor* up,
                           const lfm3_tensor* down, const float* x,
                           float* hidden, float* up_scratch, float* out, int n,
-                          void* stream, const lfm3_dense_workspace* ws) {
+                          void* stream, const lfm3_dense_workspace* ws,
+                          int split_ready) {
   if (!(Q8Matrix(down) || Bf16Matrix(down)) || !gate ||
       down->cols != gate->rows || down->type != gate->type)
     return Fail(LFM3_ERR_UNSUPPORTED, "invalid FFN down projection");
   if (int e = lfm3_cuda_project_swiglu(gate, up, x, hidden, up_scratch, n,
-                                       stream, ws))
+                                       stream, ws, split_ready))
     return e;
   if (n >= kPromptRows && ws->row_max && down->type == LFM3_Q8_0) {
     // down input from the SwiGLU row maxima (HalfRowsFromMax)

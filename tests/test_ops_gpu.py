@@ -173,7 +173,8 @@ def test_ffn_bf16(n):
     ws, keep2 = workspace(n, F)
     lfm3.check(lib.lfm3_cuda_project_ffn(ctypes.byref(gw), ctypes.byref(uw),
                                          ctypes.byref(dw), ptr(dx), ptr(h), None,
-                                         ptr(out), n, None, ctypes.byref(ws)))
+                                         ptr(out), n, None, ctypes.byref(ws),
+                                         0))
     near(host(h).reshape(n, F), hidden, 2e-5)
     near(host(out).reshape(n, H), expected, 5e-5)
 

@@ -120,3 +120,47 @@ def test_batched_residual_add():
     np.testing.assert_array_equal(out.cpu().numpy(), a + b)
     np.testing.assert_array_equal(ad.cpu().numpy(), a + b)
     assert lib.lfm3_cuda_batched_residual_add(p(ad), p(bd), p(out), 6, 1001, None) == -3
+
+
+class Output(ctypes.Structure):
+    _fields_ = [("weight", ctypes.POINTER(abi.Tensor)), ("out", ctypes.c_void_p)]
+
+
+def test_split_ready_projection():
+    """ResidualNorm with split writes the next projection's FP16 prompt input
+    into the workspace; Project with split_ready reads it from there instead
+    of converting x (hip/ops.hpp:44-48, 59-65) and matches the projection of
+    the FP32 normalised rows."""
+    lib = lfm3.library()
+    rng = np.random.default_rng(9)
+    n, H, M = 32, 512, 256
+    x = rng.standard_normal((n, H)).astype(np.float32)
+    norm_w = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    w = rng.standard_normal((M, H)).astype(np.float32) * 0.05
+    wbuf, nbuf, xd = dev(q8_bytes(w)), dev(norm_w), dev(x)
+    wt = abi.Tensor(wbuf.data_ptr(), abi.Q8_0, H, M, M * (H // 32 * 34))
+    nt = abi.Tensor(nbuf.data_ptr(), abi.F32, H, 1, H * 4)
+    q = torch.empty(lib.lfm3_cuda_dense_workspace_bytes(n, H) // 4 + 1,
+                    dtype=torch.float32, device="cuda")
+    ws = Workspace(q.data_ptr(), None, None, None)
+    z = torch.empty((n, H), dtype=torch.float32, device="cuda")
+    unused = torch.zeros((n, H), dtype=torch.float32, device="cuda")
+    a = torch.empty((n, M), dtype=torch.float32, device="cuda")
+    b = torch.empty((n, M), dtype=torch.float32, device="cuda")
+    # FP32 normalised rows, converted by the projection
+    lfm3.check(lib.lfm3_cuda_residual_norm(None, None, p(xd), ctypes.byref(nt),
+                                           p(z), n, H, 1e-5, 0, None,
+                                           ctypes.byref(ws)))
+    oa = (Output * 1)(Output(ctypes.pointer(wt), a.data_ptr()))
+    lfm3.check(lib.lfm3_cuda_project(oa, 1, p(z), n, None, ctypes.byref(ws), 0))
+    # the norm's FP16 output, read where it was written
+    lfm3.check(lib.lfm3_cuda_residual_norm(None, None, p(xd), ctypes.byref(nt),
+                                           None, n, H, 1e-5, 1, None,
+                                           ctypes.byref(ws)))
+    ob = (Output * 1)(Output(ctypes.pointer(wt), b.data_ptr()))
+    lfm3.check(lib.lfm3_cuda_project(ob, 1, p(unused), n, None,
+                                     ctypes.byref(ws), 1))
+    torch.cuda.synchronize()
+    ra, rb = a.cpu().numpy(), b.cpu().numpy()
+    assert np.isfinite(ra).all() and np.abs(ra).max() > 0.1
+    assert np.abs(ra - rb).max() <= 1e-4
