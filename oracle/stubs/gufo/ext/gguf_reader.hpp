@@ -7,6 +7,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <map>
+#include <memory>
 #include <optional>
 #include <string>
 #include <variant>
@@ -35,6 +36,11 @@ class GgufReader {
 public:
   std::map<std::string, GgufMetadataValue> metadata;
   std::map<std::string, GgufTensorInfo> tensors;
+
+  // Maps a GGUF file (declared for the engine drop-in's link check,
+  // tests/shim/engine_shim_check.cpp, which defines a stand-in).
+  static std::unique_ptr<GgufReader> OpenFile(const std::string& path,
+                                              std::string* error);
 
   const GgufMetadataValue* FindMetadata(const std::string& key) const {
     auto it = metadata.find(key);
