@@ -146,13 +146,39 @@ def test_snapshot_round_trip_and_fork(small):
     np.testing.assert_array_equal(a.read_logits(), before)
     np.testing.assert_array_equal(a.forward(tokens[297:300]),
                                   b.forward(tokens[297:300]))
-    bad = snap.copy()
-    bad[0] ^= 0x80
-    with pytest.raises(lfm3.Lfm3Error):
-        a.restore_snapshot(bad)
+    # every header word is checked (tests/session_test.cpp:200-207)
+    for word in range(8):
+        bad = snap.copy()
+        bad[word * 4] ^= 0x80
+        with pytest.raises(lfm3.Lfm3Error):
+            a.restore_snapshot(bad)
+        assert a.position == 293
     with pytest.raises(lfm3.Lfm3Error):
         a.restore_snapshot(snap[:-1])
     assert a.position == 293
+
+
+def test_intermediate_and_empty_snapshots(small):
+    """A snapshot taken after a prompt pass that computed no logits carries
+    the frontier's logits, and replays like the uninterrupted session; an
+    empty session's snapshot restores to position 0
+    (tests/session_test.cpp:211-223)."""
+    w, model = small
+    rng = np.random.default_rng(3)
+    tokens = rng.integers(0, w.config.vocab, 300).astype(np.uint32)
+    a, b = model.session(512), model.session(512)
+    a.forward(tokens[:257], logits=False)
+    partial = a.save_snapshot()
+    want = b.forward(tokens[:257])
+    np.testing.assert_allclose(a.read_logits(), want, rtol=0, atol=1e-5)
+    a.forward(tokens[:19], logits=False)
+    a.restore_snapshot(partial)
+    np.testing.assert_allclose(a.forward(tokens[257:]), b.forward(tokens[257:]),
+                               rtol=0, atol=1e-5)
+    a.reset()
+    empty = a.save_snapshot()
+    b.restore_snapshot(empty)
+    assert b.position == 0 and b.coherent
 
 
 def test_device_failure_poisons_until_reset(small):
