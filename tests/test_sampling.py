@@ -193,3 +193,17 @@ def test_invalid_tables_refused():
     with pytest.raises(lfm3.Lfm3Error):
         lfm3.sample_host(big, lfm3.sampler(0.5, 64, 1.0))
     assert lfm3.sample_host(big, lfm3.sampler(0.5, 63, 1.0)).shape == (1,)
+
+
+@pytest.mark.parametrize("temperature", [1e-30, 1e-3, 1e30])
+def test_extreme_temperatures_and_infinite_logits(temperature):
+    rng = np.random.default_rng(17)
+    x = (rng.standard_normal((6, 300)) * 4).astype(np.float32)
+    x[0, :] = -np.inf          # every candidate masked
+    x[1, 5] = np.inf           # one unbounded logit
+    x[2, 7] = x[2, 9] = np.inf
+    x[3, ::2] = -np.inf        # half the vocabulary masked
+    seeds = rng.integers(0, 2**63, size=6, dtype=np.uint64)
+    recent = [[1, 2, 3]] * 6
+    for top_k in (1, 7, 64):
+        _check(x, lfm3.sampler(temperature, top_k, 1.3), recent, seeds)
