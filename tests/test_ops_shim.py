@@ -14,7 +14,21 @@ import pytest
 
 from helpers import ROOT, lfm3
 
-REFERENCE = "/root/reference"
+
+
+def _reference_tree():
+    """The reference tree the oracle's Makefile builds from (its REFERENCE
+    variable, overridable from the environment)."""
+    if os.environ.get("REFERENCE"):
+        return os.environ["REFERENCE"]
+    with open(os.path.join(ROOT, "oracle", "Makefile")) as f:
+        for line in f:
+            if line.startswith("REFERENCE ?="):
+                return line.split("?=", 1)[1].strip()
+    return ""
+
+
+REFERENCE = _reference_tree()
 
 
 def test_reference_ops_header_links_against_library(tmp_path):
