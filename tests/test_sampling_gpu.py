@@ -124,3 +124,25 @@ def test_forward_batch_sample_refuses_without_mutation(small):
         lfm3.Session.forward_batch_sample(s, [1, 2], lfm3.sampler(),
                                           recent=[[w.config.vocab], []])
     assert [x.position for x in s] == [3, 3] and all(x.coherent for x in s)
+
+
+def test_device_degenerate_rows():
+    """Rows whose logits are all equal, two-valued, or tied exactly at the
+    top-k boundary: the selection keeps the lowest ids among equals, on the
+    device as on the host."""
+    vocab = 65536
+    x = np.zeros((6, vocab), np.float32)
+    x[1, :] = 1.5
+    x[2, ::2] = -2.0
+    x[3, :] = -1.0
+    x[3, 1000:1064] = 3.0                      # exactly 64 tied maxima
+    x[4, 5::4096] = 7.0                        # one maximum per segment
+    x[5, :] = np.float32(-0.0)
+    x[5, 777] = 0.0                            # +0 above the -0 rows
+    seeds = np.arange(6, dtype=np.uint64) * 12345 + 1
+    for smp in (lfm3.sampler(0.0, 1, 1.0), lfm3.sampler(0.5, 50, 1.0),
+                lfm3.sampler(0.5, 64, 1.1), lfm3.sampler(2.0, 1, 1.0)):
+        recent = [[0, 1, 2]] * 6
+        want = lfm3.sample_host(x, smp, recent=recent, seeds=seeds)
+        got = device_sample(x, smp, recent=recent, seeds=seeds)
+        assert (got == want).all(), (smp.temperature, smp.top_k, got, want)
