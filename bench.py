@@ -165,16 +165,15 @@ def measured_peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def committed_traffic():
-    """dram bytes per q8_gemv launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "q8_gemv_decode.md")
+def committed_traffic(kernel="q8_gemv_decode"):
+    """DRAM bytes (read + write) per launch of a kernel from one ncu capture,
+    kept in profiles/traffic.json beside the summary it comes from."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":")[1])
-    except OSError:
-        pass
-    return None
+        with open(path) as f:
+            return float(json.load(f)[kernel]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
 
 
 # ---- clocks ---------------------------------------------------------------------------
@@ -336,13 +335,40 @@ def cpu_decode_rate(weights, threads, tokens_per_session, warm_steps, prefer_ref
     return threads * tokens_per_session / elapsed, elapsed, kind
 
 
+def cpu_depth_note(cfg, depth, steps):
+    """How much the CPU sample's shallow rows understate the work of the GPU
+    rows (multiply-adds per token: weights plus attention over the keys)."""
+    H, A = cfg.hidden, cfg.heads * 128
+    weights = matrix_elements(cfg)
+
+    def macs(d):
+        keys = 0
+        for i in range(cfg.n_layers):
+            if cfg.layer_type[i] == 1:
+                keys += d + 1
+            elif cfg.layer_type[i] == 2:
+                keys += min(d + 1, cfg.window)
+        return weights + 2 * A * keys
+
+    lengths, _ = rank_workload(0, PROMPT_RANGE[1], cfg.vocab)
+    gpu = float(np.mean([macs(int(n)) for n in lengths]))
+    return (f"CPU rows at depths {depth}..{depth + steps - 1}; the GPU rows (prompts "
+            f"{int(lengths.min())}..{int(lengths.max())} tokens) need "
+            f"{100 * (gpu / macs(depth + steps // 2) - 1):.1f}% more multiply-adds per token "
+            f"(attention over their keys; {H}-wide weights dominate)")
+
+
 def reference_arm(args):
     """The reference's own CPU implementation of the path on this host."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
-    weights = lfm3.SyntheticWeights(seed=0)
+    # weights from the oracle library's copy of the generator: this arm
+    # loads no library of this package (the reference's code and its shim
+    # only, oracle/_ref)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    weights = oracle.SyntheticWeights(seed=0, prefer_reference=True)
     threads = max(1, min(SESSIONS, os.cpu_count() or 1))
     # one step = one decode token per session; warm-up steps deepen the rows
     rate, elapsed, kind = cpu_decode_rate(weights.weights, threads, args.steps,
@@ -355,6 +381,7 @@ def reference_arm(args):
         "config": {"workload": f"{threads} sessions on {threads} host threads, one decode "
                                f"token per session per step after {args.warmup} warm-up "
                                "tokens (the CPU cannot prefill 4096-token prompts in minutes)",
+                   "depth_note": cpu_depth_note(weights.config, args.warmup, args.steps),
                    "model": "LFM3 synthetic 24L h2048 f8192 16/4x128 v65536 Q8_0",
                    "parallelism": "threads"},
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": kind,
@@ -912,6 +939,9 @@ def main():
     proj_bytes = matrix_elements(cfg) * 34 // 32 * profiled_rounds
     gemv_gbs = proj_bytes / (proj_ms * 1e-3) / 1e9 if proj_ms else 0.0
     traffic = committed_traffic()
+    launches_per_round = proj_launches / profiled_rounds if profiled_rounds else 0
+    weight_bytes = matrix_elements(cfg) * 34 // 32
+    step_s = decode_ms_max / args.steps * 1e-3
 
     # ---- CPU baseline (rank 0, one GPU only; bounded sample)
     cpu = None
@@ -961,11 +991,20 @@ def main():
         },
         "roofline": {
             "bound": "hbm", "kernel": "q8_gemv_kernel (decode projections + LM head)",
-            "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",
-            "frac": gemv_gbs / hbm_peak, "traffic": traffic,
+            "achieved": weight_bytes / step_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
+            "frac": weight_bytes / step_s / 1e9 / hbm_peak,
+            "traffic": traffic * launches_per_round if traffic else None,
+            "traffic_unit": "bytes per round (ncu, all q8_gemv launches of one round)",
             "peak_source": f"{peak_source} hbm_gbs",
-            "how": f"Q8 weight bytes of {profiled_rounds} rounds / summed CUDA-event time "
-                   f"of their {proj_launches} q8_gemv launches (profiled pass)",
+            "how": "Q8 weight bytes of one round (read once by the round's q8_gemv "
+                   "launches) / the timed ms_per_step: the whole round is charged to "
+                   "the projections, so this is a lower bound of their bandwidth",
+        },
+        "serialised_gemv": {
+            "achieved": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / hbm_peak,
+            "how": f"Q8 weight bytes of {profiled_rounds} rounds / summed CUDA-event "
+                   f"time of their {proj_launches} q8_gemv launches in a separate "
+                   "profiled pass (events serialise the launches: not the headline)",
         },
         "step_roofline": {
             "bound": "hbm", "bytes_per_step": step_bytes,

@@ -375,8 +375,13 @@ int lfm3_session_set_continuation_hooks(lfm3_session* session,
 int lfm3_session_prepare_logits(lfm3_session* session);
 int lfm3_session_begin_restore(lfm3_session* session);
 int lfm3_session_finish_restore(lfm3_session* session, uint32_t position);
-/* Snapshot v2 (engine.hpp:127-131). */
+/* Snapshot v2 (engine.hpp:127-131). Header word 7 is
+ * lfm3_snapshot_signature of the model's configuration. */
 size_t lfm3_session_snapshot_bytes(const lfm3_session* session);
+/* ConfigSignature (engine.cpp:1403-1419): FNV-1a over hidden, intermediate,
+ * vocab, heads, head_dim, window, conv_width, the bit patterns of eps, theta
+ * and theta_swa, then each layer's type and KV head count. Host only. */
+uint32_t lfm3_snapshot_signature(const lfm3_config* config);
 int lfm3_session_save_snapshot(lfm3_session* session, uint8_t* out,
                                size_t bytes);
 int lfm3_session_restore_snapshot(lfm3_session* session, const uint8_t* data,

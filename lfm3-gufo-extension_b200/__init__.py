@@ -87,6 +87,7 @@ def library():
         "lfm3_session_continuation_data": ([P, I, SZ], P),
         "lfm3_session_ring_capacity": ([P, SZ], U32),
         "lfm3_session_snapshot_bytes": ([P], SZ),
+        "lfm3_snapshot_signature": ([ctypes.POINTER(abi.Config)], U32),
         "lfm3_session_save_snapshot": ([P, P, SZ], I),
         "lfm3_session_restore_snapshot": ([P, P, SZ], I),
         "lfm3_session_inject_failure": ([P, I], I),

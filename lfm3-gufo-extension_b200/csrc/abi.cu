@@ -1001,6 +1001,9 @@ uint32_t lfm3_session_ring_capacity(const lfm3_session* session,
                                     size_t layer) {
   return session ? session->session->RingCapacity(layer) : 0;
 }
+uint32_t lfm3_snapshot_signature(const lfm3_config* config) {
+  return config ? lfm3::SnapshotSignature(*config) : 0;
+}
 size_t lfm3_session_snapshot_bytes(const lfm3_session* session) {
   return session ? session->session->SnapshotBytes() : 0;
 }
@@ -1008,6 +1011,8 @@ int lfm3_session_save_snapshot(lfm3_session* session, uint8_t* out,
                                size_t bytes) {
   if (!session || !out)
     return Fail(LFM3_ERR_INVALID, "null argument");
+  if (!session->session->IsCoherent())
+    return Fail(LFM3_ERR_POISONED, "cannot snapshot a poisoned LFM3 session");
   try {
     const auto data = session->session->SaveSnapshot();
     if (data.size() != bytes)

@@ -1392,8 +1392,15 @@ uint32_t GetWord(const uint8_t* data, size_t word) {
     value |= uint32_t(data[word * 4 + i]) << (i * 8);
   return value;
 }
-// FNV-1a over the geometry that fixes the payload layout.
-uint32_t Signature(const lfm3_config& c, uint32_t context) {
+}  // namespace
+
+// FNV-1a over the configuration fields in ConfigSignature's order
+// (engine.cpp:1403-1419): hidden, intermediate, vocab, heads, head_dim,
+// window, conv_width, the bit patterns of eps, theta and theta_swa, then each
+// layer's type and KV head count. The context is not part of it (header word
+// 2 carries it), so a snapshot written by the reference's engine restores
+// here and the other way round.
+uint32_t SnapshotSignature(const lfm3_config& c) {
   uint32_t h = 2166136261u;
   const auto mix = [&](uint32_t v) {
     for (int i = 0; i < 4; ++i) {
@@ -1401,19 +1408,23 @@ uint32_t Signature(const lfm3_config& c, uint32_t context) {
       h *= 16777619u;
     }
   };
-  mix(c.hidden);
-  mix(c.vocab);
-  mix(c.n_layers);
-  mix(c.head_dim);
-  mix(c.conv_width);
-  mix(c.window);
-  mix(context);
+  const auto bits = [](float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    return u;
+  };
+  for (const uint32_t v :
+       {c.hidden, c.intermediate, c.vocab, c.heads, c.head_dim, c.window,
+        c.conv_width, bits(c.eps), bits(c.theta), bits(c.theta_swa)})
+    mix(v);
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     mix(c.layer_type[i]);
     mix(c.kv_heads[i]);
   }
   return h;
 }
+
+namespace {
 size_t RowsKept(uint32_t position, uint32_t capacity) {
   return std::min(position, capacity);
 }
@@ -1433,9 +1444,12 @@ size_t Session::SnapshotBytes() const {
 }
 
 std::vector<uint8_t> Session::SaveSnapshot() {
+  // a poisoned session's state may be partly written (engine.cpp:1471-1472)
+  if (poisoned_)
+    throw std::runtime_error("cannot snapshot a poisoned LFM3 session");
   const auto& c = model_->config();
   std::vector<uint8_t> out(SnapshotBytes());
-  if (position_ && !poisoned_)
+  if (position_)
     EnsureLogits();
   Throw(cudaStreamSynchronize(stream_));
   uint8_t* p = out.data();
@@ -1446,14 +1460,16 @@ std::vector<uint8_t> Session::SaveSnapshot() {
   PutWord(p, 4, c.hidden);
   PutWord(p, 5, c.vocab);
   PutWord(p, 6, c.n_layers);
-  PutWord(p, 7, Signature(c, context_));
+  PutWord(p, 7, SnapshotSignature(c));
   p += kSnapshotHeaderBytes;
-  Throw(cudaMemcpy(p, frontier_.data(), size_t(c.hidden) * 4,
-                   cudaMemcpyDeviceToHost));
-  p += size_t(c.hidden) * 4;
-  Throw(cudaMemcpy(p, logits_.data(), size_t(c.vocab) * 4,
-                   cudaMemcpyDeviceToHost));
-  p += size_t(c.vocab) * 4;
+  // an empty session has no frontier: zeros, as the reference writes
+  if (position_) {
+    Throw(cudaMemcpy(p, frontier_.data(), size_t(c.hidden) * 4,
+                     cudaMemcpyDeviceToHost));
+    Throw(cudaMemcpy(p + size_t(c.hidden) * 4, logits_.data(),
+                     size_t(c.vocab) * 4, cudaMemcpyDeviceToHost));
+  }
+  p += (size_t(c.hidden) + c.vocab) * 4;
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     const auto& s = states_[i];
     if (c.layer_type[i] == LFM3_CONV) {
@@ -1487,7 +1503,7 @@ bool Session::RestoreSnapshot(std::span<const uint8_t> payload,
     if (GetWord(p, 0) != kSnapshotMagic || GetWord(p, 1) != kSnapshotVersion ||
         GetWord(p, 2) != context_ || position > context_ ||
         GetWord(p, 4) != c.hidden || GetWord(p, 5) != c.vocab ||
-        GetWord(p, 6) != c.n_layers || GetWord(p, 7) != Signature(c, context_))
+        GetWord(p, 6) != c.n_layers || GetWord(p, 7) != SnapshotSignature(c))
       throw std::invalid_argument("invalid LFM3 snapshot header");
     size_t bytes = kSnapshotHeaderBytes + size_t(c.hidden) * 4 +
                    size_t(c.vocab) * 4;

@@ -23,6 +23,9 @@ namespace lfm3 {
 
 class Session;
 
+// Snapshot header word 7 (ConfigSignature, engine.cpp:1403-1419).
+uint32_t SnapshotSignature(const lfm3_config& c);
+
 // Installed by the continuation (component cache) adapter
 // (continuation_hooks.hpp:5-16): every callback runs on the host before the
 // session changes state or submits device work, and may throw to refuse it.

@@ -73,6 +73,57 @@ def reference_lib():
     return _reference
 
 
+def _synth_lib(prefer_reference):
+    """The oracle library whose copy of the synthetic-weight generator to
+    use: oracle/_ref when present and preferred, else the restatement's."""
+    lib = reference_lib() if prefer_reference and reference_available() \
+        else restatement_lib()
+    if not getattr(lib, "_synth_declared", False):
+        abi.declare_synth(lib)
+        lib._synth_declared = True
+    return lib
+
+
+def default_config(prefer_reference=False):
+    """The graded geometry (lfm3_synth_default_config), without the CUDA
+    library."""
+    cfg = abi.Config()
+    _synth_lib(prefer_reference).lfm3_synth_default_config(ctypes.byref(cfg))
+    return cfg
+
+
+class SyntheticWeights:
+    """Host weights from lfm3_synth_generate (include/lfm3_synth.h) as built
+    into an oracle library, for CPU-only runs that must not load the CUDA
+    library; the same seed gives the same bytes as the package's
+    SyntheticWeights."""
+
+    def __init__(self, config=None, seed=0, matrix_type=abi.Q8_0,
+                 norm_jitter=0.0, threads=0, prefer_reference=True):
+        self.lib = _synth_lib(prefer_reference)
+        self.model = abi.SynthModel()
+        cfg = config if config is not None else default_config(prefer_reference)
+        rc = self.lib.lfm3_synth_generate(
+            ctypes.byref(cfg), seed, matrix_type, norm_jitter, threads,
+            ctypes.byref(self.model))
+        if rc:
+            raise ValueError(f"lfm3_synth_generate failed ({rc})")
+
+    @property
+    def weights(self):
+        return self.model.weights
+
+    @property
+    def config(self):
+        return self.model.weights.config
+
+    def close(self):
+        if self.model.storage:
+            self.lib.lfm3_synth_free(ctypes.byref(self.model))
+
+    __del__ = close
+
+
 class _Base:
     def __init__(self, weights):
         self.weights = weights  # keep the ctypes struct (and its owner) alive

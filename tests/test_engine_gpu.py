@@ -181,6 +181,51 @@ def test_intermediate_and_empty_snapshots(small):
     assert b.position == 0 and b.coherent
 
 
+def test_snapshot_header_is_the_references(small):
+    """Word 7 is the reference's ConfigSignature (engine.cpp:1403-1419), so a
+    header written by the reference's engine restores: here one built word by
+    word from the reference's rule (tests/test_snapshot_format.py) around
+    this session's payload. An empty session writes zeros for the frontier
+    and logits, as the reference does."""
+    import struct
+    from test_snapshot_format import reference_signature
+
+    w, model = small
+    cfg = w.config
+    s = model.session(128)
+    s.forward(list(range(40)), logits=False)
+    snap = s.save_snapshot()
+    words = struct.unpack("<8I", snap[:32].tobytes())
+    assert words == (0x334D464C, 2, 128, 40, cfg.hidden, cfg.vocab,
+                     cfg.n_layers, reference_signature(cfg))
+    rebuilt = np.frombuffer(struct.pack(
+        "<8I", 0x334D464C, 2, 128, 40, cfg.hidden, cfg.vocab, cfg.n_layers,
+        reference_signature(cfg)), np.uint8)
+    t = model.session(128)
+    t.restore_snapshot(np.concatenate([rebuilt, snap[32:]]))
+    np.testing.assert_array_equal(t.forward([7]), s.forward([7]))
+    t.reset()
+    empty = t.save_snapshot()
+    assert not empty[32:32 + 4 * (cfg.hidden + cfg.vocab)].any()
+
+
+def test_poisoned_session_refuses_snapshot(small):
+    """A poisoned session's state may be half written: SaveSnapshot refuses
+    it (engine.cpp:1471-1472) until Reset."""
+    w, model = small
+    s = model.session(128)
+    s.forward([1, 2, 3], logits=False)
+    s.inject_failure(5)
+    with pytest.raises(lfm3.Lfm3Error):
+        s.forward([4, 5, 6, 7])
+    assert not s.coherent
+    with pytest.raises(lfm3.Lfm3Error) as refused:
+        s.save_snapshot()
+    assert refused.value.code == -4  # LFM3_ERR_POISONED
+    s.reset()
+    assert s.save_snapshot().size > 0
+
+
 def test_device_failure_poisons_until_reset(small):
     """A failing CUDA call mid-pass (injected on the host) poisons the
     session; it refuses work until Reset (engine.cpp:905-927, 1300-1332)."""

@@ -18,14 +18,11 @@ from helpers import ROOT, lfm3
 
 def _reference_tree():
     """The reference tree the oracle's Makefile builds from (its REFERENCE
-    variable, overridable from the environment)."""
-    if os.environ.get("REFERENCE"):
-        return os.environ["REFERENCE"]
-    with open(os.path.join(ROOT, "oracle", "Makefile")) as f:
-        for line in f:
-            if line.startswith("REFERENCE ?="):
-                return line.split("?=", 1)[1].strip()
-    return ""
+    variable: the environment's, else its default)."""
+    import subprocess
+    out = subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"),
+                          "print-reference"], capture_output=True, text=True)
+    return out.stdout.strip()
 
 
 REFERENCE = _reference_tree()

@@ -85,3 +85,31 @@ def test_default_geometry():
     assert cfg.pattern() == "CCSGCCSGCCSGCCSGCCSGCCGC"
     assert [cfg.kv_heads[i] for i in range(24)].count(4) == 11
     assert (cfg.window, cfg.conv_width, cfg.context) == (256, 7, 262144)
+
+
+def test_oracle_copy_of_the_generator_matches_and_loads_no_cuda_library():
+    """The bench's reference arm makes its weights with the generator built
+    into the oracle libraries: the same bytes as the package's, and the
+    process maps no library of this package."""
+    import subprocess
+    import sys
+
+    from helpers import ROOT, ensure_oracle_built
+    ensure_oracle_built()
+    import oracle
+    cfg = lfm3.small_config()
+    a = lfm3.SyntheticWeights(cfg, seed=4, threads=2)
+    for prefer in (False, True):
+        b = oracle.SyntheticWeights(cfg, seed=4, threads=3, prefer_reference=prefer)
+        for name in ("embedding", "output_norm"):
+            np.testing.assert_array_equal(tensor_bytes(getattr(a.weights, name)),
+                                          tensor_bytes(getattr(b.weights, name)))
+        np.testing.assert_array_equal(tensor_bytes(a.weights.layers[2].q),
+                                      tensor_bytes(b.weights.layers[2].q))
+    code = ("import sys; sys.path[:0] = [%r, %r]; import oracle; "
+            "w = oracle.SyntheticWeights(oracle.default_config(), seed=0); "
+            "print(open('/proc/self/maps').read())" % (ROOT, f"{ROOT}/oracle"))
+    maps = subprocess.run([sys.executable, "-c", code], capture_output=True,
+                          text=True, check=True).stdout
+    assert "liblfm3_cuda" not in maps
+    assert "oracle" in maps
