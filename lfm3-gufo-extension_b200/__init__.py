@@ -106,6 +106,8 @@ def library():
         "lfm3_cuda_shares_split": ([P, I, I, P], I),
         "lfm3_cuda_batched_residual_add": ([P, P, P, SZ, SZ, P], I),
         "lfm3_cuda_gemv": ([P, U32, P, P, SZ, SZ, P], I),
+        "lfm3_cuda_decode_workspace_bytes": ([P, I, I], SZ),
+        "lfm3_cuda_decode_project": ([P, I, I, P, I, P, P, P, P], I),
         "lfm3_cuda_batched_quant_gemm_fp32": ([U32, P, P, P, SZ, SZ, SZ, P], I),
         "lfm3_cuda_exact_bf16_gemm_fp32_small_batch": ([P, P, P, SZ, SZ, SZ, P], I),
         "lfm3_cuda_sample_scratch_bytes": ([I, I, I], SZ),

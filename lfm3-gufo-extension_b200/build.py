@@ -26,7 +26,8 @@ CUDA_FLAGS = ARCH + [
 ]
 SOURCES = [
     "abi.cu", "attention_decode.cu", "attention_prompt.cu", "conv.cu",
-    "device_error.cu", "engine.cpp", "noalloc.cu", "norm.cu", "q8_gemv.cu",
+    "device_error.cu", "engine.cpp", "noalloc.cu", "norm.cu", "q8_decode.cu",
+    "q8_gemv.cu",
     "q8_prefill.cu", "sampling.cu",
     "tensor_map.cpp",
 ]

@@ -593,6 +593,81 @@ int lfm3_cuda_batched_residual_add(const float* a, const float* b, float* out,
                                          0.0F, Stream(stream), false));
 }
 
+namespace {
+// The decode layout of caller matrices for lfm3_cuda_decode_project, and the
+// workspace pieces: packed copy, split input.
+struct DecodeWorkspace {
+  lfm3::DecodeLayout layout{};
+  size_t packed = 0, split = 0, total = 0;
+};
+bool DecodePlan(const lfm3_tensor* const* w, int n_w, int swiglu,
+                DecodeWorkspace& ws) {
+  if (!w || n_w < 1 || n_w > 4 || (swiglu && n_w != 2))
+    return false;
+  auto& l = ws.layout;
+  l.kind = swiglu ? lfm3::kDecSwiGLU : lfm3::kDecPlain;
+  l.n_src = n_w;
+  for (int j = 0; j < n_w; ++j) {
+    if (!w[j] || !w[j]->data || w[j]->type != LFM3_Q8_0 ||
+        (j && w[j]->cols != w[0]->cols))
+      return false;
+    l.rows[j] = int(w[j]->rows);
+  }
+  l.K = int(w[0]->cols);
+  if (!lfm3::decode_layout(l, Sms()))
+    return false;
+  const auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  ws.packed = up(lfm3::decode_packed_bytes(l));
+  ws.split = up(size_t(lfm3::kMaxBatch) * l.K * 4);
+  ws.total = ws.packed + ws.split;
+  return true;
+}
+}  // namespace
+
+size_t lfm3_cuda_decode_workspace_bytes(const lfm3_tensor* const* w, int n_w,
+                                        int swiglu) {
+  DecodeWorkspace ws;
+  return DecodePlan(w, n_w, swiglu, ws) ? ws.total : 0;
+}
+
+int lfm3_cuda_decode_project(const lfm3_tensor* const* w, int n_w, int swiglu,
+                             const float* x, int rows, float* const* out,
+                             const size_t* ld, void* workspace, void* stream) {
+  DecodeWorkspace ws;
+  if (!DecodePlan(w, n_w, swiglu, ws))
+    return Fail(LFM3_ERR_UNSUPPORTED, "decode projection shape not supported");
+  if (!x || !out || !ld || !workspace || rows < 1 || rows > lfm3::kMaxBatch ||
+      reinterpret_cast<uintptr_t>(workspace) % 256)
+    return Fail(LFM3_ERR_INVALID, "invalid decode projection arguments");
+  for (int j = 0; j < (swiglu ? 1 : n_w); ++j)
+    if (!out[j])
+      return Fail(LFM3_ERR_INVALID, "null output");
+  cudaStream_t s = Stream(stream);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  uint8_t* packed = base;
+  void* split = base + ws.packed;
+  const uint8_t* src[4] = {};
+  for (int j = 0; j < n_w; ++j)
+    src[j] = static_cast<const uint8_t*>(w[j]->data);
+  if (int e = Cuda(lfm3::launch_decode_pack(ws.layout, src, packed, s)))
+    return e;
+  if (int e = Cuda(lfm3::launch_split_rows(x, split, rows, ws.layout.K, s)))
+    return e;
+  lfm3::DecodeParams p{};
+  p.layout = ws.layout;
+  p.w = packed;
+  p.tokens = rows;
+  p.x = split;
+  for (int j = 0; j < (swiglu ? 0 : n_w); ++j)
+    p.o[j] = lfm3::DecodeOut{out[j], int(ld[j])};
+  if (swiglu) {
+    p.f32_out = out[0];
+    p.f32_ld = int(ld[0]);
+  }
+  return Cuda(lfm3::launch_decode_gemv(
+      p, lfm3::decode_grid(ws.layout, Sms()), s, false));
+}
+
 int lfm3_cuda_gemv(const void* A, uint32_t a_type, const float* x, float* y,
                    size_t M, size_t K, void* stream) {
   return MatrixRows(A, a_type, x, y, 1, M, K, Stream(stream));

@@ -170,6 +170,8 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
       m->weight_bytes_ += bytes;
     }
     VisitTensors(m->device_, [&](lfm3_tensor& t) { t.data = placed.at(t.data); });
+    if (!m->bf16())
+      m->PackDecodeGroups();
     // RoPE frequencies: float(pow(double theta, -2i/D)), global then sliding
     // (hip/ops.hip:1045-1050, engine.cpp:225-232).
     float freq[128];
@@ -193,6 +195,65 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
       *error = e.what();
     return nullptr;
   }
+}
+
+// Packs every Q8_0 matrix group a decode round reads into the decode
+// projections' fragment order (q8_decode.cuh), from the device copies just
+// uploaded, into one allocation (256-byte aligned groups).
+void Model::PackDecodeGroups() {
+  const auto& c = device_.config;
+  const int H = int(c.hidden), F = int(c.intermediate), A = int(c.heads) * 128;
+  struct Job {
+    DecodeGroup* group;
+    const uint8_t* src[4];
+  };
+  std::vector<Job> jobs;
+  decode_.assign(c.n_layers, DecodeLayer{});
+  const auto q8 = [](const lfm3_tensor& t) {
+    return static_cast<const uint8_t*>(t.data);
+  };
+  const auto add = [&](DecodeGroup& g, int kind, int K,
+                       std::initializer_list<const lfm3_tensor*> srcs) {
+    g.layout = DecodeLayout{};
+    g.layout.kind = kind;
+    g.layout.K = K;
+    g.layout.H = H;
+    g.layout.n_src = int(srcs.size());
+    Job job{&g, {}};
+    int j = 0;
+    for (const lfm3_tensor* t : srcs) {
+      g.layout.rows[j] = int(t->rows);
+      job.src[j++] = q8(*t);
+    }
+    if (!decode_layout(g.layout, sms_))
+      throw std::invalid_argument("decode projection shape not supported");
+    jobs.push_back(job);
+  };
+  for (uint32_t i = 0; i < c.n_layers; ++i) {
+    const auto& l = device_.layers[i];
+    DecodeLayer& d = decode_[i];
+    if (c.layer_type[i] == LFM3_CONV) {
+      add(d.in_proj, kDecConv, H, {&l.in_proj});
+      add(d.out_proj, kDecPlain, H, {&l.out_proj});
+    } else {
+      add(d.qkvg, kDecPlain, H, {&l.q, &l.k, &l.v, &l.attn_gate});
+      add(d.attn_out, kDecPlain, A, {&l.attn_out});
+    }
+    add(d.gate_up, kDecSwiGLU, H, {&l.gate, &l.up});
+    add(d.down, kDecPlain, F, {&l.down});
+  }
+  add(decode_head_, kDecPlain, H, {&device_.output});
+  size_t total = 0;
+  for (const Job& job : jobs)
+    total += (decode_packed_bytes(job.group->layout) + 255) / 256 * 256;
+  packed_ = DeviceBuffer(total);
+  uint8_t* dst = packed_.as<uint8_t>();
+  for (const Job& job : jobs) {
+    job.group->data = dst;
+    Throw(launch_decode_pack(job.group->layout, job.src, dst, nullptr));
+    dst += (decode_packed_bytes(job.group->layout) + 255) / 256 * 256;
+  }
+  Throw(cudaDeviceSynchronize());
 }
 
 const CUtensorMap& Model::RowMap(const lfm3_tensor& t, int chunk_bytes,
@@ -405,6 +466,31 @@ static cudaError_t RunGemv(GemvParams p, Model& model, cudaStream_t stream) {
   return launch_q8_gemv(p, gemv_grid(p.tiles, model.sms()), stream, true);
 }
 
+// Launches one projection of the round's rows over a packed decode group
+// (Q8_0 models): the same outputs and epilogue as the GemvParams describe.
+static cudaError_t RunDecode(const GemvParams& g, const DecodeGroup& group,
+                             Model& model, cudaStream_t stream) {
+  DecodeParams p{};
+  p.layout = group.layout;
+  p.w = group.data;
+  p.tokens = g.tokens;
+  p.x = g.x;
+  for (int j = 0; j < 4; ++j)
+    p.o[j] = DecodeOut{g.o[j].out, g.o[j].ld};
+  p.split_out = g.split_out;
+  p.split_width = g.split_width;
+  if (g.kind == kGemvSwiGLU) {
+    p.f32_out = g.o[0].out;
+    p.f32_ld = g.o[0].ld;
+  }
+  p.conv_w = g.conv_w;
+  p.rows = g.rows;
+  p.layer = g.layer;
+  p.L = g.L;
+  return launch_decode_gemv(p, decode_grid(p.layout, model.sms()), stream,
+                            true);
+}
+
 static GemvOutput Out(const lfm3_tensor& w, float* out, int ld) {
   return {static_cast<const uint8_t*>(w.data), out, int(w.rows), ld};
 }
@@ -419,7 +505,9 @@ void Session::LaunchLmHead(const void* split_rows, int rows, float* out) {
   p.n_out = 1;
   p.o[0] = Out(w.output, out, c.vocab);
   p.x = split_rows;
-  Check(RunGemv(p, *model_, stream_));
+  Check(model_->bf16()
+            ? RunGemv(p, *model_, stream_)
+            : RunDecode(p, model_->decode_head(), *model_, stream_));
 }
 
 void Session::DecodeRound(std::span<Session* const> batch,
@@ -430,9 +518,14 @@ void Session::DecodeRound(std::span<Session* const> batch,
   const int B = int(batch.size());
   const int H = c.hidden, F = c.intermediate, A = c.heads * 128;
   cudaStream_t s = stream_;
-  const auto gemv = [&](GemvParams p) {
-    Timed(kDecodeProjection,
-          [&] { Check(RunGemv(p, *model_, s)); });
+  // a projection of the round's rows: BF16 matrices directly, Q8_0 through
+  // the layer's packed decode group
+  const auto gemv = [&](GemvParams p, const DecodeGroup& group) {
+    Timed(kDecodeProjection, [&] {
+      Check(model_->bf16()
+                ? RunGemv(p, *model_, s)
+                : RunDecode(p, group, *model_, s));
+    });
   };
   // the rows of this round go through a pinned table whose previous copy is
   // done; an earlier round that returned without waiting and has finished
@@ -488,6 +581,8 @@ void Session::DecodeRound(std::span<Session* const> batch,
     });
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     const auto& l = w.layers[i];
+    static const DecodeLayer kNone{};
+    const DecodeLayer& dl = model_->bf16() ? kNone : model_->decode_layer(i);
     if (c.layer_type[i] == LFM3_CONV) {
       GemvParams p{};
       p.kind = kGemvConv;
@@ -503,7 +598,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       p.layer = int(i);
       p.H = H;
       p.L = int(c.conv_width);
-      gemv(p);
+      gemv(p, dl.in_proj);
       GemvParams o{};
       o.kind = kGemvPlain;
       o.K = H;
@@ -511,7 +606,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       o.n_out = 1;
       o.o[0] = Out(l.out_proj, out, H);
       o.x = a_split_.data();
-      gemv(o);
+      gemv(o, dl.out_proj);
     } else {
       const int kv = int(c.kv_heads[i]) * 128;
       GemvParams p{};
@@ -524,7 +619,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       p.o[2] = Out(l.v, v_.as<float>(), kv);
       p.o[3] = Out(l.attn_gate, gate_.as<float>(), c.heads);
       p.x = z;
-      gemv(p);
+      gemv(p, dl.qkvg);
       const bool swa = c.layer_type[i] == LFM3_SLIDING_ATTENTION;
       DecodeAttentionParams ap{};
       ap.q = q_.as<float>();
@@ -573,7 +668,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       o.n_out = 1;
       o.o[0] = Out(l.attn_out, out, H);
       o.x = a_split_.data();
-      gemv(o);
+      gemv(o, dl.attn_out);
     }
     Timed(kRowKernels, [&] {
       Check(launch_residual_norm(
@@ -591,7 +686,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
     f.x = z;
     f.split_out = h_split_.data();
     f.split_width = F;
-    gemv(f);
+    gemv(f, dl.gate_up);
     GemvParams d{};
     d.kind = kGemvPlain;
     d.K = F;
@@ -599,7 +694,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
     d.n_out = 1;
     d.o[0] = Out(l.down, out, H);
     d.x = h_split_.data();
-    gemv(d);
+    gemv(d, dl.down);
     const bool last = i + 1 == c.n_layers;
     const float* next = static_cast<const float*>(
         last ? w.output_norm.data : w.layers[i + 1].norm.data);
@@ -1301,6 +1396,10 @@ bool Session::Reset(std::string* error) {
         Throw(cudaMemsetAsync(states_[i].conv.data(), 0,
                               size_t(c.hidden) * (c.conv_width - 1) * 4,
                               stream_));
+    // a launch that gave up part way (a poisoned pass) may have left the
+    // decode attention's span tickets counted; clear them with the state
+    Throw(cudaMemsetAsync(attn_tickets_.data(), 0, attn_tickets_.bytes(),
+                          stream_));
     Throw(cudaStreamSynchronize(stream_));
     position_ = 0;
     logits_ready_ = false;

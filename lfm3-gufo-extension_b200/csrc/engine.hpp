@@ -17,6 +17,7 @@
 
 #include "../../include/lfm3_types.h"
 #include "decode_types.cuh"
+#include "q8_decode.cuh"
 #include "sampling.cuh"
 
 namespace lfm3 {
@@ -64,6 +65,20 @@ private:
 // (engine.hpp:9-15, ContinuationTensor).
 enum class ContinuationTensor { kLogits, kFrontier, kConvolution, kKey, kValue };
 
+// A Q8_0 matrix group in the decode projections' fragment order
+// (q8_decode.cuh), packed once at load.
+struct DecodeGroup {
+  DecodeLayout layout{};
+  const uint8_t* data = nullptr;
+};
+// The groups one decode round reads per layer: a conv layer's in_proj
+// (with the convolution step) and out_proj, an attention layer's fused
+// q / k / v / gate projection and attn_out, and every layer's gate + up
+// (SwiGLU) and down.
+struct DecodeLayer {
+  DecodeGroup in_proj, out_proj, qkvg, attn_out, gate_up, down;
+};
+
 class Model : public std::enable_shared_from_this<Model> {
 public:
   ~Model();
@@ -97,6 +112,11 @@ public:
   // chunk_bytes (encoded once, cached).
   const CUtensorMap& RowMap(const lfm3_tensor& t, int chunk_bytes,
                             int box_rows);
+  // Q8_0 models: the packed decode groups of layer i and of the LM head.
+  const DecodeLayer& decode_layer(uint32_t i) const { return decode_[i]; }
+  const DecodeGroup& decode_head() const { return decode_head_; }
+  // Device bytes of the packed decode copies.
+  size_t packed_bytes() const { return packed_.bytes(); }
 
 private:
   Model() = default;
@@ -111,6 +131,11 @@ private:
   unsigned* error_device_ = nullptr;
 
   size_t weight_bytes_ = 0;
+  // the decode groups (Q8_0 models), all in one allocation
+  DeviceBuffer packed_;
+  std::vector<DecodeLayer> decode_;
+  DecodeGroup decode_head_;
+  void PackDecodeGroups();
   std::mutex maps_mutex_;
   std::map<std::pair<const void*, int>, CUtensorMap> maps_;
   friend class Session;
@@ -280,6 +305,7 @@ private:
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
       attn_tickets_, prompt_scratch_, split_partial_, zf_;
+
   // token selection of the rounds this session leads: candidates, the
   // selected tokens, and their pinned host copy
   DeviceBuffer sample_scratch_, sample_out_;
