@@ -46,6 +46,33 @@ static float half_to_float(uint16_t bits) {
   return f;
 }
 
+/* Round-to-nearest-even to the nearest fp16 value (overflow to infinity),
+ * back in float: the value an F16 K/V ring holds. */
+static float round_half(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint32_t sign = x & 0x80000000u, ax = x & 0x7fffffffu;
+  uint16_t h;
+  if (ax >= 0x7f800000u)
+    h = (uint16_t)((sign >> 16) | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0));
+  else if (ax >= 0x477ff000u) /* rounds to >= 65520: infinity */
+    h = (uint16_t)((sign >> 16) | 0x7c00u);
+  else if (ax < 0x38800000u) { /* below 2^-14: subnormal or zero */
+    float a;
+    memcpy(&a, &ax, 4);
+    const float q = a * 16777216.0f; /* units of 2^-24, exact */
+    h = (uint16_t)((sign >> 16) | (uint16_t)nearbyintf(q));
+  } else {
+    const uint32_t e = (ax >> 23) - 112, m = ax & 0x7fffffu;
+    uint32_t v = (e << 10) | (m >> 13);
+    const uint32_t rest = m & 0x1fffu;
+    if (rest > 0x1000u || (rest == 0x1000u && (v & 1)))
+      ++v;
+    h = (uint16_t)((sign >> 16) | v);
+  }
+  return half_to_float(h);
+}
+
 /* ---- thread pool for Mat ------------------------------------------------ */
 
 typedef struct mat_task {
@@ -186,6 +213,7 @@ typedef struct layer_state {
 struct lfm3_oracle {
   const lfm3_weights* w;
   uint32_t context, position;
+  int kv_half; /* round stored K/V through fp16 (lfm3_oracle_set_kv_half) */
   layer_state states[LFM3_MAX_LAYERS];
   /* per-step scratch */
   float *x, *z, *out, *p, *conv, *q, *kk, *vv, *gate, *a, *ff_gate, *ff_up,
@@ -374,6 +402,10 @@ void lfm3_oracle_reset(lfm3_oracle* o) {
 
 uint32_t lfm3_oracle_position(const lfm3_oracle* o) { return o->position; }
 
+void lfm3_oracle_set_kv_half(lfm3_oracle* o, int on) { o->kv_half = on != 0; }
+
+float lfm3_oracle_round_half(float value) { return round_half(value); }
+
 const float* lfm3_oracle_hidden(const lfm3_oracle* o) { return o->hidden; }
 
 /* reference.cpp:72-168 */
@@ -451,6 +483,11 @@ int lfm3_oracle_step(lfm3_oracle* o, uint32_t token, float* logits) {
       const size_t slot = o->position % state->capacity;
       memcpy(state->k + slot * stride, k, stride * 4);
       memcpy(state->v + slot * stride, v, stride * 4);
+      if (o->kv_half)
+        for (size_t i = 0; i < stride; ++i) {
+          state->k[slot * stride + i] = round_half(state->k[slot * stride + i]);
+          state->v[slot * stride + i] = round_half(state->v[slot * stride + i]);
+        }
       const uint32_t first =
           swa && o->position + 1 > c->window ? o->position + 1 - c->window : 0;
       float* scores = o->scores;

@@ -33,6 +33,15 @@ void lfm3_oracle_reset(lfm3_oracle* oracle);
  * Returns 0, or -1 for an invalid token or a full context. */
 int lfm3_oracle_step(lfm3_oracle* oracle, uint32_t token, float* logits);
 uint32_t lfm3_oracle_position(const lfm3_oracle* oracle);
+/* Test-only numerics switch (off by default, no counterpart in
+ * reference.cpp): round every stored K and V value to the nearest fp16, as
+ * the engine's F16 rings hold them (engine.cpp:71-72), where reference.cpp
+ * keeps FP32 (reference.cpp:113-115). Isolates that one storage difference
+ * in GPU-vs-oracle comparisons. */
+void lfm3_oracle_set_kv_half(lfm3_oracle* oracle, int on);
+/* The fp16 rounding that switch applies (round to nearest even, overflow
+ * to infinity), for tests. */
+float lfm3_oracle_round_half(float value);
 /* Final hidden state after the last step's final norm (valid when that step
  * produced logits). */
 const float* lfm3_oracle_hidden(const lfm3_oracle* oracle);

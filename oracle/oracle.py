@@ -46,6 +46,10 @@ def restatement_lib():
         lib.lfm3_oracle_position.restype = ctypes.c_uint32
         lib.lfm3_oracle_hidden.argtypes = [ctypes.c_void_p]
         lib.lfm3_oracle_hidden.restype = ctypes.POINTER(ctypes.c_float)
+        lib.lfm3_oracle_set_kv_half.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        lib.lfm3_oracle_set_kv_half.restype = None
+        lib.lfm3_oracle_round_half.argtypes = [ctypes.c_float]
+        lib.lfm3_oracle_round_half.restype = ctypes.c_float
         _restatement = lib
     return _restatement
 
@@ -156,13 +160,15 @@ class _Base:
 class Oracle(_Base):
     """The C restatement (reference.cpp:72-168)."""
 
-    def __init__(self, weights, context, threads=1):
+    def __init__(self, weights, context, threads=1, kv_half=False):
         super().__init__(weights)
         self.lib = restatement_lib()
         self.handle = self.lib.lfm3_oracle_create(
             ctypes.byref(weights), context, threads)
         if not self.handle:
             raise ValueError("invalid oracle context")
+        # test-only: K/V stored through fp16 as the engine's rings hold them
+        self.lib.lfm3_oracle_set_kv_half(self.handle, int(kv_half))
 
     def step(self, token, want_logits=True):
         logits = np.empty(self.vocab, np.float32) if want_logits else None

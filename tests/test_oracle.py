@@ -88,3 +88,22 @@ def test_restatement_refuses_invalid_steps():
         o.step(1, False)
     with pytest.raises(ValueError):
         oracle.Oracle(w.weights, 0)
+
+
+def test_kv_half_rounding_matches_numpy():
+    """The oracle's test-only F16 K/V switch rounds exactly as IEEE fp16
+    (numpy): ties to even, subnormals, overflow to infinity."""
+    import oracle
+    lib = oracle.restatement_lib()
+    rng = np.random.default_rng(0)
+    values = np.concatenate([
+        rng.normal(0, 1, 3000), rng.normal(0, 1e-5, 3000),
+        rng.normal(0, 3e4, 500),
+        [65504, 65519.99, 65520, 1e9, -1e-8, 0.0, -0.0, 2.0 ** -24,
+         2.0 ** -25, 3 * 2.0 ** -25, 1 + 2.0 ** -11, 1 + 3 * 2.0 ** -11,
+         2.0 ** -14 * (1 - 2.0 ** -11)]]).astype(np.float32)
+    for v in values:
+        got = lib.lfm3_oracle_round_half(float(v))
+        want = float(np.float32(np.float16(v)))
+        assert got == want or (np.isinf(got) and np.isinf(want)), (float(v), got, want)
+        assert np.signbit(got) == np.signbit(want) or got != 0
