@@ -157,9 +157,10 @@ int lfm3_cuda_attention(const float* q, const uint16_t* k, const uint16_t* v,
  * scratch; its scratch is a static device array of about 1 MiB per GPU that
  * loads the library, kept until the process exits, so heads must be <= 32
  * (LFM3_ERR_UNSUPPORTED with a message beyond that). It allocates nothing.
- * The first call on each device looks up that array's device address; make
- * it before any stream capture. Calls share the array: calls that overlap
- * on the GPU race and must be serialised by the caller. */
+ * The first call on each device looks up that array's device address (and
+ * again the first call after cudaDeviceReset, whose new context holds the
+ * array afresh); make it before any stream capture. Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. */
 int lfm3_cuda_attention_decode_noalloc(const float* q, const uint16_t* k,
                                        const uint16_t* v, const float* gate,
                                        const uint16_t* cache_k,
@@ -389,6 +390,50 @@ int lfm3_session_set_continuation_hooks(lfm3_session* session,
 int lfm3_session_prepare_logits(lfm3_session* session);
 int lfm3_session_begin_restore(lfm3_session* session);
 int lfm3_session_finish_restore(lfm3_session* session, uint32_t position);
+/* ---- continuous batching ------------------------------------------------
+ * The step the reference's host scheduler drives through its text runner
+ * (scheduling profile runner.cpp:140-177: prompt passes of at most 512 rows
+ * in one layer group between decode rounds of at most 8 sessions; Prefill /
+ * AdvanceBatch / SelectNext, runner.cpp:249-351). Each step runs one prompt
+ * pass of at most 512 rows for the first admitted request with prompt rows
+ * left (first come, first served; after its last pass the request's first
+ * token is selected on the device), then one decode round of up to 8
+ * decoding requests in admission order with device token selection. Every
+ * selection uses the scheduler's sampler over the request's last 64 tokens
+ * (prompt tail, then each advanced token) and the draw seed
+ * seed ^ (position * 0x9E3779B97F4A7C15), position = tokens advanced.
+ * One host thread per scheduler. */
+typedef struct lfm3_scheduler lfm3_scheduler;
+typedef struct lfm3_step_stats {
+  int32_t pass_request; /* request of the step's prompt pass, or -1 */
+  uint32_t pass_rows;
+  uint32_t round_rows;  /* requests the decode round advanced */
+  uint32_t finished;    /* requests completed by the step */
+  double pass_ms;       /* host time of the pass (results on the host) */
+  double round_ms;      /* host time of the round (tokens on the host) */
+} lfm3_step_stats;
+lfm3_scheduler* lfm3_scheduler_create(lfm3_model* model,
+                                      const lfm3_sampler* sampler);
+void lfm3_scheduler_free(lfm3_scheduler* scheduler);
+/* Admits a request (the prompt is copied) with its own session of
+ * `context` rows (>= n + max_new). Returns the request id (>= 0) or a
+ * negative LFM3_ERR_* code. */
+int lfm3_scheduler_admit(lfm3_scheduler* scheduler, const uint32_t* prompt,
+                         size_t n, uint32_t max_new, uint64_t seed,
+                         uint32_t context);
+/* One step; stats may be NULL. A failed device call retires the requests
+ * of that call (LFM3_ERR_CUDA or LFM3_ERR_DEVICE_WAIT); the others go on. */
+int lfm3_scheduler_step(lfm3_scheduler* scheduler, lfm3_step_stats* stats);
+/* 1 when no admitted request has work left, else 0. */
+int lfm3_scheduler_idle(const lfm3_scheduler* scheduler);
+/* The tokens request `id` has selected so far: copies up to cap into out
+ * (may be NULL) and returns how many there are. */
+size_t lfm3_scheduler_tokens(const lfm3_scheduler* scheduler, int id,
+                             uint32_t* out, size_t cap);
+/* 1 when request `id` is complete (2 when it was retired by a failure),
+ * else 0. */
+int lfm3_scheduler_finished(const lfm3_scheduler* scheduler, int id);
+
 /* Snapshot v2 (engine.hpp:127-131). Header word 7 is
  * lfm3_snapshot_signature of the model's configuration. */
 size_t lfm3_session_snapshot_bytes(const lfm3_session* session);

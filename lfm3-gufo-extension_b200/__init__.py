@@ -118,6 +118,13 @@ def library():
         "lfm3_session_forward_batch_sample": ([P, P, SZ,
                                                ctypes.POINTER(abi.Sampler),
                                                P, P, P, P], I),
+        "lfm3_scheduler_create": ([P, ctypes.POINTER(abi.Sampler)], P),
+        "lfm3_scheduler_free": ([P], None),
+        "lfm3_scheduler_admit": ([P, P, SZ, U32, ctypes.c_uint64, U32], I),
+        "lfm3_scheduler_step": ([P, ctypes.POINTER(abi.StepStats)], I),
+        "lfm3_scheduler_idle": ([P], I),
+        "lfm3_scheduler_tokens": ([P, I, P, SZ], SZ),
+        "lfm3_scheduler_finished": ([P, I], I),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -248,6 +255,56 @@ class Model:
 
     def session(self, context):
         return Session(self, context)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self._free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+class Scheduler:
+    """lfm3_scheduler: continuous batching of requests on one model (one
+    <=512-row prompt pass, first come first served, then one decode round of
+    up to 8 requests with device token selection, per step)."""
+
+    def __init__(self, model, sampler_):
+        lib = library()
+        self.model = model
+        self._free = lib.lfm3_scheduler_free
+        self._sampler = sampler_
+        self.handle = lib.lfm3_scheduler_create(model.handle, ctypes.byref(sampler_))
+        if not self.handle:
+            raise Lfm3Error(-1, lib.lfm3_last_error().decode())
+
+    def admit(self, prompt, max_new, seed, context):
+        toks = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        rc = library().lfm3_scheduler_admit(self.handle, _ptr(toks), toks.size,
+                                            int(max_new), int(seed), int(context))
+        if rc < 0:
+            check(rc)
+        return rc
+
+    def step(self):
+        st = abi.StepStats()
+        check(library().lfm3_scheduler_step(self.handle, ctypes.byref(st)))
+        return st
+
+    @property
+    def idle(self):
+        return bool(library().lfm3_scheduler_idle(self.handle))
+
+    def tokens(self, request):
+        lib = library()
+        n = lib.lfm3_scheduler_tokens(self.handle, request, None, 0)
+        out = np.zeros(n, np.uint32)
+        lib.lfm3_scheduler_tokens(self.handle, request, _ptr(out), n)
+        return out
+
+    def finished(self, request):
+        return library().lfm3_scheduler_finished(self.handle, request)
 
     def close(self):
         if getattr(self, "handle", None):

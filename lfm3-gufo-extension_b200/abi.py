@@ -116,6 +116,18 @@ class Sampler(ctypes.Structure):
     ]
 
 
+class StepStats(ctypes.Structure):
+    """lfm3_step_stats: what one scheduler step ran."""
+    _fields_ = [
+        ("pass_request", ctypes.c_int32),
+        ("pass_rows", ctypes.c_uint32),
+        ("round_rows", ctypes.c_uint32),
+        ("finished", ctypes.c_uint32),
+        ("pass_ms", ctypes.c_double),
+        ("round_ms", ctypes.c_double),
+    ]
+
+
 def declare_synth(lib):
     """Argument types of the lfm3_synth_* entry points (include/lfm3_synth.h)."""
     lib.lfm3_synth_default_config.argtypes = [ctypes.POINTER(Config)]

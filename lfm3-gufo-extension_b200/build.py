@@ -28,7 +28,7 @@ SOURCES = [
     "abi.cu", "attention_decode.cu", "attention_prompt.cu", "conv.cu",
     "device_error.cu", "engine.cpp", "noalloc.cu", "norm.cu", "q8_decode.cu",
     "q8_gemv.cu",
-    "q8_prefill.cu", "sampling.cu",
+    "q8_prefill.cu", "sampling.cu", "scheduler.cpp",
     "tensor_map.cpp",
 ]
 HOST_C = ["host/synth.c"]

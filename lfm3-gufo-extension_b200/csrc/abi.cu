@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "engine.hpp"
 #include "kernels.cuh"
+#include "scheduler.hpp"
 
 namespace {
 
@@ -1076,6 +1077,81 @@ uint32_t lfm3_session_ring_capacity(const lfm3_session* session,
                                     size_t layer) {
   return session ? session->session->RingCapacity(layer) : 0;
 }
+struct lfm3_scheduler {
+  std::unique_ptr<lfm3::Scheduler> scheduler;
+};
+
+lfm3_scheduler* lfm3_scheduler_create(lfm3_model* model,
+                                      const lfm3_sampler* sampler) {
+  if (!model || !sampler) {
+    Fail(LFM3_ERR_INVALID, "null argument");
+    return nullptr;
+  }
+  lfm3::SampleControls c{};
+  if (const char* why = lfm3::sample_controls(
+          sampler->temperature, sampler->top_k, sampler->repeat_penalty,
+          int(model->model->config().vocab), &c)) {
+    Fail(LFM3_ERR_INVALID, why);
+    return nullptr;
+  }
+  try {
+    auto* s = new lfm3_scheduler;
+    s->scheduler = std::make_unique<lfm3::Scheduler>(model->model, c);
+    return s;
+  } catch (const std::exception& e) {
+    Fail(LFM3_ERR_CUDA, e.what());
+    return nullptr;
+  }
+}
+void lfm3_scheduler_free(lfm3_scheduler* scheduler) { delete scheduler; }
+int lfm3_scheduler_admit(lfm3_scheduler* scheduler, const uint32_t* prompt,
+                         size_t n, uint32_t max_new, uint64_t seed,
+                         uint32_t context) {
+  if (!scheduler || (!prompt && n))
+    return Fail(LFM3_ERR_INVALID, "null argument");
+  std::string error;
+  try {
+    const int id = scheduler->scheduler->Admit(
+        std::span<const uint32_t>(prompt, n), max_new, seed, context, &error);
+    return id >= 0 ? id : Fail(LFM3_ERR_INVALID, error);
+  } catch (const std::exception& e) {
+    return Fail(LFM3_ERR_CUDA, e.what());
+  }
+}
+int lfm3_scheduler_step(lfm3_scheduler* scheduler, lfm3_step_stats* stats) {
+  if (!scheduler)
+    return Fail(LFM3_ERR_INVALID, "null argument");
+  lfm3::Scheduler::StepStats st;
+  std::string error;
+  const bool ok = scheduler->scheduler->Step(&st, &error);
+  if (stats)
+    *stats = lfm3_step_stats{st.pass_request, st.pass_rows, st.round_rows,
+                             st.finished, st.pass_ms, st.round_ms};
+  if (ok)
+    return LFM3_OK;
+  return Fail(error.find("device wait") != std::string::npos
+                  ? LFM3_ERR_DEVICE_WAIT
+                  : LFM3_ERR_CUDA,
+              error);
+}
+int lfm3_scheduler_idle(const lfm3_scheduler* scheduler) {
+  return scheduler && scheduler->scheduler->Idle() ? 1 : 0;
+}
+size_t lfm3_scheduler_tokens(const lfm3_scheduler* scheduler, int id,
+                             uint32_t* out, size_t cap) {
+  if (!scheduler)
+    return 0;
+  const auto t = scheduler->scheduler->Tokens(id);
+  if (out)
+    std::copy(t.begin(), t.begin() + std::min(cap, t.size()), out);
+  return t.size();
+}
+int lfm3_scheduler_finished(const lfm3_scheduler* scheduler, int id) {
+  if (!scheduler || !scheduler->scheduler->Finished(id))
+    return 0;
+  return scheduler->scheduler->Failed(id) ? 2 : 1;
+}
+
 uint32_t lfm3_snapshot_signature(const lfm3_config* config) {
   return config ? lfm3::SnapshotSignature(*config) : 0;
 }

@@ -1350,6 +1350,61 @@ bool Session::ForwardBatchSample(std::span<Session* const> sessions,
   }
 }
 
+bool Session::SampleLogits(const SampleControls& controls,
+                           const uint32_t* recent, uint32_t recent_count,
+                           uint64_t seed, uint32_t* token,
+                           std::string* error) {
+  const int vocab = int(config().vocab);
+  const int segments = (vocab + kSampleSegment - 1) / kSampleSegment;
+  const char* refused = nullptr;
+  if (poisoned_ || !position_)
+    refused = "no LFM3 logit frontier to select from";
+  else if (!token || (recent_count && !recent) ||
+           recent_count > uint32_t(kSampleMaxRecent))
+    refused = "invalid selection tables";
+  else if (controls.top_k < 1 || controls.top_k > kSampleMaxTopK ||
+           segments * controls.top_k > kSampleMaxCandidates)
+    refused = "sampler top_k does not fit this vocabulary";
+  for (uint32_t j = 0; j < recent_count && !refused; ++j)
+    if (recent[j] >= uint32_t(vocab))
+      refused = "recent token outside the vocabulary";
+  if (refused) {
+    if (error)
+      *error = refused;
+    return false;
+  }
+  try {
+    EnsureLogits();
+    SampleParams p{};
+    p.rows = 1;
+    p.logits = logits_.as<float>();
+    p.vocab = vocab;
+    p.ld = vocab;
+    p.segments = segments;
+    p.c = controls;
+    p.recent_count[0] = recent_count;
+    p.seed[0] = seed;
+    std::copy(recent, recent + recent_count, p.recent[0]);
+    p.cand_key = sample_scratch_.as<uint32_t>();
+    p.cand_id = p.cand_key + size_t(segments) * controls.top_k;
+    p.out = sample_out_.as<uint32_t>();
+    Timed(kRowKernels, [&] { Check(launch_sample(p, stream_)); });
+    Check(cudaMemcpyAsync(sample_host_, p.out, sizeof(uint32_t),
+                          cudaMemcpyDeviceToHost, stream_));
+    Check(cudaStreamSynchronize(stream_));
+    if (const unsigned e = take_device_error())
+      throw std::runtime_error("device wait gave up, code " +
+                               std::to_string(e));
+    *token = sample_host_[0];
+    return true;
+  } catch (const std::exception& e) {
+    poisoned_ = true;
+    if (error)
+      *error = e.what();
+    return false;
+  }
+}
+
 bool Session::ReadHidden(std::span<float> hidden, std::string* error) {
   try {
     if (hidden.size() != model_->config().hidden)

@@ -218,6 +218,13 @@ public:
                                  const uint64_t* seeds,
                                  std::span<uint32_t> next,
                                  std::string* error = nullptr);
+  // Token selection on the device from this session's own frontier logits
+  // (a prompt pass's last row): the runner's SelectNext after Prefill
+  // (runner.cpp:249-299) without the logits' trip to the host. recent holds
+  // recent_count (<= 64) tokens. Returns once the token is on the host.
+  bool SampleLogits(const SampleControls& controls, const uint32_t* recent,
+                    uint32_t recent_count, uint64_t seed, uint32_t* token,
+                    std::string* error = nullptr);
   // The final-normed hidden state / logits of the last advanced row.
   bool ReadHidden(std::span<float> hidden, std::string* error = nullptr);
   bool ReadLogits(std::span<float> logits, std::string* error = nullptr);

@@ -15,6 +15,8 @@
 // tickets are cleared on each call, and calls that overlap on the GPU (two
 // streams, or two host threads) race on it and must be serialised by the
 // caller.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "../../include/lfm3_cuda.h"
@@ -37,11 +39,36 @@ static __device__ __align__(256) float
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
+// Per device: the array's device address and the context it was looked up
+// in. cudaDeviceReset ends that context and a later call runs in a new one
+// where the module (and the array) is loaded again, possibly elsewhere, so
+// a cached address is only reused in the context it came from.
 float* g_scratch[kMaxDevices] = {};
+CUcontext g_context[kMaxDevices] = {};
+
+// The calling thread's current context (driver API, reached through the
+// runtime so the library needs no link against libcuda).
+cudaError_t current_context(CUcontext* ctx) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  static GetCurrent get = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault,
+                                &status) != cudaSuccess ||
+        status != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<GetCurrent>(fn);
+  }();
+  if (!get)
+    return cudaErrorNotSupported;
+  return get(ctx) == CUDA_SUCCESS ? cudaSuccess : cudaErrorDeviceUninitialized;
+}
 
 // The device address of g_noalloc_scratch on the current device. In host
 // code the array's name is only a host-side stand-in, so the address is
-// looked up once per device with that device current.
+// looked up with that device current: once per device and context (the
+// first call on a device, or the first after a cudaDeviceReset), and reused
+// while that context lives.
 cudaError_t scratch_address(float** out) {
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
@@ -49,13 +76,20 @@ cudaError_t scratch_address(float** out) {
     return e;
   if (device < 0 || device >= kMaxDevices)
     return cudaErrorInvalidDevice;
+  // (before the runtime's first call on this device there is no current
+  // context yet: the lookup below creates it, and the next call, seeing a
+  // different context, looks the address up once more)
+  CUcontext ctx = nullptr;
+  if ((e = current_context(&ctx)) != cudaSuccess)
+    return e;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_scratch[device]) {
+  if (!g_scratch[device] || g_context[device] != ctx) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess)
       return e;
     g_scratch[device] = static_cast<float*>(ptr);
+    g_context[device] = ctx;
   }
   *out = g_scratch[device];
   return cudaSuccess;
