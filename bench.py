@@ -500,81 +500,108 @@ class SampledRounds:
         self.tokens[:] = self.out
 
 
+CONFIG5_PROMPTS = (512, 32768)
+
+
+def config5_workload(rank, vocab):
+    """This rank's share of BASELINE config 5 (64 sessions over 8 GPUs = 8 per
+    GPU): prompt lengths log-uniform in [512, 32768] and tokens, from seed
+    (5, rank), so ranks hold different sessions."""
+    rng = np.random.default_rng([5, rank])
+    lo, hi = CONFIG5_PROMPTS
+    lengths = np.exp(rng.uniform(np.log(lo), np.log(hi), SESSIONS)).astype(int)
+    prompts = [rng.integers(0, vocab, int(n)).astype(np.uint32) for n in lengths]
+    return lengths, prompts
+
+
+def config5_rank(lfm3, model, cfg, rank, rounds, warmup=3):
+    """Config 5 on this rank's GPU: prefill its 8 sessions (512-row passes,
+    device-timed per session), then `rounds` decode rounds of the 8 ragged
+    rows (ForwardBatchInputs, logits on the device), device-timed."""
+    import torch
+    lengths, prompts = config5_workload(rank, cfg.vocab)
+    sessions = [model.session(int(n) + rounds + warmup + 16) for n in lengths]
+    prefill_ms = 0.0
+    for sess, p in zip(sessions, prompts):
+        st = torch.cuda.ExternalStream(sess.stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        sess.forward(p, logits=False)
+        b.record(st)
+        b.synchronize()
+        prefill_ms += a.elapsed_time(b)
+    tokens = [int(t) for t in np.random.default_rng([6, rank]).integers(0, cfg.vocab, SESSIONS)]
+
+    def run(k):
+        for step in range(k):
+            lfm3.Session.forward_batch_inputs(
+                sessions, [(t + step) % cfg.vocab for t in tokens], logits=True)
+
+    run(warmup)
+    depths = [sess.position for sess in sessions]
+    st = torch.cuda.ExternalStream(sessions[0].stream)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    run(rounds)
+    b.record(st)
+    b.synchronize()
+    decode_ms = a.elapsed_time(b)
+    for sess in sessions:
+        sess.close()
+    return {"prefill_tokens": int(lengths.sum()), "prefill_ms": prefill_ms,
+            "decode_ms": decode_ms, "depths": depths,
+            "lengths": [int(n) for n in lengths]}
+
+
 def config3_job(lfm3, model, cfg, rank, prompt_max, decode_tokens=256, trace=None):
-    """BASELINE config 3 as one whole job on this GPU: 8 sessions (prompts
-    U[64, prompt_max], seed (1, rank)) arriving 0-2 decode rounds apart
-    (seed (2, rank)). Each scheduler step runs one prompt pass of at most 512
-    rows for the first arrived session with prompt left (FIFO), then one
-    decode round of every decoding session with the reference runner's
-    sampler on the device (ForwardBatchSample); a session's first token is
-    selected on the host from its last pass's logits (lfm3_sample_host).
-    Every session decodes `decode_tokens` tokens. Each call returns with its
-    results on the host, so host time per call is the end-to-end time.
-    `trace`, when given, receives (step, "pass", session) and (step, "round",
-    sessions) in order."""
+    """BASELINE config 3 as one whole job on this GPU, through the library's
+    continuous-batching scheduler (lfm3_scheduler): 8 requests (prompts
+    U[64, prompt_max], seed (1, rank)) admitted 0-2 steps apart (seed
+    (2, rank)); each scheduler step runs one prompt pass of at most 512 rows
+    (first come, first served) and one decode round of every decoding
+    request, tokens selected on the device with the reference runner's
+    sampler. Every request selects `decode_tokens` tokens (the first from its
+    last prompt pass). Pass and round times are the scheduler's host times
+    (each part returns with its results on the host). `trace`, when given,
+    receives (step, "pass", request) and (step, "round", rows) in order."""
     lengths, prompts = rank_workload(rank, prompt_max, cfg.vocab)
     rng = np.random.default_rng([2, rank])
     arrive = np.concatenate([[0], np.cumsum(rng.integers(0, 3, SESSIONS - 1))])
-    sessions = [model.session(int(n) + decode_tokens + 8) for n in lengths]
-    smp = lfm3.sampler(*SAMPLER)
-    done = [0] * SESSIONS
-    decoded = [0] * SESSIONS
-    pending = [None] * SESSIONS
-    history = [list(map(int, p[-64:])) for p in prompts]
-
-    def seed(i, position):
-        return ((1000 + rank) << 40) ^ (i << 32) ^ position
-
+    sched = lfm3.Scheduler(model, lfm3.sampler(*SAMPLER))
+    ids = {}
     t_prefill = t_decode = 0.0
     prefill_tokens = decode_rows = rounds = passes = 0
     step = 0
     t_job = time.perf_counter()
-    while any(d < decode_tokens for d in decoded):
-        queue = [i for i in range(SESSIONS)
-                 if arrive[i] <= step and done[i] < len(prompts[i])]
-        if queue:
-            i = queue[0]
-            a = done[i]
-            b = min(a + 512, len(prompts[i]))
-            last = b == len(prompts[i])
-            t0 = time.perf_counter()
-            logits = sessions[i].forward(prompts[i][a:b], logits=last)
-            if last:
-                pending[i] = int(lfm3.sample_host(logits, smp, recent=[history[i]],
-                                                  seeds=[seed(i, b)])[0])
-                decoded[i] = 1
-            t_prefill += time.perf_counter() - t0
-            if trace is not None:
-                trace.append((step, "pass", i))
-            prefill_tokens += b - a
+    while len(ids) < SESSIONS or not sched.idle:
+        for i in range(SESSIONS):
+            if arrive[i] == step:
+                ids[i] = sched.admit(prompts[i], decode_tokens,
+                                     ((1000 + rank) << 40) ^ (i << 32),
+                                     int(lengths[i]) + decode_tokens + 8)
+        st = sched.step()
+        if st.pass_request >= 0:
             passes += 1
-            done[i] = b
-        live = [i for i in range(SESSIONS)
-                if pending[i] is not None and decoded[i] < decode_tokens]
-        if live:
-            for i in live:
-                history[i] = (history[i] + [pending[i]])[-64:]
-            t0 = time.perf_counter()
-            nxt = lfm3.Session.forward_batch_sample(
-                [sessions[i] for i in live], [pending[i] for i in live], smp,
-                recent=[history[i] for i in live],
-                seeds=[seed(i, sessions[i].position) for i in live])
-            t_decode += time.perf_counter() - t0
+            prefill_tokens += st.pass_rows
+            t_prefill += st.pass_ms / 1e3
             if trace is not None:
-                trace.append((step, "round", live))
-            for i, t in zip(live, nxt):
-                pending[i] = int(t)
-                decoded[i] += 1
-            decode_rows += len(live)
+                trace.append((step, "pass", int(st.pass_request)))
+        if st.round_rows:
             rounds += 1
+            decode_rows += st.round_rows
+            t_decode += st.round_ms / 1e3
+            if trace is not None:
+                trace.append((step, "round", int(st.round_rows)))
         step += 1
     t_job = time.perf_counter() - t_job
-    for s in sessions:
-        s.close()
+    for i in range(SESSIONS):
+        if len(sched.tokens(ids[i])) != decode_tokens:
+            raise RuntimeError(f"request {i} ended early")
+    sched.close()
     return {"decode_tokens": decode_rows, "decode_s": t_decode,
             "prefill_tokens": prefill_tokens, "prefill_s": t_prefill,
             "job_s": t_job, "rounds": rounds, "passes": passes,
-            "arrivals": [int(a) for a in arrive]}
+            "steps": step, "arrivals": [int(a) for a in arrive]}
 
 
 def job_rate(tokens_per_rank, world, max_ms):
@@ -814,7 +841,9 @@ def main():
     lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
     weights = lfm3.SyntheticWeights(seed=0)
     cfg = weights.config
-    model = lfm3.Model(weights.weights)
+    t_load = time.perf_counter()
+    model = lfm3.Model(weights.weights)  # upload + the decode copies' packing
+    load_s = time.perf_counter() - t_load
     lengths, prompts = rank_workload(rank, args.prompt_max, cfg.vocab)
     total_steps = args.warmup * 2 + args.steps * 3 + 8
     sessions = [model.session(int(n) + total_steps + 16) for n in lengths]
@@ -952,6 +981,14 @@ def main():
                "sample": f"{threads} sessions x 6 decode tokens at depth 3, one session "
                          f"per host thread ({elapsed:.1f} s)"}
 
+    # ---- this GPU's 8 sessions of the 64 (prompts
+    # log-uniform [512, 32768]), prefill then decode rounds
+    c5_rounds = 64
+    c5 = config5_rank(lfm3, model, cfg, rank, c5_rounds)
+    c5_prefill_ms = sync_max(c5["prefill_ms"])
+    c5_decode_ms = sync_max(c5["decode_ms"])
+    c5_prefill_tokens = ranks.sync_sum(c5["prefill_tokens"])
+
     # ---- BASELINE config 3 as a whole job (arrivals, passes between rounds)
     job = config3_job(lfm3, model, cfg, rank, args.prompt_max)
     job_decode_s = sync_max(job["decode_s"])
@@ -962,6 +999,7 @@ def main():
     e2e = job_rate(SESSIONS * args.steps, world, sampled_ms_max)
     e2e_logits = job_rate(SESSIONS * args.steps, world, e2e_ms_max)
     prefill_rate = ranks.sync_sum(prefill_tokens) / (sync_max(prefill_ms) / 1e3)
+    load_s_max = sync_max(load_s)
     if rank != 0:
         ranks.close()
         return
@@ -1041,10 +1079,26 @@ def main():
             "decode_tokens": job["decode_tokens"] * world,
             "prefill_tokens": job["prefill_tokens"] * world,
             "arrivals_rank0": job["arrivals"],
-            "how": "8 sessions/GPU, prompts U[64,4096], arrivals 0-2 rounds apart; each "
-                   "step one <=512-row prompt pass (FIFO) then one decode round of every "
-                   "decoding session with device sampling; 256 tokens per session; "
-                   "host-timed calls, max over ranks"},
+            "how": "lfm3_scheduler: 8 requests/GPU, prompts U[64,4096], admitted 0-2 "
+                   "steps apart; each step one <=512-row prompt pass (FIFO) then one "
+                   "decode round of every decoding request with device sampling; 256 "
+                   "tokens per request; host times of the scheduler's parts, max over "
+                   "ranks"},
+        "config5": {
+            "sessions": SESSIONS * world, "per_gpu": SESSIONS,
+            "prefill_tok_s": c5_prefill_tokens / (c5_prefill_ms / 1e3),
+            "decode_tok_s": job_rate(SESSIONS * c5_rounds, world, c5_decode_ms),
+            "decode_ms_per_round": c5_decode_ms / c5_rounds,
+            "rounds": c5_rounds, "prompt_lengths_rank0": c5["lengths"],
+            "how": "each rank its 8 sessions (prompts log-uniform [512, 32768], seed "
+                   "(5, rank)), prefilled in 512-row passes (device-timed per "
+                   "session), then 64 ForwardBatchInputs rounds of the 8 rows; "
+                   "aggregate tokens over the max time over ranks"},
+        "load": {"seconds": load_s_max, "weight_bytes": int(model.weight_bytes),
+                 "host_to_device_gb_s": model.weight_bytes / load_s_max / 1e9,
+                 "how": "Model::Load from host memory (pinned staging, 4 reader "
+                        "threads) plus packing the decode copies on the device; max "
+                        "over ranks"},
         "gpu_launches": int(launches),
         "clocks": clocks,
     }

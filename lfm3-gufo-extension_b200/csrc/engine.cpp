@@ -9,9 +9,12 @@
 
 #include <algorithm>
 #include <cmath>
+#include <condition_variable>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <stdexcept>
+#include <thread>
 #include <unordered_set>
 
 #include "kernels.cuh"
@@ -102,6 +105,115 @@ void VisitTensors(lfm3_weights& w, F f) {
 
 int CeilDiv(int a, int b) { return (a + b - 1) / b; }
 
+// Host payloads to device memory through pinned staging: reader threads
+// copy pieces of the payloads (in host-address order, i.e. file order for a
+// mapped checkpoint) into a pool of pinned buffers and queue each buffer's
+// asynchronous copy to its device destination; a buffer is reused once its
+// copy has completed (its event). Pageable memory copied by cudaMemcpy
+// goes through one internal staging buffer per call from one thread; this
+// keeps several host readers and the copy engine busy at once, the role of
+// the reference's parallel reader (upload.cpp:33-68).
+class StagedUpload {
+public:
+  static constexpr size_t kPiece = 32ull << 20;
+  static constexpr int kBuffers = 6;
+
+  struct Copy {
+    const char* host;
+    char* device;
+    size_t bytes;
+  };
+
+  explicit StagedUpload(int readers) : readers_(std::max(1, readers)) {}
+
+  void Add(const void* host, void* device, size_t bytes) {
+    for (size_t off = 0; off < bytes; off += kPiece)
+      copies_.push_back({static_cast<const char*>(host) + off,
+                         static_cast<char*>(device) + off,
+                         std::min(kPiece, bytes - off)});
+  }
+
+  // Runs every queued copy; throws on a CUDA failure (after the readers
+  // have stopped and the queued copies have finished).
+  void Run() {
+    if (copies_.empty())
+      return;
+    cudaStream_t stream = nullptr;
+    Throw(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    std::vector<void*> staging(kBuffers, nullptr);
+    std::vector<cudaEvent_t> done(kBuffers, nullptr);
+    cudaError_t failure = cudaSuccess;
+    for (int b = 0; b < kBuffers && failure == cudaSuccess; ++b) {
+      failure = cudaHostAlloc(&staging[b], kPiece, cudaHostAllocDefault);
+      if (failure == cudaSuccess)
+        failure = cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming);
+    }
+    if (failure == cudaSuccess) {
+      std::vector<int> free_buffers;
+      for (int b = 0; b < kBuffers; ++b)
+        free_buffers.push_back(b);
+      std::mutex mu;
+      std::condition_variable cv;
+      size_t next = 0;
+      const auto reader = [&] {
+        for (;;) {
+          int b = -1;
+          size_t i = 0;
+          {
+            std::unique_lock<std::mutex> lock(mu);
+            cv.wait(lock, [&] {
+              return !free_buffers.empty() || next == copies_.size() ||
+                     failure != cudaSuccess;
+            });
+            if (next == copies_.size() || failure != cudaSuccess)
+              return;
+            b = free_buffers.back();
+            free_buffers.pop_back();
+            i = next++;
+          }
+          // the buffer's previous copy must have left it
+          cudaError_t e = cudaEventSynchronize(done[b]);
+          const Copy& c = copies_[i];
+          if (e == cudaSuccess) {
+            std::memcpy(staging[b], c.host, c.bytes);
+            e = cudaMemcpyAsync(c.device, staging[b], c.bytes,
+                                cudaMemcpyHostToDevice, stream);
+          }
+          if (e == cudaSuccess)
+            e = cudaEventRecord(done[b], stream);
+          {
+            std::lock_guard<std::mutex> lock(mu);
+            if (e != cudaSuccess && failure == cudaSuccess)
+              failure = e;
+            free_buffers.push_back(b);
+          }
+          cv.notify_all();
+        }
+      };
+      std::vector<std::thread> threads;
+      for (int t = 0; t < std::min<int>(readers_, kBuffers); ++t)
+        threads.emplace_back(reader);
+      for (auto& t : threads)
+        t.join();
+    }
+    const cudaError_t sync = cudaStreamSynchronize(stream);
+    if (failure == cudaSuccess)
+      failure = sync;
+    for (int b = 0; b < kBuffers; ++b) {
+      if (done[b])
+        cudaEventDestroy(done[b]);
+      if (staging[b])
+        cudaFreeHost(staging[b]);
+    }
+    cudaStreamDestroy(stream);
+    Throw(failure);
+  }
+
+private:
+  int readers_;
+  std::vector<Copy> copies_;
+};
+
 }  // namespace
 
 // ---- DeviceBuffer -------------------------------------------------------------
@@ -142,8 +254,9 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
     Throw(cudaGetDevice(&device));
     Throw(cudaDeviceGetAttribute(&m->sms_, cudaDevAttrMultiProcessorCount,
                                  device));
-    // Distinct payloads in host order, packed into <=128 MiB segments with
-    // 256-byte alignment (upload.cpp:12-16, 33-68).
+    // Distinct payloads in host order (a mapped checkpoint's file order),
+    // packed into <=128 MiB segments with 256-byte alignment
+    // (upload.cpp:12-16, 33-68), filled through pinned staging.
     std::map<const void*, size_t> payloads;
     VisitTensors(m->device_, [&](lfm3_tensor& t) {
       auto& bytes = payloads[t.data];
@@ -151,6 +264,7 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
     });
     constexpr size_t kSegment = 128ull << 20, kAlign = 256;
     std::map<const void*, void*> placed;
+    StagedUpload upload(int(std::min(4u, std::max(1u, std::thread::hardware_concurrency()))));
     auto it = payloads.begin();
     while (it != payloads.end()) {
       size_t bytes = 0;
@@ -163,12 +277,13 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
       m->segments_.emplace_back(bytes);
       char* dst = m->segments_.back().as<char>();
       for (; it != end; ++it) {
-        Throw(cudaMemcpy(dst, it->first, it->second, cudaMemcpyHostToDevice));
+        upload.Add(it->first, dst, it->second);
         placed[it->first] = dst;
         dst += (it->second + kAlign - 1) / kAlign * kAlign;
       }
       m->weight_bytes_ += bytes;
     }
+    upload.Run();
     VisitTensors(m->device_, [&](lfm3_tensor& t) { t.data = placed.at(t.data); });
     if (!m->bf16())
       m->PackDecodeGroups();

@@ -31,8 +31,11 @@ def _rank_main(rank, world, port, out_dir):
     slowest = ranks.sync_max(10.0 + ranks.rank)
     tokens = ranks.sync_sum(float(sum(len(p) for p in prompts)))
     ranks.barrier()
+    c5_lengths, c5_prompts = bench.config5_workload(ranks.rank, 65536)
     record = {"rank": ranks.rank, "world": ranks.world, "slowest": slowest,
               "tokens": tokens, "lengths": [int(n) for n in lengths],
+              "c5_lengths": [int(n) for n in c5_lengths],
+              "c5_heads": [[int(t) for t in p[:4]] for p in c5_prompts],
               "rate": bench.job_rate(bench.SESSIONS * 4, ranks.world, slowest)}
     with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
         json.dump(record, f)
@@ -53,6 +56,12 @@ def test_two_rank_replicas(tmp_path):
     assert all(64 <= n <= 4096 for r in recs for n in r["lengths"])
     total = sum(sum(r["lengths"]) for r in recs)
     assert all(r["tokens"] == total for r in recs)
+    # config 5's 64 sessions: 8 per rank, disjoint between ranks, prompts
+    # log-uniform in [512, 32768]
+    assert all(len(r["c5_lengths"]) == 8 for r in recs)
+    assert all(512 <= n <= 32768 for r in recs for n in r["c5_lengths"])
+    heads = [tuple(h) for r in recs for h in r["c5_heads"]]
+    assert len(set(heads)) == len(heads)
     # whole-job rate: 8 sessions x 4 steps on each of 2 ranks over 11 ms
     assert recs[0]["rate"] == pytest.approx(8 * 4 * 2 / 0.011)
 
