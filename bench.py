@@ -165,7 +165,7 @@ def measured_peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def committed_traffic(kernel="q8_gemv_decode"):
+def committed_traffic(kernel="decode_gemv_round"):
     """DRAM bytes (read + write) per launch of a kernel from one ncu capture,
     kept in profiles/traffic.json beside the summary it comes from."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -617,9 +617,9 @@ PROFILE_WARM_ROUNDS = 3
 def profile_sequence():
     """A fixed, untimed launch sequence for ncu: 8 sessions prefilled with
     64-token prompts (one prompt pass each, whose last row's logits take one
-    LM-head q8_gemv launch), 3 warm decode rounds, then the captured work: one
+    LM-head decode_gemv launch), 3 warm decode rounds, then the captured work: one
     decode round of the 8 rows, then one 512-row prompt pass on session 0.
-    Before the captured round: 8 + 3 x 97 = 299 q8_gemv launches and
+    Before the captured round: 8 + 3 x 97 = 299 decode_gemv launches and
     8 x 96 = 768 q8_prefill_tc_kernel launches (24 layers: 4 projection
     launches per layer)."""
     import torch
@@ -1028,20 +1028,20 @@ def main():
             "l2": "inputs larger than L2: each round streams 1.78 GB of weights",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "q8_gemv_kernel (decode projections + LM head)",
+            "bound": "hbm", "kernel": "decode_gemv_kernel (decode projections + LM head)",
             "achieved": weight_bytes / step_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
             "frac": weight_bytes / step_s / 1e9 / hbm_peak,
             "traffic": traffic * launches_per_round if traffic else None,
-            "traffic_unit": "bytes per round (ncu, all q8_gemv launches of one round)",
+            "traffic_unit": "bytes per round (ncu, all decode_gemv launches of one round)",
             "peak_source": f"{peak_source} hbm_gbs",
-            "how": "Q8 weight bytes of one round (read once by the round's q8_gemv "
+            "how": "Q8 weight bytes of one round (read once by the round's decode_gemv "
                    "launches) / the timed ms_per_step: the whole round is charged to "
                    "the projections, so this is a lower bound of their bandwidth",
         },
         "serialised_gemv": {
             "achieved": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / hbm_peak,
             "how": f"Q8 weight bytes of {profiled_rounds} rounds / summed CUDA-event "
-                   f"time of their {proj_launches} q8_gemv launches in a separate "
+                   f"time of their {proj_launches} decode_gemv launches in a separate "
                    "profiled pass (events serialise the launches: not the headline)",
         },
         "step_roofline": {

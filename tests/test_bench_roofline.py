@@ -44,10 +44,10 @@ def test_traffic_comes_from_the_data_file():
     """roofline.traffic reads profiles/traffic.json (never a Markdown
     summary); the recorded round traffic is within a few percent of the
     algorithmic weight bytes (every weight byte read once)."""
-    per_launch = bench.committed_traffic("q8_gemv_decode")
+    per_launch = bench.committed_traffic("decode_gemv_round")
     assert per_launch is not None
     import json
-    entry = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))["q8_gemv_decode"]
+    entry = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))["decode_gemv_round"]
     assert per_launch == entry["dram_bytes_per_launch"]
     ratio = per_launch / entry["algorithmic_bytes_per_launch"]
     assert 0.99 < ratio < 1.05
