@@ -168,6 +168,17 @@ int lfm3_cuda_attention_decode_noalloc(const float* q, const uint16_t* k,
                                        int heads, int kv_heads, int dim,
                                        int position, int capacity, int window,
                                        void* stream);
+/* No counterpart in the reference: lfm3_cuda_attention with window 0 when
+ * every key, the chunk's own included, is already in the cache (store the
+ * chunk with lfm3_cuda_store_kv first; position + n <= capacity, so nothing
+ * wraps). The engine's prompt pass of the full-attention layers: tcgen05
+ * tensor cores with TMA-loaded key tiles, the same FP16 roundings of Q and
+ * probabilities and the same scratch as lfm3_cuda_attention. n >= 1. */
+int lfm3_cuda_attention_stored(const float* q, const float* gate,
+                               const uint16_t* cache_k,
+                               const uint16_t* cache_v, float* out, int n,
+                               int heads, int kv_heads, int dim, int position,
+                               int capacity, void* stream, float* scratch);
 /* AttentionScratchBytes (hip/ops.hpp:99). */
 size_t lfm3_cuda_attention_scratch_bytes(int heads, int dim, int context,
                                          int rows);

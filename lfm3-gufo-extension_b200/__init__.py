@@ -58,6 +58,8 @@ def library():
         "lfm3_cuda_rope": ([P, P, P, I, I, I, I, P], I),
         "lfm3_cuda_attention": ([P, P, P, P, P, P, P, I, I, I, I, I, I, I, P,
                                  P], I),
+        "lfm3_cuda_attention_stored": ([P, P, P, P, P, I, I, I, I, I, I, P,
+                                        P], I),
         "lfm3_cuda_attention_scratch_bytes": ([I, I, I, I], SZ),
         "lfm3_cuda_attention_decode_noalloc": ([P, P, P, P, P, P, P, I, I, I,
                                                 I, I, I, P], I),

@@ -25,7 +25,8 @@ CUDA_FLAGS = ARCH + [
     "--expt-relaxed-constexpr",
 ]
 SOURCES = [
-    "abi.cu", "attention_decode.cu", "attention_prompt.cu", "conv.cu",
+    "abi.cu", "attention_decode.cu", "attention_prompt.cu",
+    "attention_prompt_tc.cu", "conv.cu",
     "device_error.cu", "engine.cpp", "noalloc.cu", "norm.cu", "q8_decode.cu",
     "q8_gemv.cu",
     "q8_prefill.cu", "sampling.cu", "scheduler.cpp",

@@ -482,6 +482,23 @@ int lfm3_cuda_attention(const float* q, const uint16_t* k, const uint16_t* v,
       position, capacity, window, scratch, s));
 }
 
+int lfm3_cuda_attention_stored(const float* q, const float* gate,
+                               const uint16_t* cache_k,
+                               const uint16_t* cache_v, float* out, int n,
+                               int heads, int kv_heads, int dim, int position,
+                               int capacity, void* stream, float* scratch) {
+  if (dim != 128 || kv_heads <= 0 || heads % kv_heads ||
+      (heads / kv_heads != 2 && heads / kv_heads != 4 && heads / kv_heads != 8))
+    return Fail(LFM3_ERR_UNSUPPORTED, "unsupported LFM3 attention shape");
+  if (!q || !gate || !cache_k || !cache_v || !out || !scratch || n <= 0 ||
+      position < 0 || position + n > capacity)
+    return Fail(LFM3_ERR_INVALID, "invalid stored-key attention arguments");
+  return Cuda(lfm3::launch_prompt_attention_tc(
+      q, heads * 128, reinterpret_cast<const __half*>(cache_k),
+      reinterpret_cast<const __half*>(cache_v), gate, heads, out, n, heads,
+      kv_heads, position, capacity, scratch, Stream(stream)));
+}
+
 int lfm3_cuda_prompt_heads(float* q, float* k, const float* v,
                            const float* q_norm, const float* k_norm,
                            const float* frequencies, const float* factors,

@@ -110,6 +110,25 @@ cudaError_t launch_prompt_attention(const float* q, int ldq, const __half* k16,
                                     cudaStream_t stream, bool pdl = false);
 size_t prompt_attention_scratch_floats(int heads, int rows, int keys);
 
+// The same attention with window 0 when every key, the chunk's own
+// included, is already in the ring (position + n <= capacity, no wrap): the
+// prompt pass of the full-attention layers. tcgen05 tensor cores with
+// TMA-loaded K/V tiles; the same FP16 roundings of Q and P, the same spans
+// and the same scratch as launch_prompt_attention.
+cudaError_t launch_prompt_attention_tc(const float* q, int ldq,
+                                       const __half* ring_k,
+                                       const __half* ring_v, const float* gate,
+                                       int ldg, float* out, int n, int heads,
+                                       int kv_heads, int position,
+                                       int capacity, float* scratch,
+                                       cudaStream_t stream, bool pdl = false);
+// Merges the spans' (maximum, sum, output) partials of either kernel and
+// applies the gate.
+cudaError_t launch_prompt_combine(const float* partial, const float* gate,
+                                  int ldg, float* out, int n, int heads,
+                                  int spans, cudaStream_t stream,
+                                  bool pdl = false);
+
 // Copies the last min(n, capacity) chunk rows into the ring at
 // position (hip/ops.hip:1737-1749).
 cudaError_t launch_store_kv(const __half* k16, const __half* v16,

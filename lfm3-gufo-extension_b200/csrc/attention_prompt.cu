@@ -450,6 +450,14 @@ cudaError_t launch_prompt_attention(const float* q, int ldq, const __half* k16,
                        ldg, out, n, heads, a.spans);
 }
 
+cudaError_t launch_prompt_combine(const float* partial, const float* gate,
+                                  int ldg, float* out, int n, int heads,
+                                  int spans, cudaStream_t stream, bool pdl) {
+  return launch_kernel(prompt_combine_kernel, dim3(n * heads), dim3(kHeadDim),
+                       0, stream, pdl, partial, gate, ldg, out, n, heads,
+                       spans);
+}
+
 cudaError_t launch_store_kv(const __half* k16, const __half* v16,
                             __half* ring_k, __half* ring_v, int n, int stride,
                             int position, int capacity, cudaStream_t stream,

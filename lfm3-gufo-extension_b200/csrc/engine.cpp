@@ -1018,12 +1018,20 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
       const int skip = n - std::min(n, rows_out);
       float* a = a_.as<float>();
       Timed(kPromptAttention, [&] {
-        Check(launch_prompt_attention(
-            q + size_t(skip) * A, A, kc + size_t(skip) * stride,
-            vc + size_t(skip) * stride, st.k.as<__half>(), st.v.as<__half>(),
-            g + size_t(skip) * c.heads, c.heads, a + size_t(skip) * A,
-            n - skip, c.heads, kvh, int(position_) + skip, int(st.capacity),
-            swa ? int(c.window) : 0, prompt_scratch_.as<float>(), s, kPdl));
+        if (swa)
+          Check(launch_prompt_attention(
+              q + size_t(skip) * A, A, kc + size_t(skip) * stride,
+              vc + size_t(skip) * stride, st.k.as<__half>(),
+              st.v.as<__half>(), g + size_t(skip) * c.heads, c.heads,
+              a + size_t(skip) * A, n - skip, c.heads, kvh,
+              int(position_) + skip, int(st.capacity), int(c.window),
+              prompt_scratch_.as<float>(), s, kPdl));
+        else  // every key is in the cache already
+          Check(launch_prompt_attention_tc(
+              q + size_t(skip) * A, A, st.k.as<__half>(), st.v.as<__half>(),
+              g + size_t(skip) * c.heads, c.heads, a + size_t(skip) * A,
+              n - skip, c.heads, kvh, int(position_) + skip,
+              int(st.capacity), prompt_scratch_.as<float>(), s, kPdl));
       });
       if (swa)
         other([&] {
