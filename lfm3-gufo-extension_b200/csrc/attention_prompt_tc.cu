@@ -9,20 +9,30 @@
 //
 // A CTA owns one KV group and 128 / G queries of it: the G heads' query rows
 // (head-major) make the M = 128 rows of every MMA, so each key tile serves
-// the whole group. Per tile of 64 keys:
-//   S = Q K^T     M128 N64, 8 K16 steps, FP32 in tensor memory
-//   softmax       thread r owns row r (its tensor-memory lane): reads S,
-//                 masks causally, rescales its O row in tensor memory when
-//                 the row maximum moves, writes its P row (fp16) to shared
-//                 memory; the four softmax warps also transpose the V tile
-//                 into the K-major operand layout
-//   O += P V      M128 N128, 4 K16 steps, FP32 in tensor memory
+// the whole group. Per tile j of 64 keys:
+//   S_j = Q K_j^T   M128 N64, 8 K16 steps, into one of two FP32 buffers in
+//                   tensor memory; S_{j+2} is issued as soon as the softmax
+//                   has read S_j, so scores never wait for P V
+//   softmax         thread r owns row r (its tensor-memory lane): reads S_j,
+//                   masks causally and writes its P row (fp16) into one of
+//                   two shared buffers
+//   O += P_j V_j    M128 N160, 4 K16 steps; B is V_j read as an MN-major
+//                   operand straight from the TMA tile (no transpose) plus a
+//                   block of ones, so columns 128..159 of the accumulator
+//                   sum the rounded probabilities (the softmax denominator)
+// A row's probabilities are taken against a reference maximum m, not the
+// exact running maximum: m moves (and the row's O and denominator are
+// rescaled in tensor memory) only when a tile's maximum passes it by more
+// than kRescaleSlack, so rescales, which must wait for the previous P V,
+// are rare. P = 2^(s - m) <= 2^8 is still rounded to FP16 once; O / l is
+// the same quantity the reference normalises.
 // Warp roles: warps 0-3 softmax and epilogue, warp 4 the TMA producer (K and
-// V tiles of 64 keys from the F16 cache, two stages, 64-byte swizzle),
-// warp 5 tensor-memory allocation and (one thread) every MMA. Every
-// handover is an mbarrier and every wait is bounded: a pipeline that stops
-// reports kErrPrefillWait, the warps skip to the end and the tensor memory
-// is freed.
+// V tiles of 64 keys from the F16 cache, four stages, 64-byte swizzle),
+// warp 5 tensor-memory allocation and (one thread) every MMA; the MMA
+// commits release the K and V stages and the P buffers. Every wait is
+// bounded: a pipeline that stops reports kErrPrefillWait, the warps skip to
+// the end, the copies and MMAs in flight are waited for and the tensor
+// memory is freed.
 #include "attention.cuh"
 #include "common.cuh"
 #include "kernels.cuh"
@@ -34,27 +44,37 @@ namespace {
 
 constexpr int kRowsTc = 128;  // query rows per CTA (M)
 constexpr int kKeysTc = 64;   // keys per tile
-constexpr int kStagesTc = 2;
+constexpr int kStagesTc = 4;
 constexpr int kThreadsTc = 6 * 32;
 constexpr int kMinSpanTc = 1024, kMaxSpansTc = 8;  // as the mma.sync kernel
-constexpr uint32_t kColS = 0, kColO = 128, kColumns = 256;
+// A row's probabilities are taken against a reference maximum that moves
+// (rescaling O) only when the running maximum passes it by more than this
+// (base 2): P <= 2^8 stays well inside FP16.
+constexpr float kRescaleSlack = 8.0F;
+// tensor memory: S buffers at columns 0 and 64; O at 128 .. 255 and the
+// softmax denominators (P times a block of ones) at 256 .. 287
+constexpr uint32_t kColO = 128, kColL = 256, kColumns = 512;
 constexpr uint32_t kIdescS = tc::f16_idesc(kRowsTc, kKeysTc);
-constexpr uint32_t kIdescO = tc::f16_idesc(kRowsTc, kHeadDim);
-constexpr uint32_t kStageBytes = 2 * 4 * kKeysTc * 64;  // K and V of a tile
+constexpr uint32_t kIdescO = tc::f16_idesc(kRowsTc, kHeadDim + 32, true);
+constexpr uint32_t kChunkBytes = kKeysTc * 64;  // 64 keys x 32 dims
+constexpr uint32_t kTileBytes = 4 * kChunkBytes;
 
 struct __align__(1024) PromptTcSmem {
   uint8_t q[4][kRowsTc * 64];             // Q rows, 4 chunks of 32 dims
-  uint8_t k[kStagesTc][4][kKeysTc * 64];  // K tiles [key][dim]
-  uint8_t v[kStagesTc][4][kKeysTc * 64];  // V tiles [key][dim]
-  uint8_t vt[2][kHeadDim * 64];           // V^T [dim][key], 2 chunks of keys
-  uint8_t p[2][kRowsTc * 64];             // P [row][key], 2 chunks of keys
-  uint64_t kv_full[kStagesTc], kv_empty[kStagesTc];
-  uint64_t q_full, s_full, s_empty, p_full, o_done, mma_idle;
+  uint8_t k[kStagesTc][4][kChunkBytes];   // K tiles [key][32 dims] x 4
+  // V tiles [key][32 dims] x 4, then a block of ones: P V and the row
+  // sums of the rounded P in one MMA (N = 160)
+  uint8_t v[kStagesTc][5][kChunkBytes];
+  uint8_t p[2][2][kRowsTc * 64];          // P [row][key], 2 chunks of keys
+  uint64_t k_full[kStagesTc], k_empty[kStagesTc];
+  uint64_t v_full[kStagesTc], v_empty[kStagesTc];
+  uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
+  uint64_t q_full, mma_idle;
   uint32_t tmem_base;
 };
 
 struct PromptTcArgs {
-  alignas(64) CUtensorMap kmap;  // the K ring [capacity][kv_heads * 128]
+  alignas(64) CUtensorMap kmap;  // K ring rows [position + n][kv_heads * 128]
   alignas(64) CUtensorMap vmap;
   const float* q;  // [rows][ldq], normalised and rotated
   int ldq;
@@ -64,6 +84,12 @@ struct PromptTcArgs {
   float* partial;  // spans > 1: [spans][rows][heads][130]
   int n, heads, kv_heads, group, position, span, spans;
 };
+
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ uint32_t pack2(__half a, __half b) {
   const __half2 h = __halves2half2(a, b);
@@ -80,21 +106,24 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   const int q0 = blockIdx.x * QB, grp = blockIdx.y, split = blockIdx.z;
   const int P = a.position;
   const int nq = min(QB, a.n - q0);
-  const int span_first = split * a.span, span_last = span_first + a.span - 1;
-  const int first_key = span_first;
+  const int first_key = split * a.span, span_last = first_key + a.span - 1;
   const int last_key = min(P + q0 + nq - 1, span_last);
   const int tiles =
       first_key <= last_key ? (last_key - first_key) / kKeysTc + 1 : 0;
   if (tid == 0) {
     for (int i = 0; i < kStagesTc; ++i) {
-      mbar_init(&s.kv_full[i], 1);
-      mbar_init(&s.kv_empty[i], 4);
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+      mbar_init(&s.v_full[i], 1);
+      mbar_init(&s.v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.s_full[i], 1);
+      mbar_init(&s.s_empty[i], 4);
+      mbar_init(&s.p_full[i], 4);
+      mbar_init(&s.p_empty[i], 1);
     }
     mbar_init(&s.q_full, 4);
-    mbar_init(&s.s_full, 1);
-    mbar_init(&s.s_empty, 4);
-    mbar_init(&s.p_full, 4);
-    mbar_init(&s.o_done, 1);
     mbar_init(&s.mma_idle, 1);
     fence_barrier_init();
   }
@@ -114,58 +143,77 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       int issued = 0;
       for (int j = 0; j < tiles && ok; ++j) {
         const int st = j % kStagesTc;
+        const uint32_t reuse = ((j / kStagesTc) - 1) & 1;
+        const int key0 = first_key + j * kKeysTc;
         if (j >= kStagesTc &&
-            !mbar_wait(&s.kv_empty[st], ((j / kStagesTc) - 1) & 1,
-                       kErrPrefillWait)) {
+            !mbar_wait(&s.k_empty[st], reuse, kErrPrefillWait)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&s.kv_full[st], kStageBytes);
-        ++issued;
-        const int key0 = first_key + j * kKeysTc;
+        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int x = grp * kHeadDim + c * 32;
-          tma_load_2d(s.k[st][c], &a.kmap, x, key0, &s.kv_full[st]);
-          tma_load_2d(s.v[st][c], &a.vmap, x, key0, &s.kv_full[st]);
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(s.k[st][c], &a.kmap, grp * kHeadDim + c * 32, key0,
+                      &s.k_full[st]);
+        if (j >= kStagesTc &&
+            !mbar_wait(&s.v_empty[st], reuse, kErrPrefillWait)) {
+          ok = false;
+          break;
         }
+        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(s.v[st][c], &a.vmap, grp * kHeadDim + c * 32, key0,
+                      &s.v_full[st]);
+        ++issued;
       }
-      // no copy may still be landing when the block exits (error paths)
-      for (int j = max(0, issued - kStagesTc); j < issued; ++j)
-        mbar_wait(&s.kv_full[j % kStagesTc], (j / kStagesTc) & 1,
+      // no copy may still be landing when the block exits (error paths;
+      // a K tile whose V was never issued has landed by the V wait above)
+      for (int j = max(0, issued - kStagesTc); j < issued; ++j) {
+        mbar_wait(&s.k_full[j % kStagesTc], (j / kStagesTc) & 1,
                   kErrPrefillWait);
+        mbar_wait(&s.v_full[j % kStagesTc], (j / kStagesTc) & 1,
+                  kErrPrefillWait);
+      }
     }
   } else if (warp == 5) {
-    // ---- MMA issue (one thread)
+    // ---- MMA issue (one thread): S_0, then per tile S_{j+1} ahead of
+    // P_j V_j
     if (lane == 0 && tiles > 0) {
-      ok = mbar_wait(&s.q_full, 0, kErrPrefillWait);
-      for (int j = 0; j < tiles && ok; ++j) {
-        const int st = j % kStagesTc;
-        if (!mbar_wait(&s.kv_full[st], (j / kStagesTc) & 1,
-                       kErrPrefillWait) ||
-            (j > 0 && !mbar_wait(&s.s_empty, (j - 1) & 1, kErrPrefillWait))) {
-          ok = false;
-          break;
-        }
+      const auto scores = [&](int i) {
+        const int st = i % kStagesTc, b = i & 1;
+        if (!mbar_wait(&s.k_full[st], (i / kStagesTc) & 1, kErrPrefillWait) ||
+            (i >= 2 &&
+             !mbar_wait(&s.s_empty[b], ((i >> 1) - 1) & 1, kErrPrefillWait)))
+          return false;
         tc::fence_after();
 #pragma unroll
         for (int k16 = 0; k16 < 8; ++k16)
-          tc::mma(tmem + kColS,
-                  tc::sw64_desc(s.q[k16 / 2]) + (k16 % 2) * 2,
+          tc::mma(tmem + b * kKeysTc, tc::sw64_desc(s.q[k16 / 2]) + (k16 % 2) * 2,
                   tc::sw64_desc(s.k[st][k16 / 2]) + (k16 % 2) * 2, kIdescS,
                   k16 > 0);
-        tc::commit(&s.s_full);
-        if (!mbar_wait(&s.p_full, j & 1, kErrPrefillWait)) {
+        tc::commit(&s.k_empty[st]);
+        tc::commit(&s.s_full[b]);
+        return true;
+      };
+      ok = mbar_wait(&s.q_full, 0, kErrPrefillWait) && scores(0) &&
+           (tiles < 2 || scores(1));
+      for (int j = 0; j < tiles && ok; ++j) {
+        const int st = j % kStagesTc, b = j & 1;
+        if ((j + 2 < tiles && !scores(j + 2)) ||
+            !mbar_wait(&s.v_full[st], (j / kStagesTc) & 1, kErrPrefillWait) ||
+            !mbar_wait(&s.p_full[b], (j >> 1) & 1, kErrPrefillWait)) {
           ok = false;
           break;
         }
         tc::fence_after();
 #pragma unroll
         for (int k16 = 0; k16 < 4; ++k16)
-          tc::mma(tmem + kColO, tc::sw64_desc(s.p[k16 / 2]) + (k16 % 2) * 2,
-                  tc::sw64_desc(s.vt[k16 / 2]) + (k16 % 2) * 2, kIdescO,
+          tc::mma(tmem + kColO, tc::sw64_desc(s.p[b][k16 / 2]) + (k16 % 2) * 2,
+                  tc::sw64_mn_desc(s.v[st][0], kChunkBytes) + k16 * 64, kIdescO,
                   j > 0 || k16 > 0);
-        tc::commit(&s.o_done);
+        tc::commit(&s.v_empty[st]);
+        tc::commit(&s.p_empty[b]);
       }
       // every MMA issued has finished before the tensor memory is freed
       tc::commit(&s.mma_idle);
@@ -203,6 +251,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         *reinterpret_cast<uint4*>(s.q[piece / 4] +
                                   tc::sw64_offset(t, piece % 4)) = packed;
       }
+      // the ones blocks of the V stages (fp16 1.0), 128 bytes a thread
+#pragma unroll
+      for (int i = 0; i < kStagesTc * kChunkBytes / (16 * 128); ++i) {
+        const int byte = (i * 128 + t) * 16;
+        *reinterpret_cast<uint4*>(s.v[byte / kChunkBytes][4] +
+                                  byte % kChunkBytes) =
+            make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+      }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0)
@@ -213,96 +269,81 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, kErrPrefillWait));
     };
-    float m = -INFINITY, l = 0;
+    float m = -INFINITY;
     for (int j = 0; j < tiles && ok; ++j) {
-      const int st = j % kStagesTc;
+      const int b = j & 1;
       const int key0 = first_key + j * kKeysTc;
-      if (!wait_all(&s.s_full, j & 1) ||
-          !wait_all(&s.kv_full[st], (j / kStagesTc) & 1)) {
+      if (!wait_all(&s.s_full[b], (j >> 1) & 1)) {
         ok = false;
         break;
       }
       tc::fence_after();
       uint32_t sv[64];
-      tc::ld32(lane_base + kColS, *reinterpret_cast<uint32_t(*)[32]>(sv));
-      tc::ld32(lane_base + kColS + 32,
+      tc::ld32(lane_base + b * kKeysTc, *reinterpret_cast<uint32_t(*)[32]>(sv));
+      tc::ld32(lane_base + b * kKeysTc + 32,
                *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
       tc::wait_ld();
       tc::fence_before();
       __syncwarp();
       if (lane == 0)
-        mbar_arrive(&s.s_empty);
-      // causal mask, running maximum (base 2)
-      float top = -INFINITY;
+        mbar_arrive(&s.s_empty[b]);
+      // causal mask (keys key0 + i with i <= lim are in), running maximum
+      // (base 2) over 8 independent chains
+      const int lim = min(last_key, qpos) - key0;
+      if (lim < kKeysTc - 1) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int key = key0 + i;
-        const bool in = key <= last_key && key <= qpos;
-        const float x = in ? __uint_as_float(sv[i]) : -INFINITY;
-        sv[i] = __float_as_uint(x);
-        top = fmaxf(top, x);
+        for (int i = 0; i < 64; ++i)
+          if (i > lim)
+            sv[i] = __float_as_uint(-INFINITY);
       }
-      const float next = fmaxf(m, top);
-      const float shift = next == -INFINITY ? 0.0F : next;
-      const float alpha = exp2f(m - shift);
-      m = next;
-      // probabilities rounded to FP16; the denominator adds the rounded
+      float tops[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        tops[i] = __uint_as_float(sv[i]);
+#pragma unroll
+      for (int i = 8; i < 64; ++i)
+        tops[i % 8] = fmaxf(tops[i % 8], __uint_as_float(sv[i]));
+      const float top = fmaxf(fmaxf(fmaxf(tops[0], tops[1]), fmaxf(tops[2], tops[3])),
+                              fmaxf(fmaxf(tops[4], tops[5]), fmaxf(tops[6], tops[7])));
+      // the reference maximum m moves only when the row's maximum passes
+      // it by more than the slack (always on its first finite tile)
+      const bool move = top > m + kRescaleSlack;
+      const float alpha = move ? exp2f(m - top) : 1.0F;
+      if (move)
+        m = top;
+      const float shift = m == -INFINITY ? 0.0F : m;
+      // probabilities rounded to FP16 (exp2 by ex2.approx.ftz: an output
+      // below 2^-126 that it flushes rounds to zero in FP16 all the same);
+      // the tensor cores add the rounded values into the denominator
       uint32_t pw[32];
-      float local = 0;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const __half p0 = __float2half_rn(exp2f(__uint_as_float(sv[2 * i]) - shift));
-        const __half p1 =
-            __float2half_rn(exp2f(__uint_as_float(sv[2 * i + 1]) - shift));
-        local += __half2float(p0) + __half2float(p1);
-        pw[i] = pack2(p0, p1);
+        const __half2 h =
+            __floats2half2_rn(ex2_ftz(__uint_as_float(sv[2 * i]) - shift),
+                              ex2_ftz(__uint_as_float(sv[2 * i + 1]) - shift));
+        pw[i] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      l = l * alpha + local;
-      // the previous tile's P V has finished with P, V^T and O
-      if (j > 0 && !wait_all(&s.o_done, (j - 1) & 1)) {
+      // P_{j-2} V_{j-2} has finished reading this P buffer
+      if (j >= 2 && !wait_all(&s.p_empty[b], ((j >> 1) - 1) & 1)) {
         ok = false;
         break;
       }
-      tc::fence_after();
 #pragma unroll
       for (int piece = 0; piece < 8; ++piece)
-        *reinterpret_cast<uint4*>(s.p[piece / 4] +
+        *reinterpret_cast<uint4*>(s.p[b][piece / 4] +
                                   tc::sw64_offset(t, piece % 4)) =
             make_uint4(pw[4 * piece], pw[4 * piece + 1], pw[4 * piece + 2],
                        pw[4 * piece + 3]);
-      {
-        // V^T: thread t transposes the 8 x 8 block of keys 8 kb .. 8 kb + 7
-        // and dimensions 8 db .. 8 db + 7. Keys past last_key (ring slots
-        // this pass has not written, whatever they hold) become zeros: a
-        // zero probability times a NaN would still be NaN.
-        const int kb = t / 16, db = t % 16;
-        uint4 rows[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-          rows[r] = key0 + 8 * kb + r <= last_key
-                        ? *reinterpret_cast<const uint4*>(
-                              s.v[st][db / 4] +
-                              tc::sw64_offset(8 * kb + r, db % 4))
-                        : make_uint4(0, 0, 0, 0);
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(rows);
-#pragma unroll
-        for (int d = 0; d < 8; ++d) {
-          // dimension 8 db + d: keys 8 kb + 2 i and 8 kb + 2 i + 1
-          const uint32_t sel = (d & 1) ? 0x7632u : 0x5410u;
-          uint32_t o[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            o[i] = __byte_perm(w[(2 * i) * 4 + d / 2],
-                               w[(2 * i + 1) * 4 + d / 2], sel);
-          *reinterpret_cast<uint4*>(s.vt[kb / 4] +
-                                    tc::sw64_offset(8 * db + d, kb % 4)) =
-              make_uint4(o[0], o[1], o[2], o[3]);
-        }
-      }
-      // rescale this row of O when its maximum moved
+      // rescale this row of O and its denominator when m moved, once
+      // P_{j-1} V_{j-1} has landed
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0F)) {
+        if (!wait_all(&s.p_empty[b ^ 1], ((j - 1) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 5; ++c) {
           uint32_t ov[32];
           tc::ld32(lane_base + kColO + c * 32, ov);
           tc::wait_ld();
@@ -316,17 +357,23 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       fence_proxy_async();
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s.p_full);
-        mbar_arrive(&s.kv_empty[st]);
-      }
+      if (lane == 0)
+        mbar_arrive(&s.p_full[b]);
     }
     // ---- epilogue: the row's output (or, with spans, its maximum, sum and
     // unnormalised output for the combine kernel)
-    if (ok && tiles > 0 && !wait_all(&s.o_done, (tiles - 1) & 1))
+    if (ok && tiles > 0 &&
+        !wait_all(&s.p_empty[(tiles - 1) & 1], ((tiles - 1) >> 1) & 1))
       ok = false;
     tc::fence_after();
     if (ok) {
+      float l = 0;
+      if (tiles > 0) {  // CTA-uniform
+        uint32_t lv[32];
+        tc::ld32(lane_base + kColL, lv);
+        tc::wait_ld();
+        l = __uint_as_float(lv[0]);
+      }
       float* part = a.partial + ((size_t(split) * a.n + row) * a.heads + head) *
                                     (kHeadDim + 2);
       if (live && a.spans > 1) {
@@ -389,10 +436,14 @@ cudaError_t launch_prompt_attention_tc(const float* q, int ldq,
   if (group != 2 && group != 4 && group != 8)
     return cudaErrorInvalidValue;
   PromptTcArgs a{};
-  if (cudaError_t e = cached_activation_map(&a.kmap, ring_k, capacity,
+  // The maps end at the pass's last key: a tile reaching past it reads
+  // zeros, never the ring slots this pass has not written (a zero
+  // probability times a NaN there would still be NaN).
+  const int keys = position + n;
+  if (cudaError_t e = encode_activation_map(&a.kmap, ring_k, keys,
                                             kv_heads * kHeadDim, kKeysTc, 32))
     return e;
-  if (cudaError_t e = cached_activation_map(&a.vmap, ring_v, capacity,
+  if (cudaError_t e = encode_activation_map(&a.vmap, ring_v, keys,
                                             kv_heads * kHeadDim, kKeysTc, 32))
     return e;
   a.q = q;

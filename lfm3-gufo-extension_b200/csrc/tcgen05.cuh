@@ -1,7 +1,7 @@
-// tcgen05 building blocks shared by the tensor-core kernels (the prompt
-// projections and the prompt attention): shared-memory operand descriptors
-// of the 64-byte-swizzled K-major layout, instruction descriptors of
-// kind::f16, MMA issue and commit, tensor-memory loads and stores.
+// tcgen05 building blocks of the prompt attention kernel: shared-memory
+// operand descriptors of the 64-byte-swizzled layouts TMA writes,
+// instruction descriptors of kind::f16, MMA issue and commit, tensor-memory
+// allocation, loads and stores.
 #pragma once
 #include <stdint.h>
 
@@ -26,9 +26,24 @@ __device__ __forceinline__ uint64_t sw64_desc(const void* p) {
          (uint64_t(4) << 61);
 }
 
+// Descriptor of an MN-major operand in the same 64-byte-swizzled tiles: each
+// 64-byte row holds 32 consecutive M (or N) elements of one K index, 8-row
+// groups 512 bytes apart along K, and the 32-element blocks of M (N)
+// `block_bytes` apart. Adding 64 advances K by 16 rows (1024 bytes).
+__device__ __forceinline__ uint64_t sw64_mn_desc(const void* p,
+                                                 uint32_t block_bytes) {
+  const uint32_t addr = smem_addr(p);
+  return uint64_t((addr >> 4) & 0x3FFF) |
+         (uint64_t((block_bytes >> 4) & 0x3FFF) << 16) |
+         (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(4) << 61);
+}
+
 // Instruction descriptor of kind::f16: A and B fp16 K-major, D fp32, M x N.
-constexpr uint32_t f16_idesc(int m, int n) {
-  return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+// b_mn_major reads B (N x K) from an MN-major tile instead.
+constexpr uint32_t f16_idesc(int m, int n, bool b_mn_major = false) {
+  return (1u << 4) | (uint32_t(b_mn_major) << 16) | (uint32_t(n >> 3) << 17) |
+         (uint32_t(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void fence_after() {
