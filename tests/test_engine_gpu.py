@@ -65,6 +65,34 @@ def test_free_running_greedy_matches_oracle(small):
         ref = o.step(tok, True)
 
 
+def test_deep_prompt_matches_oracle(small):
+    """A 2200-token prompt in 512-row passes (the full-attention layers'
+    prompt attention on the tcgen05 kernel, keys split into three spans and
+    merged by the combine kernel), then greedy steps, against the oracle
+    with the engine's F16 K/V rounding (the configs' deep prompts at the
+    small geometry)."""
+    w, model = small
+    n = 2200
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, w.config.vocab, n).astype(np.uint32)
+    o = oracle.Oracle(w.weights, n + 8, threads=8, kv_half=True)
+    marks = list(range(511, n, 512)) + [n - 1]
+    want = o.run(prompt, logits_at=marks)
+    s = model.session(n + 8)
+    for first in range(0, n, 512):
+        got = s.forward(prompt[first:first + 512])
+        last = min(first + 512, n) - 1
+        ref = want[last]
+        err = float(np.abs(got - ref).max())
+        assert err <= MAX_ABS, (last, err)
+        assert kl(ref, got) < MAX_KL, last
+    for step in range(3):
+        tok = int(np.argmax(ref))
+        got, ref = s.forward([tok]), o.step(tok, True)
+        assert float(np.abs(got - ref).max()) <= MAX_ABS, step
+        assert kl(ref, got) < MAX_KL, step
+
+
 def test_chunked_matches_serial(small):
     """513 tokens in one Forward (512 + 1 rows) vs one token at a time
     (tests/session_test.cpp:117-144)."""
