@@ -21,7 +21,10 @@
 //   A = the block's 16 x 32 codes: one 16-byte shared load per thread, four
 //       byte permutes and four half2 subtractions (exact fp16 values q)
 //   B = the input rows' hi and lo fp16 terms (x = hi + lo, 22 significant
-//       bits) of up to 8 tokens, loaded from L2 a unit ahead
+//       bits) of up to 8 tokens, loaded from L2 a unit ahead, or from
+//       shared memory when the CTA holds several tiles of a K <= 2048
+//       projection (the producer copies the inputs in once, after the
+//       ring's first weights and the dependency wait)
 //   C = four m16n8k16 MMAs (two k16 halves, hi and lo chains) in FP32, then
 //       acc += d * (hi + lo)
 //
@@ -38,12 +41,17 @@ namespace lfm3 {
 
 namespace {
 
+template <bool kStaged>
 struct DecodeSmem {
-  alignas(128) uint8_t ring[kDecRingBytes];
+  static constexpr int kRing = kStaged ? kDecRingStaged : kDecRingBytes;
+  alignas(128) uint8_t ring[kRing];
+  // kStaged: the input records, token g's at g * kDecXRowBytes
+  alignas(16) uint8_t x[kStaged ? kMaxBatch * kDecXRowBytes : 16];
   alignas(16) float red[kDecWarps][kDecMaxMtiles * 128];
   alignas(16) float tile[kDecMaxMtiles * 128];
   uint64_t full[kDecMaxSlots];
   uint64_t empty[kDecMaxSlots];
+  uint64_t x_full;
 };
 
 // Four biased codes (u = q + 128, one little-endian word) as two half2 of q,
@@ -135,8 +143,8 @@ __device__ void decode_epilogue(const DecodeParams& p, const float* tile,
 
 // Tile t's sums are in the consumer warps' acc: merge the warps in order,
 // then the epilogue.
-template <int kKind, int kMT>
-__device__ void decode_finish(const DecodeParams& p, DecodeSmem& s,
+template <int kKind, int kMT, class Smem>
+__device__ void decode_finish(const DecodeParams& p, Smem& s,
                               const float (&acc)[kMT][4], int t) {
   constexpr int kThreads = kDecWarps * 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -161,24 +169,25 @@ __device__ void decode_finish(const DecodeParams& p, DecodeSmem& s,
   named_barrier(1, kThreads);
 }
 
-template <int kKind, int kMT, int kUB>
+template <int kKind, int kMT, int kUB, bool kStaged>
 __global__ void __launch_bounds__(kDecThreads, 1)
     decode_gemv_kernel(const __grid_constant__ DecodeParams p) {
+  using Smem = DecodeSmem<kStaged>;
   constexpr int kPerWarp = kUB / kDecWarps;          // blocks per warp
   constexpr int kW = kMT * kUB * kDecRecord;         // bytes per unit
-  constexpr int kSlots = kDecRingBytes / kW < kDecMaxSlots
-                             ? kDecRingBytes / kW
-                             : kDecMaxSlots;
+  constexpr int kSlots = Smem::kRing / kW < kDecMaxSlots ? Smem::kRing / kW
+                                                         : kDecMaxSlots;
   static_assert(kSlots >= 4 && kW % 16 == 0 && kPerWarp >= 1, "ring");
   static_assert(kDecThreads == (kDecWarps + 1) * 32, "consumers + producer");
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  DecodeSmem& s = *reinterpret_cast<DecodeSmem*>(smem_raw);
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], kDecWarps);
     }
+    mbar_init(&s.x_full, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -187,13 +196,28 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int G = gridDim.x;
 
   if (warp == kDecWarps) {
-    // ---- producer: constant weights only, so no dependency wait
+    // ---- producer: the weights are constant, so the ring fills before the
+    // dependency wait; staged inputs follow it
     if (lane != 0)
       return;
-    int slot = 0;
+    int slot = 0, issued = 0;
     uint32_t phase = 0;
+    bool x_sent = !kStaged;
+    const auto send_x = [&] {
+      grid_dependency_wait();
+      const uint32_t row = uint32_t(p.layout.K) * 4;
+      mbar_arrive_expect_tx(&s.x_full, row * uint32_t(p.tokens));
+      for (int g = 0; g < p.tokens; ++g)
+        bulk_load(s.x + g * kDecXRowBytes,
+                  static_cast<const uint8_t*>(p.x) + size_t(g) * row, row,
+                  &s.x_full);
+      x_sent = true;
+    };
     for (int t = blockIdx.x; t < p.layout.tiles; t += G)
       for (int c = 0; c < C; ++c) {
+        if (!x_sent && issued == kSlots)
+          send_x();
+        ++issued;
         if (!mbar_wait(&s.empty[slot], phase ^ 1, kErrGemvEmptyWait))
           return;
         mbar_arrive_expect_tx(&s.full[slot], kW);
@@ -204,11 +228,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           phase ^= 1;
         }
       }
+    if (!x_sent)
+      send_x();
     return;
   }
 
   // ---- consumers
   grid_dependency_wait();
+  if constexpr (kStaged)
+    if (!mbar_wait(&s.x_full, 0, kErrGemvFullWait))
+      return;
   const int g = lane >> 2, cq = lane & 3;
   const bool live = g < p.tokens;
   const uint4* xr = static_cast<const uint4*>(p.x);
@@ -224,9 +253,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       x.lo[i] = x.hi[i];
       if (live) {
         const int kb = c * kUB + warp * kPerWarp + i;
-        const uint4* rec = xr + (size_t(g) * records + kb * 4 + cq) * 2;
-        x.hi[i] = __ldg(rec);
-        x.lo[i] = __ldg(rec + 1);
+        if constexpr (kStaged) {
+          const uint4* rec = reinterpret_cast<const uint4*>(
+              s.x + g * kDecXRowBytes + (kb * 4 + cq) * 32);
+          x.hi[i] = rec[0];
+          x.lo[i] = rec[1];
+        } else {
+          const uint4* rec = xr + (size_t(g) * records + kb * 4 + cq) * 2;
+          x.hi[i] = __ldg(rec);
+          x.lo[i] = __ldg(rec + 1);
+        }
       }
     }
   };
@@ -332,17 +368,26 @@ __global__ void decode_pack_kernel(const DecodeLayout l, const uint8_t* s0,
 template <int kKind, int kMT>
 cudaError_t launch_kind(const DecodeParams& p, int grid, cudaStream_t stream,
                         bool pdl) {
-  auto kernel = decode_gemv_kernel<kKind, kMT, 16>;
+  // inputs of K <= kDecStagedK columns staged in shared memory when CTAs
+  // hold several tiles (read once per CTA instead of once per tile; with
+  // one tile per CTA waiting for all of the inputs up front costs more than
+  // fetching each unit's terms one unit ahead)
+  const bool staged = p.layout.K <= kDecStagedK && p.layout.tiles > grid;
+  auto kernel = staged ? decode_gemv_kernel<kKind, kMT, 16, true>
+                       : decode_gemv_kernel<kKind, kMT, 16, false>;
   if constexpr (kMT == 1)
     if (p.layout.K % 1024 == 0)
-      kernel = decode_gemv_kernel<kKind, kMT, 32>;
-  if (const cudaError_t e = ensure_dynamic_smem(
-          reinterpret_cast<const void*>(kernel), int(sizeof(DecodeSmem))))
+      kernel = staged ? decode_gemv_kernel<kKind, kMT, 32, true>
+                      : decode_gemv_kernel<kKind, kMT, 32, false>;
+  const int bytes = staged ? int(sizeof(DecodeSmem<true>))
+                           : int(sizeof(DecodeSmem<false>));
+  if (const cudaError_t e =
+          ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), bytes))
     return e;
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(grid);
   config.blockDim = dim3(kDecThreads);
-  config.dynamicSmemBytes = sizeof(DecodeSmem);
+  config.dynamicSmemBytes = bytes;
   config.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

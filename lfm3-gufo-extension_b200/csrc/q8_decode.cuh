@@ -36,6 +36,13 @@ constexpr int kDecThreads = (kDecWarps + 1) * 32;  // + the producer warp
 // Shared-memory ring: 9 slots of 17 KB units, 6 of 26 KB, 4 of 35 KB.
 constexpr int kDecRingBytes = 156672;
 constexpr int kDecMaxSlots = 9;
+// Projections with K <= kDecStagedK and more tiles than CTAs keep the
+// round's input records in shared memory (one bulk copy per token, rows padded by 16 bytes so the
+// fragment loads hit distinct banks) beside a smaller ring: 8 slots of
+// 17 KB, 5 of 26 KB, 4 of 35 KB.
+constexpr int kDecStagedK = 2048;
+constexpr int kDecXRowBytes = kDecStagedK * 4 + 16;
+constexpr int kDecRingStaged = 139264;
 constexpr int kDecMaxMtiles = 4;
 
 enum DecodeKind : int {
