@@ -228,10 +228,11 @@ int lfm3_cuda_batched_residual_add(const float* a, const float* b, float* out,
 int lfm3_cuda_gemv(const void* A, uint32_t a_type, const float* x, float* y,
                    size_t M, size_t K, void* stream);
 /* Decode projections over the fragment-ordered copy that the engine packs
- * its Q8_0 matrices into at load (no reference counterpart: the reference's
+ * its matrices into at load (no reference counterpart: the reference's
  * decode GEMVs read the GGUF rows directly; this exposes the engine's decode
- * kernel on caller-supplied matrices). w[0..n_w) are Q8_0 matrices of K
- * columns (K a multiple of 512). swiglu == 0: n_w <= 4 outputs,
+ * kernel on caller-supplied matrices). w[0..n_w) are Q8_0 matrices, or BF16
+ * matrices (all of one type), of K columns (K a multiple of 512); BF16
+ * products use each input as three exact bf16 terms of its 22-bit split. swiglu == 0: n_w <= 4 outputs,
  * out[j][r * ld[j] + i] = x[r] . row i of w[j]. swiglu == 1: w = {gate, up}
  * of equal rows, out[0][r * ld[0] + i] = silu(g) * u. rows 1..8 FP32 input
  * rows x[r * K + k]. Each call packs the matrices into `workspace`

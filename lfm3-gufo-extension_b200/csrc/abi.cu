@@ -626,12 +626,14 @@ bool DecodePlan(const lfm3_tensor* const* w, int n_w, int swiglu,
   l.kind = swiglu ? lfm3::kDecSwiGLU : lfm3::kDecPlain;
   l.n_src = n_w;
   for (int j = 0; j < n_w; ++j) {
-    if (!w[j] || !w[j]->data || w[j]->type != LFM3_Q8_0 ||
-        (j && w[j]->cols != w[0]->cols))
+    if (!w[j] || !w[j]->data ||
+        (w[j]->type != LFM3_Q8_0 && w[j]->type != LFM3_BF16) ||
+        (j && (w[j]->cols != w[0]->cols || w[j]->type != w[0]->type)))
       return false;
     l.rows[j] = int(w[j]->rows);
   }
   l.K = int(w[0]->cols);
+  l.bf16 = w[0]->type == LFM3_BF16 ? 1 : 0;
   if (!lfm3::decode_layout(l, Sms()))
     return false;
   const auto up = [](size_t b) { return (b + 255) / 256 * 256; };

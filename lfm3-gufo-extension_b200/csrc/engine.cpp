@@ -285,8 +285,7 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
     }
     upload.Run();
     VisitTensors(m->device_, [&](lfm3_tensor& t) { t.data = placed.at(t.data); });
-    if (!m->bf16())
-      m->PackDecodeGroups();
+    m->PackDecodeGroups();
     // RoPE frequencies: float(pow(double theta, -2i/D)), global then sliding
     // (hip/ops.hip:1045-1050, engine.cpp:225-232).
     float freq[128];
@@ -312,9 +311,10 @@ std::shared_ptr<Model> Model::Load(const lfm3_weights& host,
   }
 }
 
-// Packs every Q8_0 matrix group a decode round reads into the decode
-// projections' fragment order (q8_decode.cuh), from the device copies just
-// uploaded, into one allocation (256-byte aligned groups).
+// Packs every matrix group a decode round reads (Q8_0, or the BF16
+// numerical-reference weights) into the decode projections' fragment order
+// (q8_decode.cuh), from the device copies just uploaded, into one
+// allocation (256-byte aligned groups).
 void Model::PackDecodeGroups() {
   const auto& c = device_.config;
   const int H = int(c.hidden), F = int(c.intermediate), A = int(c.heads) * 128;
@@ -334,6 +334,7 @@ void Model::PackDecodeGroups() {
     g.layout.K = K;
     g.layout.H = H;
     g.layout.n_src = int(srcs.size());
+    g.layout.bf16 = bf16() ? 1 : 0;
     Job job{&g, {}};
     int j = 0;
     for (const lfm3_tensor* t : srcs) {
@@ -369,20 +370,6 @@ void Model::PackDecodeGroups() {
     dst += (decode_packed_bytes(job.group->layout) + 255) / 256 * 256;
   }
   Throw(cudaDeviceSynchronize());
-}
-
-const CUtensorMap& Model::RowMap(const lfm3_tensor& t, int chunk_bytes,
-                                 int box_rows) {
-  std::lock_guard<std::mutex> lock(maps_mutex_);
-  const auto key = std::make_pair(t.data, chunk_bytes * 1024 + box_rows);
-  auto it = maps_.find(key);
-  if (it == maps_.end()) {
-    CUtensorMap map;
-    Throw(encode_q8_rows(&map, t.data, size_t(t.cols) / 32 * 34, int(t.rows),
-                         chunk_bytes, box_rows));
-    it = maps_.emplace(key, map).first;
-  }
-  return it->second;
 }
 
 std::unique_ptr<Session> Model::CreateSession(uint32_t context,
@@ -451,7 +438,8 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     ff_ = DeviceBuffer(R * F * 4);
     zf_ = DeviceBuffer(R * H * 4);
     split_partial_ = DeviceBuffer(kPrefillPartialFloats * 4);
-    half_ = DeviceBuffer(R * width * 2);
+    // FP16 row-scaled activations, or (BF16 models) three bf16 planes
+    half_ = DeviceBuffer(R * width * 2 * (model_->bf16() ? 3 : 1));
     scale_ = DeviceBuffer(R * 4);
     z_split_ = DeviceBuffer(kMaxBatch * H * 4);
     a_split_ = DeviceBuffer(kMaxBatch * std::max(A, H) * 4);
@@ -563,24 +551,6 @@ void Session::TakeProfile(double* ms, long long* launches) {
 
 // ---- decode round -------------------------------------------------------------
 
-// Launches one projection of the round's rows (split input x).
-static cudaError_t RunGemv(GemvParams p, Model& model, cudaStream_t stream) {
-  if (model.bf16()) {
-    if (!bf16_plan(p))
-      return cudaErrorInvalidValue;
-    return launch_bf16_gemv(p, nullptr, 0, 0, stream);
-  }
-  if (!gemv_plan(p, model.sms()))
-    return cudaErrorInvalidValue;
-  const int maps = p.kind == kGemvPlain ? p.n_out : p.kind == kGemvSwiGLU ? 2 : 1;
-  for (int j = 0; j < maps; ++j) {
-    lfm3_tensor t{p.o[j].w, LFM3_Q8_0, uint32_t(p.K), uint32_t(p.o[j].rows), 0};
-    p.maps[j] = model.RowMap(t, gemv_pitch_units(p.chunk_blocks) * 16,
-                             gemv_box_rows(p));
-  }
-  return launch_q8_gemv(p, gemv_grid(p.tiles, model.sms()), stream, true);
-}
-
 // Launches one projection of the round's rows over a packed decode group
 // (Q8_0 models): the same outputs and epilogue as the GemvParams describe.
 static cudaError_t RunDecode(const GemvParams& g, const DecodeGroup& group,
@@ -620,9 +590,7 @@ void Session::LaunchLmHead(const void* split_rows, int rows, float* out) {
   p.n_out = 1;
   p.o[0] = Out(w.output, out, c.vocab);
   p.x = split_rows;
-  Check(model_->bf16()
-            ? RunGemv(p, *model_, stream_)
-            : RunDecode(p, model_->decode_head(), *model_, stream_));
+  Check(RunDecode(p, model_->decode_head(), *model_, stream_));
 }
 
 void Session::DecodeRound(std::span<Session* const> batch,
@@ -633,14 +601,11 @@ void Session::DecodeRound(std::span<Session* const> batch,
   const int B = int(batch.size());
   const int H = c.hidden, F = c.intermediate, A = c.heads * 128;
   cudaStream_t s = stream_;
-  // a projection of the round's rows: BF16 matrices directly, Q8_0 through
-  // the layer's packed decode group
+  // a projection of the round's rows through the layer's packed decode
+  // group (Q8_0 or BF16)
   const auto gemv = [&](GemvParams p, const DecodeGroup& group) {
-    Timed(kDecodeProjection, [&] {
-      Check(model_->bf16()
-                ? RunGemv(p, *model_, s)
-                : RunDecode(p, group, *model_, s));
-    });
+    Timed(kDecodeProjection,
+          [&] { Check(RunDecode(p, group, *model_, s)); });
   };
   // the rows of this round go through a pinned table whose previous copy is
   // done; an earlier round that returned without waiting and has finished
@@ -696,8 +661,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
     });
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     const auto& l = w.layers[i];
-    static const DecodeLayer kNone{};
-    const DecodeLayer& dl = model_->bf16() ? kNone : model_->decode_layer(i);
+    const DecodeLayer& dl = model_->decode_layer(i);
     if (c.layer_type[i] == LFM3_CONV) {
       GemvParams p{};
       p.kind = kGemvConv;
@@ -875,13 +839,31 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
   __half* half = half_.as<__half>();
   float* scale = scale_.as<float>();
   const auto half_at = [&](int row, int width) { return half + size_t(row) * width; };
-  // prompt projections read FP16 rows of the workspace (viewed as
-  // [rows][K]) starting at row `first`
+  // Q8_0 prompt projections read FP16 rows of the workspace (viewed as
+  // [rows][K]) starting at row `first`; BF16 ones the FP32 rows in32 (p.tokens
+  // rows of K), split into three exact bf16 planes of the workspace first
+  const bool bf16 = model_->bf16();
   const size_t half_elems = half_.bytes() / 2;
-  const auto prefill = [&](PrefillParams p, int first) {
-    p.x_row0 = first;
+  const auto prefill = [&](PrefillParams p, int first,
+                           const float* in32 = nullptr) {
     p.partial = split_partial_.as<float>();
     int splits = 1;
+    if (bf16) {
+      const int plane_rows = int(kPrefillChunk);
+      Timed(kPromptOther, [&] {
+        Check(launch_split_bf16_rows(in32, half, p.tokens, p.K, plane_rows, s,
+                                     kPdl));
+      });
+      p.bf16 = 1;
+      p.scale = nullptr;
+      p.row_max = nullptr;
+      p.x_row0 = 0;
+      Timed(kPromptProjection, [&] {
+        Check(launch_q8_prefill(p, half, plane_rows, s, &splits, kPdl));
+      });
+      return splits;
+    }
+    p.x_row0 = first;
     Timed(kPromptProjection, [&] {
       Check(launch_q8_prefill(p, half, int(half_elems / size_t(p.K)), s,
                               &splits, kPdl));
@@ -890,9 +872,6 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
   };
   const auto other = [&](auto launch) { Timed(kPromptOther, launch); };
   const auto rows = [&](auto launch) { Timed(kRowKernels, launch); };
-  // BF16 models project FP32 rows (in32) on the CUDA cores; Q8_0 models the
-  // FP16 row-scaled copies on the tensor cores
-  const bool bf16 = model_->bf16();
   float* zf = zf_.as<float>();
   const auto norm_out = [&](int row) {
     return bf16 ? NormOut{zf + size_t(row) * H, nullptr, nullptr, nullptr}
@@ -916,20 +895,6 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
                          std::initializer_list<PrefillOutput> outs,
                          bool planes = false) {
     const Branch whole{outs.begin()->out, {}};
-    if (bf16) {
-      GemvParams g{};
-      g.kind = kGemvPlain;
-      g.K = K;
-      g.n_out = int(outs.size());
-      int j = 0;
-      for (const auto& o : outs)
-        g.o[j++] = GemvOutput{o.w, o.out, o.rows, o.ld};
-      if (!bf16_plan(g))
-        Throw(cudaErrorInvalidValue);
-      Timed(kPromptProjection,
-            [&] { Check(launch_bf16_gemv(g, in32, K, rows, s)); });
-      return whole;
-    }
     PrefillParams p{};
     p.kind = kPrefillPlain;
     p.K = K;
@@ -938,9 +903,9 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
     int j = 0;
     for (const auto& o : outs)
       p.o[j++] = o;
-    p.scale = scale + first_row;
+    p.scale = bf16 ? nullptr : scale + first_row;
     p.keep_splits = planes;
-    const int splits = prefill(p, first_row);
+    const int splits = prefill(p, first_row, in32);
     return planes && splits > 1
                ? Branch{nullptr,
                         SplitBranch{split_partial_.as<float>(), p.scale, splits,
@@ -1050,22 +1015,18 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
           norm_out(o), rows_out, H, c.eps, s, kPdl, branch.parts()));
     });
     if (bf16) {
+      // h rows in FP32, split into bf16 planes by the down projection
       float* ff = ff_.as<float>();
-      GemvParams g{};
-      g.kind = kGemvSwiGLU;
-      g.K = H;
-      g.n_out = 2;
-      g.o[0] = GemvOutput{static_cast<const uint8_t*>(l.gate.data),
-                          ff + size_t(o) * F, int(l.gate.rows), F};
-      g.o[1] = GemvOutput{static_cast<const uint8_t*>(l.up.data), nullptr,
-                          int(l.up.rows), 0};
-      if (!bf16_plan(g))
-        Throw(cudaErrorInvalidValue);
-      Timed(kPromptProjection, [&] {
-        Check(launch_bf16_gemv(g, zf + size_t(o) * H, H, rows_out, s));
-      });
+      PrefillParams p{};
+      p.kind = kPrefillSwiGLU;
+      p.K = H;
+      p.tokens = rows_out;
+      p.n_out = 2;
+      p.o[0] = pout(l.gate, ff + size_t(o) * F, F);
+      p.o[1] = pout(l.up, nullptr, F);
+      prefill(p, o, zf + size_t(o) * H);
       branch = plain(F, rows_out, o, ff + size_t(o) * F,
-                     {pout(l.down, out + size_t(o) * H, H)});
+                     {pout(l.down, out + size_t(o) * H, H)}, true);
     } else {
       // h rows in FP32, then FP16 with per-row scales (half_rows finds each
       // row's maximum itself)

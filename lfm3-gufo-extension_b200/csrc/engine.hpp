@@ -65,7 +65,7 @@ private:
 // (engine.hpp:9-15, ContinuationTensor).
 enum class ContinuationTensor { kLogits, kFrontier, kConvolution, kKey, kValue };
 
-// A Q8_0 matrix group in the decode projections' fragment order
+// A Q8_0 or BF16 matrix group in the decode projections' fragment order
 // (q8_decode.cuh), packed once at load.
 struct DecodeGroup {
   DecodeLayout layout{};
@@ -108,11 +108,7 @@ public:
   bool bf16() const { return device_.output.type == LFM3_BF16; }
   // Device bytes of the weight segments.
   size_t weight_bytes() const { return weight_bytes_; }
-  // The TMA map over a Q8_0 matrix's rows with boxes of box_rows rows x
-  // chunk_bytes (encoded once, cached).
-  const CUtensorMap& RowMap(const lfm3_tensor& t, int chunk_bytes,
-                            int box_rows);
-  // Q8_0 models: the packed decode groups of layer i and of the LM head.
+  // The packed decode groups of layer i and of the LM head.
   const DecodeLayer& decode_layer(uint32_t i) const { return decode_[i]; }
   const DecodeGroup& decode_head() const { return decode_head_; }
   // Device bytes of the packed decode copies.
@@ -131,13 +127,11 @@ private:
   unsigned* error_device_ = nullptr;
 
   size_t weight_bytes_ = 0;
-  // the decode groups (Q8_0 models), all in one allocation
+  // the decode groups, all in one allocation
   DeviceBuffer packed_;
   std::vector<DecodeLayer> decode_;
   DecodeGroup decode_head_;
   void PackDecodeGroups();
-  std::mutex maps_mutex_;
-  std::map<std::pair<const void*, int>, CUtensorMap> maps_;
   friend class Session;
 };
 

@@ -1,6 +1,8 @@
 // Row kernels: embedding gather, fused residual + sandwich RMSNorm, FP16
 // row scaling, split records. One CTA of 256 threads per row; each thread
 // owns 8 consecutive elements (H <= 2048 x ... in 8-element groups).
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "norm.cuh"
 #include "kernels.cuh"
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(kNormThreads)
         s0.x += d0.x, s0.y += d0.y, s0.z += d0.z, s0.w += d0.w;
         s1.x += d1.x, s1.y += d1.y, s1.z += d1.z, s1.w += d1.w;
       }
-      const float sc = split.scale[row];
+      const float sc = split.scale ? split.scale[row] : 1.0F;
       b[j][0] = s0.x * sc, b[j][1] = s0.y * sc, b[j][2] = s0.z * sc,
       b[j][3] = s0.w * sc;
       b[j][4] = s1.x * sc, b[j][5] = s1.y * sc, b[j][6] = s1.z * sc,
@@ -194,6 +196,38 @@ __global__ void __launch_bounds__(kNormThreads)
   }
   if (norm_w)
     finish_norm(v, live, nw, out, row, H, eps, scratch);
+}
+
+// Eight values of one row per thread as three exact bf16 planes.
+__global__ void split_bf16_rows_kernel(const float* __restrict__ x,
+                                       __nv_bfloat16* planes, int rows, int K,
+                                       int plane_rows) {
+  grid_dependency_wait();
+  allow_dependents();
+  const size_t e = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (e >= size_t(rows) * K)
+    return;
+  const int r = int(e / K), k = int(e % K);
+  const float4 a = *reinterpret_cast<const float4*>(x + e);
+  const float4 b = *reinterpret_cast<const float4*>(x + e + 4);
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  union {
+    __nv_bfloat16 h[8];
+    uint4 u;
+  } t[3];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float rest = v[i];
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      t[q].h[i] = __float2bfloat16_rn(rest);
+      rest -= __bfloat162float(t[q].h[i]);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+    *reinterpret_cast<uint4*>(planes + (size_t(q) * plane_rows + r) * K + k) =
+        t[q].u;
 }
 
 __device__ __forceinline__ float half_bits(uint16_t h) {
@@ -384,7 +418,7 @@ cudaError_t launch_residual_norm(const float* branch, const float* post_w,
   SplitBranch sb{};
   if (split) {
     sb = *split;
-    if (branch || !sb.partial || !sb.scale || sb.splits < 1 ||
+    if (branch || !sb.partial || sb.splits < 1 ||
         sb.token_tiles < (rows + 255) / 256 || H % 256)
       return cudaErrorInvalidValue;
   }
@@ -432,6 +466,21 @@ cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
                                     : half_rows_kernel<8>;
   return launch_kernel(kernel, dim3(rows), dim3(kNormThreads), 0, stream, pdl,
                        x, row_max, values, scale, K);
+}
+
+cudaError_t launch_split_bf16_rows(const float* x, void* planes, int rows,
+                                   int K, int plane_rows, cudaStream_t stream,
+                                   bool pdl) {
+  if (rows <= 0)
+    return cudaSuccess;
+  if (K % 8 || rows > plane_rows || reinterpret_cast<uintptr_t>(x) % 16 ||
+      reinterpret_cast<uintptr_t>(planes) % 16)
+    return cudaErrorInvalidValue;
+  const size_t groups = size_t(rows) * K / 8;
+  return launch_kernel(split_bf16_rows_kernel,
+                       dim3(unsigned((groups + 255) / 256)), dim3(256), 0,
+                       stream, pdl, x, static_cast<__nv_bfloat16*>(planes),
+                       rows, K, plane_rows);
 }
 
 cudaError_t launch_row_copies(const RowCopies& copies, cudaStream_t stream,

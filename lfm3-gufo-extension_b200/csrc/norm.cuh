@@ -18,7 +18,8 @@ struct NormOut {
 // A residual branch still split over K: the FP32 partial sums of a prompt
 // projection, one [256 prompt rows][256 output rows] block per (tile, split)
 // with tile = output row tile * token_tiles + prompt row tile; the branch
-// is scale[prompt row] * (sum of the splits in split order).
+// is scale[prompt row] * (sum of the splits in split order); a null scale
+// (BF16 projections) is 1.
 constexpr int kSplitTileFloats = 256 * 256;
 struct SplitBranch {
   const float* partial;
@@ -52,6 +53,14 @@ cudaError_t launch_embed_norm(const void* table, uint32_t type,
 cudaError_t launch_half_rows(const float* x, const unsigned* row_max,
                              __half* values, float* scale, int rows, int K,
                              cudaStream_t stream, bool pdl = false);
+
+// FP32 rows -> three bf16 planes whose sum is each value exactly (plane q
+// the round-to-nearest bf16 of what planes 0 .. q - 1 left): plane q of row
+// r at planes + (q * plane_rows + r) * K elements. The BF16 prompt
+// projections read them (K a multiple of 8, 16-byte aligned rows).
+cudaError_t launch_split_bf16_rows(const float* x, void* planes, int rows,
+                                   int K, int plane_rows, cudaStream_t stream,
+                                   bool pdl = false);
 
 // FP32 rows -> split records (x = hi + lo, fp16 each).
 // Up to kMaxRowCopies FP32 row copies in one launch (16-byte pieces when

@@ -33,6 +33,8 @@
 // shared memory in warp order, so results never depend on timing.
 #include <algorithm>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8_decode.cuh"
@@ -78,6 +80,37 @@ __device__ __forceinline__ void mma_f16_first(float (&d)[4],
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
         "f"(0.0F));
+}
+
+// m16n8k16 bf16 x bf16 -> f32, accumulating into d.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4],
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two input values given as fp16 hi and lo terms (x = hi + lo, exact in
+// FP32) as three bf16 terms t1 + t2 + t3 == x exactly: each term is the
+// round-to-nearest bf16 of what the earlier terms left (x carries at most
+// 22 significant bits, bf16 eight).
+__device__ __forceinline__ void split_bf16(uint32_t hi, uint32_t lo,
+                                           uint32_t (&t)[3]) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  float r0 = a.x + b.x, r1 = a.y + b.y;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(r0, r1);
+    t[i] = *reinterpret_cast<const uint32_t*>(&v);
+    if (i < 2) {
+      const float2 f = __bfloat1622float2(v);
+      r0 -= f.x;
+      r1 -= f.y;
+    }
+  }
 }
 
 template <int kKind, int kMT>
@@ -169,12 +202,13 @@ __device__ void decode_finish(const DecodeParams& p, Smem& s,
   named_barrier(1, kThreads);
 }
 
-template <int kKind, int kMT, int kUB, bool kStaged>
+template <int kKind, int kMT, int kUB, bool kStaged, bool kBf16>
 __global__ void __launch_bounds__(kDecThreads, 1)
     decode_gemv_kernel(const __grid_constant__ DecodeParams p) {
   using Smem = DecodeSmem<kStaged>;
+  constexpr int kRec = kBf16 ? kDecRecordBf16 : kDecRecord;
   constexpr int kPerWarp = kUB / kDecWarps;          // blocks per warp
-  constexpr int kW = kMT * kUB * kDecRecord;         // bytes per unit
+  constexpr int kW = kMT * kUB * kRec;               // bytes per unit
   constexpr int kSlots = Smem::kRing / kW < kDecMaxSlots ? Smem::kRing / kW
                                                          : kDecMaxSlots;
   static_assert(kSlots >= 4 && kW % 16 == 0 && kPerWarp >= 1, "ring");
@@ -286,8 +320,31 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
       for (int i = 0; i < kPerWarp; ++i) {
         const uint4 h = cur.hi[i], l = cur.lo[i];
-        const uint8_t* rec =
-            base + (warp * kPerWarp + i) * (kMT * kDecRecord);
+        const uint8_t* rec = base + (warp * kPerWarp + i) * (kMT * kRec);
+        if constexpr (kBf16) {
+          // the block's input as three exact bf16 terms, shared by its
+          // m-tiles; three MMAs per k16 half accumulate straight into acc
+          uint32_t b[4][3];
+          split_bf16(h.x, l.x, b[0]);
+          split_bf16(h.y, l.y, b[1]);
+          split_bf16(h.z, l.z, b[2]);
+          split_bf16(h.w, l.w, b[3]);
+#pragma unroll
+          for (int m = 0; m < kMT; ++m) {
+            const uint8_t* q = rec + m * kRec;
+            const uint4 u = *reinterpret_cast<const uint4*>(q + lane * 16);
+            const uint4 v =
+                *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
+            const uint32_t a1[4] = {u.x, v.x, u.y, v.y};  // columns 8c..8c+3
+            const uint32_t a2[4] = {u.z, v.z, u.w, v.w};  // 8c+4..8c+7
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              mma_bf16(acc[m], a1, b[0][j], b[1][j]);
+              mma_bf16(acc[m], a2, b[2][j], b[3][j]);
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int m = 0; m < kMT; ++m) {
           const uint8_t* r = rec + m * kDecRecord;
@@ -326,6 +383,34 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 }
 
 // ---- packing -------------------------------------------------------------------
+// BF16: lane l = 4g + c of a record writes row g's columns 8c..8c+7 of the
+// block at 16 l and row g + 8's at 512 + 16 l (zeros for padding rows).
+__global__ void decode_pack_bf16_kernel(const DecodeLayout l, const uint8_t* s0,
+                                        const uint8_t* s1, const uint8_t* s2,
+                                        const uint8_t* s3, uint8_t* dst) {
+  const int KB = l.K / 32;
+  const long long total = static_cast<long long>(l.tiles) * KB * l.mt;
+  const long long rec = static_cast<long long>(blockIdx.x) * 8 + threadIdx.x / 32;
+  if (rec >= total)
+    return;
+  const int lane = threadIdx.x % 32, g = lane / 4, c = lane % 4;
+  const int m = int(rec % l.mt);
+  const long long tb = rec / l.mt;
+  const int kb = int(tb % KB), t = int(tb / KB);
+  int j = 0, row0 = 0;
+  const bool valid = decode_mtile_source(l, t, m, j, row0);
+  const uint8_t* src = j == 0 ? s0 : j == 1 ? s1 : j == 2 ? s2 : s3;
+  uint8_t* out = dst + rec * kDecRecordBf16;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = row0 + g + 8 * h;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid && row < l.rows[j])
+      v = *reinterpret_cast<const uint4*>(src + (size_t(row) * l.K + kb * 32 + 8 * c) * 2);
+    *reinterpret_cast<uint4*>(out + 512 * h + lane * 16) = v;
+  }
+}
+
 __global__ void decode_pack_kernel(const DecodeLayout l, const uint8_t* s0,
                                    const uint8_t* s1, const uint8_t* s2,
                                    const uint8_t* s3, uint8_t* dst) {
@@ -373,12 +458,21 @@ cudaError_t launch_kind(const DecodeParams& p, int grid, cudaStream_t stream,
   // one tile per CTA waiting for all of the inputs up front costs more than
   // fetching each unit's terms one unit ahead)
   const bool staged = p.layout.K <= kDecStagedK && p.layout.tiles > grid;
-  auto kernel = staged ? decode_gemv_kernel<kKind, kMT, 16, true>
-                       : decode_gemv_kernel<kKind, kMT, 16, false>;
+  auto kernel = staged ? decode_gemv_kernel<kKind, kMT, 16, true, false>
+                       : decode_gemv_kernel<kKind, kMT, 16, false, false>;
   if constexpr (kMT == 1)
     if (p.layout.K % 1024 == 0)
-      kernel = staged ? decode_gemv_kernel<kKind, kMT, 32, true>
-                      : decode_gemv_kernel<kKind, kMT, 32, false>;
+      kernel = staged ? decode_gemv_kernel<kKind, kMT, 32, true, false>
+                      : decode_gemv_kernel<kKind, kMT, 32, false, false>;
+  if (p.layout.bf16) {
+    // BF16 units: 16 blocks of one-m-tile tiles, else 8 (16-32 KB)
+    if constexpr (kMT == 1)
+      kernel = staged ? decode_gemv_kernel<kKind, kMT, 16, true, true>
+                      : decode_gemv_kernel<kKind, kMT, 16, false, true>;
+    else
+      kernel = staged ? decode_gemv_kernel<kKind, kMT, 8, true, true>
+                      : decode_gemv_kernel<kKind, kMT, 8, false, true>;
+  }
   const int bytes = staged ? int(sizeof(DecodeSmem<true>))
                            : int(sizeof(DecodeSmem<false>));
   if (const cudaError_t e =
@@ -451,7 +545,8 @@ bool decode_layout(DecodeLayout& l, int sms) {
 }
 
 size_t decode_packed_bytes(const DecodeLayout& l) {
-  return size_t(l.tiles) * (l.K / 32) * l.mt * kDecRecord;
+  return size_t(l.tiles) * (l.K / 32) * l.mt *
+         (l.bf16 ? kDecRecordBf16 : kDecRecord);
 }
 
 cudaError_t launch_decode_pack(const DecodeLayout& l,
@@ -465,8 +560,12 @@ cudaError_t launch_decode_pack(const DecodeLayout& l,
   const long long records =
       static_cast<long long>(l.tiles) * (l.K / 32) * l.mt;
   note_launch();
-  decode_pack_kernel<<<unsigned((records + 7) / 8), 256, 0, stream>>>(
-      l, src[0], src[1], src[2], src[3], dst);
+  if (l.bf16)
+    decode_pack_bf16_kernel<<<unsigned((records + 7) / 8), 256, 0, stream>>>(
+        l, src[0], src[1], src[2], src[3], dst);
+  else
+    decode_pack_kernel<<<unsigned((records + 7) / 8), 256, 0, stream>>>(
+        l, src[0], src[1], src[2], src[3], dst);
   return cudaGetLastError();
 }
 

@@ -13,6 +13,9 @@
 //   bytes 512..543  half2 {d(row g), d(row g + 8)} for g = 0..7
 //
 // 544 bytes per 512 weights, the GGUF size, so a round moves the same bytes.
+// BF16 matrices (the numerical-reference weights) get the same layout with
+// 1024-byte records: lane l = 4g + c holds row g's columns 8c..8c+7 at
+// bytes 16 l and row g + 8's at 512 + 16 l, the values themselves.
 // Records are ordered [tile][block][m-tile of the tile], so a unit of work
 // (one tile x 16 or 32 blocks) is one contiguous run of memory that a single
 // bulk copy brings into shared memory.
@@ -30,7 +33,8 @@
 
 namespace lfm3 {
 
-constexpr int kDecRecord = 544;  // bytes per (m-tile, block) record
+constexpr int kDecRecord = 544;  // bytes per (m-tile, block) record, Q8_0
+constexpr int kDecRecordBf16 = 1024;  // the same for BF16 matrices
 constexpr int kDecWarps = 8;     // consumer warps
 constexpr int kDecThreads = (kDecWarps + 1) * 32;  // + the producer warp
 // Shared-memory ring: 9 slots of 17 KB units, 6 of 26 KB, 4 of 35 KB.
@@ -67,6 +71,7 @@ struct DecodeLayout {
   int first_mtile[5];
   int rows[4];  // rows of each source matrix
   int H;        // Conv: channels (in_proj has 3H rows)
+  int bf16;     // BF16 matrices (1024-byte records) instead of Q8_0
 };
 
 // Source matrix j and first row of m-tile m of tile t; false for padding.

@@ -37,6 +37,14 @@
 //               accumulators; applies the prompt-row scales and writes the
 //               outputs (SwiGLU: silu(g) * u, optionally per-row maxima;
 //               split tiles: the FP32 partial sums)
+// BF16 weights (p.bf16, the numerical-reference models) skip the converters:
+// warp 0 also loads the weight tiles (two 128-row boxes of the [rows][K]
+// bf16 matrix, 64-byte swizzle) and the activations are three bf16 planes
+// whose sum is the FP32 input exactly, so each K32 block is 2 accumulators
+// x 3 planes x 2 K16 steps of bf16 MMAs: exact products, FP32
+// accumulation, the precision of the reference's exact BF16 x FP32 GEMM
+// (hip/ops.hip:1917-2005). Planes 1 and 2 of a stage sit where the Q8 mode
+// keeps its lo tile and raw weight rows.
 // Stages hand over through mbarriers and every wait is bounded: a pipeline
 // that stops making progress reports kErrPrefillWait and the CTA returns.
 // When that happens every copy and MMA it issued is seconds old and complete.
@@ -61,10 +69,10 @@ constexpr int kBBytes = kTN * 64;             // kTN rows x 32 fp16
 constexpr int kThreads = 14 * 32;
 
 struct __align__(1024) PrefillSmem {
-  uint8_t a_hi[kStages][kAPartBytes];
-  uint8_t a_lo[kStages][kAPartBytes];
-  uint8_t b[kStages][kBBytes];
-  uint8_t w[kWBytes];
+  uint8_t a_hi[kStages][kAPartBytes];  // bf16: the weight tile
+  uint8_t a_lo[kStages][kAPartBytes];  // bf16: activation plane 1
+  uint8_t b[kStages][kBBytes];         // activation tile (bf16: plane 0)
+  uint8_t w[kWBytes];                  // bf16: plane 2 of stage s at s * kBBytes
   uint64_t w_full, w_empty;
   uint64_t full[kStages], empty[kStages];
   uint64_t acc_full[kAccBufs], acc_empty[kAccBufs];
@@ -72,9 +80,11 @@ struct __align__(1024) PrefillSmem {
 };
 
 // tcgen05 instruction descriptor: kind::f16, A and B fp16 K-major, D fp32,
-// M = 128, N = kTN.
+// M = 128, N = kTN; the same with A and B bf16.
 constexpr uint32_t kInstrDesc =
     (1u << 4) | (uint32_t(kTN >> 3) << 17) | (uint32_t(kTM >> 4) << 24);
+constexpr uint32_t kInstrDescBf16 = kInstrDesc | (1u << 7) | (1u << 10);
+static_assert(kStages * kBBytes <= kWBytes, "bf16 plane 2 fits the w buffer");
 
 // Shared-memory matrix descriptor of a K-major operand with 64-byte rows and
 // the 64-byte swizzle: 8-row groups 512 bytes apart. Adding 2 advances K by
@@ -93,12 +103,13 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b,
-                                       uint32_t accumulate) {
+                                       uint32_t accumulate,
+                                       uint32_t idesc = kInstrDesc) {
   asm volatile(
       "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
           d_tmem),
-      "l"(a), "l"(b), "r"(kInstrDesc), "r"(accumulate)
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -179,6 +190,7 @@ __device__ __forceinline__ void load_weights(const PrefillParams& p,
   }
 }
 
+template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -193,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s.w_full, 1);
     mbar_init(&s.w_empty, 8);
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&s.full[i], 9);  // 8 converter warps + the producer's bytes
+      // 8 converter warps + the producer's bytes (bf16: the producer only)
+      mbar_init(&s.full[i], kBf16 ? 1 : 9);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < kAccBufs; ++i) {
@@ -227,9 +240,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = x.kb0; kb < x.kb1; ++kb) {
           if (!mbar_wait(&s.empty[b.slot], b.phase ^ 1, kErrPrefillWait))
             goto done;
-          mbar_arrive_expect_tx(&s.full[b.slot], kBBytes);
-          tma_load_2d(s.b[b.slot], &p.x_map, kb * 32,
-                      p.x_row0 + x.tt * kTN, &s.full[b.slot]);
+          const int row = p.x_row0 + x.tt * kTN;
+          if constexpr (kBf16) {
+            uint64_t* bar = &s.full[b.slot];
+            mbar_arrive_expect_tx(bar, kAPartBytes + 3 * kBBytes);
+            // weight tile: 256 rows (SwiGLU: 128 gate then 128 up rows)
+            if (p.kind == kPrefillPlain) {
+              const int j = output_of(p, x.rt);
+              const int r0 = (x.rt - p.first_tile[j]) * kRows;
+              tma_load_2d(s.a_hi[b.slot], &p.w_maps[j], kb * 32, r0, bar);
+              tma_load_2d(s.a_hi[b.slot] + kTM * 64, &p.w_maps[j], kb * 32,
+                          r0 + kTM, bar);
+            } else {
+              tma_load_2d(s.a_hi[b.slot], &p.w_maps[0], kb * 32, x.rt * kTM,
+                          bar);
+              tma_load_2d(s.a_hi[b.slot] + kTM * 64, &p.w_maps[1], kb * 32,
+                          x.rt * kTM, bar);
+            }
+            tma_load_2d(s.b[b.slot], &p.x_map, kb * 32, row, bar);
+            tma_load_2d(s.a_lo[b.slot], &p.x_map, kb * 32,
+                        row + p.x_plane_rows, bar);
+            tma_load_2d(s.w + b.slot * kBBytes, &p.x_map, kb * 32,
+                        row + 2 * p.x_plane_rows, bar);
+          } else {
+            mbar_arrive_expect_tx(&s.full[b.slot], kBBytes);
+            tma_load_2d(s.b[b.slot], &p.x_map, kb * 32, row, &s.full[b.slot]);
+          }
           b.next(kStages);
         }
       }
@@ -256,6 +292,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t lo = sw64_desc(s.a_lo[st.slot]);
           const uint64_t xb = sw64_desc(s.b[st.slot]);
           const uint32_t acc = kb != x.kb0;
+          if constexpr (kBf16) {
+            const uint64_t x2 = sw64_desc(s.w + st.slot * kBBytes);
+            const uint64_t planes[3] = {xb, lo, x2};
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+              tc_mma(d0, hi, planes[q], q ? 1 : acc, kInstrDescBf16);
+              tc_mma(d0, hi + 2, planes[q] + 2, 1, kInstrDescBf16);
+              tc_mma(d1, hi + 512, planes[q], q ? 1 : acc, kInstrDescBf16);
+              tc_mma(d1, hi + 514, planes[q] + 2, 1, kInstrDescBf16);
+            }
+            tc_commit(&s.empty[st.slot]);
+            st.next(kStages);
+            continue;
+          }
           tc_mma(d0, hi, xb, acc);
           tc_mma(d0, hi + 2, xb + 2, 1);
           tc_mma(d0, lo, xb, 1);
@@ -271,7 +321,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < 10) {
-    // ---- converters: thread owns weight row r of the tile
+    // ---- converters: thread owns weight row r of the tile (Q8_0 only)
+    if constexpr (kBf16)
+      goto done;
     const int r = (warp - 2) * 32 + lane;
     const bool loader = warp == 2 && lane == 0;
     const int swz = (r >> 1) & 3;  // 64-byte swizzle of row r
@@ -398,7 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_ld32(base + kTN + c * 32, v);
           // lane i holds the row scale of prompt row c * 32 + i
           const int tl = c * 32 + lane;
-          const float lane_scale = tl < ntok ? p.scale[tok0 + tl] : 0.f;
+          const float lane_scale =
+              tl < ntok ? (p.scale ? p.scale[tok0 + tl] : 1.0F) : 0.f;
           tc_wait_ld();
           if (c == kTN / 32 - 1)
             release();
@@ -464,7 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tc_ld32(base + acc * kTN + c * 32, v);
           const int tl = c * 32 + lane;
-          const float lane_scale = tl < ntok ? p.scale[tok0 + tl] : 0.f;
+          const float lane_scale =
+              tl < ntok ? (p.scale ? p.scale[tok0 + tl] : 1.0F) : 0.f;
           tc_wait_ld();
           if (acc == 1 && c == kTN / 32 - 1)
             release();
@@ -531,7 +585,7 @@ __global__ void __launch_bounds__(256)
     sum.z += v.z;
     sum.w += v.w;
   }
-  const float sc = p.scale[tok];
+  const float sc = p.scale ? p.scale[tok] : 1.0F;
   const int row = (rt - p.first_tile[j]) * kRows + 4 * q;
   float* out = p.out[j] + size_t(tok) * p.ld[j];
   const float v[4] = {sum.x * sc, sum.y * sc, sum.z * sc, sum.w * sc};
@@ -547,7 +601,7 @@ __global__ void __launch_bounds__(256)
 
 }  // namespace
 
-cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
+cudaError_t launch_q8_prefill(PrefillParams p, const void* x, int x_rows,
                               cudaStream_t stream, int* splits, bool pdl) {
   int device = 0, sms = 148;
   cudaError_t e = cudaGetDevice(&device);
@@ -555,14 +609,22 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
     return e;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   const int smem = int(sizeof(PrefillSmem)) + 1024;
-  e = ensure_dynamic_smem(reinterpret_cast<const void*>(q8_prefill_tc_kernel),
-                          smem);
+  const auto kernel =
+      p.bf16 ? q8_prefill_tc_kernel<true> : q8_prefill_tc_kernel<false>;
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
   if (e != cudaSuccess)
     return e;
-  if (p.K <= 0 || p.K % 256 || p.tokens <= 0 || !x || !p.scale ||
-      x_rows < p.x_row0 + p.tokens)
+  if (p.K <= 0 || p.K % 256 || p.tokens <= 0 || !x ||
+      (!p.scale && !p.bf16) || x_rows < p.x_row0 + p.tokens)
     return cudaErrorInvalidValue;
-  const size_t row_bytes = size_t(p.K / 32) * 34;
+  p.x_plane_rows = x_rows;
+  // weight maps: Q8_0 rows in 8-block chunks, or bf16 [rows][K] tiles
+  const auto weight_map = [&](CUtensorMap* map, const uint8_t* w, int rows,
+                              int box_rows) {
+    return p.bf16 ? cached_activation_map(map, w, rows, p.K, kTM, 32)
+                  : cached_q8_rows(map, w, size_t(p.K / 32) * 34, rows,
+                                   kWRowBytes, box_rows);
+  };
   const int token_tiles = (p.tokens + kTN - 1) / kTN;
   p.splits = 1;
   if (p.kind == kPrefillPlain) {
@@ -574,8 +636,7 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
         return cudaErrorInvalidValue;
       p.first_tile[j] = tiles;
       tiles += (p.o[j].rows + kRows - 1) / kRows;
-      e = cached_q8_rows(&p.w_maps[j], p.o[j].w, row_bytes, p.o[j].rows,
-                         kWRowBytes, kRows);
+      e = weight_map(&p.w_maps[j], p.o[j].w, p.o[j].rows, kRows);
       if (e != cudaSuccess)
         return e;
     }
@@ -605,17 +666,17 @@ cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
     p.n_out = 2;
     p.row_tiles = (p.o[0].rows + kTM - 1) / kTM;
     for (int j = 0; j < 2; ++j) {
-      e = cached_q8_rows(&p.w_maps[j], p.o[j].w, row_bytes, p.o[j].rows,
-                         kWRowBytes, kTM);
+      e = weight_map(&p.w_maps[j], p.o[j].w, p.o[j].rows, kTM);
       if (e != cudaSuccess)
         return e;
     }
   }
-  e = cached_activation_map(&p.x_map, x, x_rows, p.K, kTN, 32);
+  e = cached_activation_map(&p.x_map, x, p.bf16 ? 3 * x_rows : x_rows, p.K,
+                            kTN, 32);
   if (e != cudaSuccess)
     return e;
   const int units = p.row_tiles * token_tiles * p.splits;
-  e = launch_kernel(q8_prefill_tc_kernel, dim3(units < sms ? units : sms),
+  e = launch_kernel(kernel, dim3(units < sms ? units : sms),
                     dim3(kThreads), smem, stream, pdl, p);
   if (splits)
     *splits = p.splits;

@@ -61,14 +61,20 @@ struct PrefillParams {
   // [256 prompt rows][256 output rows], row scales not applied) for the
   // consumer to add in split order, instead of reducing them into o[0].out
   bool keep_splits;
+  // BF16 weights (the numerical-reference models) instead of Q8_0: the
+  // weight tiles come straight from [rows][K] bf16 by TMA, and x is three
+  // bf16 planes (split_bf16_rows) whose sum is the FP32 input exactly,
+  // plane q's rows at q * x_rows of the buffer; scale may be null (1).
+  int bf16;
+  int x_plane_rows;  // filled by launch_q8_prefill: x_rows
 };
 
-// Fills the maps and the tiling of p (x is [x_rows][K] fp16; the pass reads
-// rows x_row0 .. x_row0 + tokens - 1) and launches. K must be a multiple of
-// 256.
+// Fills the maps and the tiling of p (x is [x_rows][K] fp16, or for bf16
+// [3][x_rows][K] bf16 planes; the pass reads rows x_row0 .. x_row0 +
+// tokens - 1) and launches. K must be a multiple of 256.
 // *splits (optional) receives the K ranges used: with keep_splits set and
 // more than one, the output is left as partial sums in `partial`.
-cudaError_t launch_q8_prefill(PrefillParams p, const __half* x, int x_rows,
+cudaError_t launch_q8_prefill(PrefillParams p, const void* x, int x_rows,
                               cudaStream_t stream, int* splits = nullptr,
                               bool pdl = false);
 

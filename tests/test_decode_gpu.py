@@ -4,7 +4,9 @@ and fused four-output projections, gate/up with SwiGLU, K = 2048 and 8192,
 the LM head's height) at 1..8 rows against an FP64 formula, with the
 reference's projection tolerance (tests/ops_test.cpp:46-89: 1e-4). Shapes
 whose tiles fall to several CTAs exercise the ordered partial-sum fix-up;
-repeated calls must agree bit for bit."""
+repeated calls must agree bit for bit. The same shapes with BF16 matrices
+(the numerical-reference weights) run the kernel's BF16 records: each input
+as three exact bf16 terms, products accumulated in FP32."""
 import ctypes
 
 import numpy as np
@@ -39,14 +41,25 @@ def q8_matrix(M, K, seed):
     return blocks.tobytes(), w
 
 
+def bf16_matrix(M, K, seed):
+    """Random BF16 rows ~ N(0, 0.02); returns (bytes, FP64 weights)."""
+    rng = np.random.default_rng(seed)
+    w = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    b = w.to(torch.bfloat16)
+    raw = b.view(torch.int16).numpy().tobytes()
+    return raw, b.to(torch.float64).numpy()
+
+
 class Matrices:
-    def __init__(self, shapes, K, seed=0):
+    def __init__(self, shapes, K, seed=0, bf16=False):
         self.keep, self.tensors, self.w = [], [], []
         for j, M in enumerate(shapes):
-            raw, w = q8_matrix(M, K, seed + j)
+            raw, w = (bf16_matrix if bf16 else q8_matrix)(M, K, seed + j)
             buf = torch.from_numpy(np.frombuffer(raw, np.uint8).copy()).cuda()
             self.keep.append(buf)
-            self.tensors.append(abi.Tensor(buf.data_ptr(), abi.Q8_0, K, M, len(raw)))
+            self.tensors.append(abi.Tensor(buf.data_ptr(),
+                                           abi.BF16 if bf16 else abi.Q8_0, K,
+                                           M, len(raw)))
             self.w.append(w)
         n = len(self.tensors)
         self.array = (ctypes.POINTER(abi.Tensor) * n)(
@@ -136,3 +149,40 @@ def test_refuses_unsupported_shapes():
     arr = (ctypes.POINTER(abi.Tensor) * 1)(ctypes.pointer(bad))
     assert lib.lfm3_cuda_decode_workspace_bytes(arr, 1, 0) == 0
     assert lib.lfm3_cuda_decode_workspace_bytes(mats.array, 1, 1) == 0  # swiglu needs 2
+
+
+@pytest.mark.parametrize("rows", [1, 8])
+@pytest.mark.parametrize("M,K", [(2048, 2048), (2048, 8192), (600, 512),
+                                 (65536, 2048)])
+def test_plain_bf16(rows, M, K):
+    mats = Matrices([M], K, seed=M + K, bf16=True)
+    x = inputs(rows, K)
+    (got,), = project(mats, x)
+    near(got, x.astype(np.float64) @ mats.w[0].T)
+
+
+@pytest.mark.parametrize("rows", [3, 8])
+def test_fused_qkvg_bf16(rows):
+    mats = Matrices([2048, 512, 512, 16], 2048, seed=13, bf16=True)
+    x = inputs(rows, 2048, seed=2)
+    got = project(mats, x)[0]
+    for g, w in zip(got, mats.w):
+        near(g, x.astype(np.float64) @ w.T)
+
+
+@pytest.mark.parametrize("F", [8192, 48])
+def test_swiglu_bf16(F):
+    mats = Matrices([F, F], 2048, seed=F + 1, bf16=True)
+    x = inputs(8, 2048, seed=3)
+    (got,), = project(mats, x, swiglu=True)
+    g = x.astype(np.float64) @ mats.w[0].T
+    u = x.astype(np.float64) @ mats.w[1].T
+    near(got, g / (1 + np.exp(-g)) * u)
+
+
+def test_mixed_types_refused():
+    q = Matrices([64], 512)
+    b = Matrices([64], 512, bf16=True)
+    arr = (ctypes.POINTER(abi.Tensor) * 2)(ctypes.pointer(q.tensors[0]),
+                                           ctypes.pointer(b.tensors[0]))
+    assert lib.lfm3_cuda_decode_workspace_bytes(arr, 2, 0) == 0
