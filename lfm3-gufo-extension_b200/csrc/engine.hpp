@@ -317,6 +317,18 @@ private:
   DecodeRows* host_rows_ = nullptr;
   cudaEvent_t rows_copied_[kRowTables] = {};
   int rows_next_ = 0;
+  // The decode round as a CUDA graph (rounds this session leads): captured
+  // on the second round of a batch composition (sessions by id, width,
+  // logits) and attention span plan, replayed while they hold, updated in
+  // place when only the plan changes. Its row table is copied from
+  // graph_rows_ (pinned), refilled once the previous replay's copy is done.
+  uint64_t uid_ = 0;
+  cudaGraphExec_t round_exec_ = nullptr;
+  std::vector<uint64_t> round_key_, pending_key_;
+  int round_kernels_ = 0;
+  bool round_graphs_ = true;  // off after a capture that failed
+  DecodeRows* graph_rows_ = nullptr;
+  cudaEvent_t graph_rows_copied_ = nullptr;
   // this session's queued work, waited for by a round another session leads
   cudaEvent_t ready_ = nullptr;
   bool profiling_ = false;
@@ -333,6 +345,10 @@ private:
   long long profile_launches_[kProfileClasses] = {};
   template <class F>
   void Timed(int cls, F launch);
+  // Records a decode round's launches (enqueue) as this session's round
+  // graph under `key`; false if capture or instantiation failed.
+  template <class Enqueue>
+  bool CaptureRound(const Enqueue& enqueue, const std::vector<uint64_t>& key);
   void CollectProfile();
   friend class Model;
 };
