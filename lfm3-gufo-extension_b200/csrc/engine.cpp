@@ -639,7 +639,9 @@ void Session::DecodeRound(std::span<Session* const> batch,
   }
   const DecodeRows* dev_rows = rows_.as<DecodeRows>();
   // each attention layer's key spans: about equal lengths over the round's
-  // rows, about four CTAs (one wave) per SM; {tiles per span, spans used}
+  // rows, about four CTAs (one wave) per SM, at least 4 key tiles (a
+  // sliding window's 256 keys stay one span, no merge); {tiles per span,
+  // spans used}
   std::vector<std::pair<int, int>> spans(c.n_layers, {0, 0});
   for (uint32_t i = 0; i < c.n_layers; ++i) {
     if (c.layer_type[i] == LFM3_CONV)
@@ -651,7 +653,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       key_tiles += decode_key_tiles(rows.position[r], window);
     const long slots = 4L * model_->sms();
     const int span_tiles = int(std::max(
-        1L, (key_tiles * long(c.kv_heads[i]) + slots - 1) / slots));
+        4L, (key_tiles * long(c.kv_heads[i]) + slots - 1) / slots));
     int span_grid = 0;
     for (int r = 0; r < B; ++r)
       span_grid = std::max(span_grid,
