@@ -4,17 +4,21 @@
 // span of that row's keys, so ragged depths need no per-row launches. Every
 // CTA normalises and rotates its group's query heads itself (cheap), and the
 // CTA whose span ends at the row's position also stores the new K/V row in
-// the ring. Keys stream through shared memory in tiles of 64 and an online
-// softmax keeps FP32 scores, probabilities and accumulators (the decode
-// precision of hip/ops.hip:1562-1691). Both products run on the tensor cores
-// (mma.sync m16n8k16, FP32 accumulation) with the FP32 operands split in two
-// fp16 terms, x = hi + lo (22 significant bits): S^T = K (Q_hi + Q_lo)^T with
-// the keys as M and the group's heads (padded to 8) as N, then
-// O^T = V^T (P_hi + P_lo)^T with the 128 dimensions as M; K and V are the
-// cache's fp16 values, exactly. With several spans, each CTA writes its
-// maximum, denominator and unnormalised output, and whichever CTA of the
-// group finishes last (a ticket, not a wait) merges them in span order and
-// applies the gate (hip/ops.hip:1710-1728).
+// the ring. Keys stream through shared memory in tiles of 64, three tiles in
+// flight; warp w copies and consumes keys 16 w .. 16 w + 15 of every tile
+// and keeps its own online softmax (FP32 scores, probabilities and
+// accumulators: the decode precision of hip/ops.hip:1562-1691), so warps
+// never wait for one another inside the key loop; the four warps' states
+// merge once at the end. Both products run on the tensor cores (mma.sync
+// m16n8k16, FP32 accumulation) with the FP32 operands split in two fp16
+// terms, x = hi + lo (22 significant bits): S^T = K (Q_hi + Q_lo)^T with the
+// warp's 16 keys as M and the group's heads (padded to 8) as N, then
+// O^T += V^T (P_hi + P_lo)^T with the 128 dimensions as M, the probability
+// fragments transposed in registers (movmatrix); K and V are the cache's
+// fp16 values, exactly. With several spans, each CTA writes its maximum,
+// denominator and unnormalised output, and whichever CTA of the group
+// finishes last (a ticket, not a wait) merges them in span order and applies
+// the gate (hip/ops.hip:1710-1728).
 #include "attention.cuh"
 #include "common.cuh"
 #include "kernels.cuh"
@@ -35,39 +39,63 @@ __device__ __forceinline__ int at64(int row, int piece) {  // 64-wide rows
   return row * kDecodeTile + ((piece ^ (row & 7)) << 3);
 }
 
-// Two key tiles in flight: K and V of tile t in buffer t % 2.
-constexpr int kTileBufs = 2;
+// Three key tiles in flight: K and V of tile t in buffer t % 3.
+constexpr int kTileBufs = 3;
+constexpr int kWarpKeys = kDecodeTile / kWarps;  // keys of a tile per warp
+static_assert(kWarpKeys == 16, "one m16 key block per warp and tile");
 struct DecodeSmem {
   alignas(16) __half k[kTileBufs][kDecodeTile * kHeadDim];  // [key][dim]
   alignas(16) __half v[kTileBufs][kDecodeTile * kHeadDim];  // [key][dim]
   alignas(16) __half qh[8 * kHeadDim], ql[8 * kHeadDim];      // [head][dim]
-  alignas(16) __half ph[8 * kDecodeTile], pl[8 * kDecodeTile];  // [head][key]
-  float tile_max[kWarps][8];
-  float l[kWarps][8];  // running denominators of each warp's keys
+  float wm[kWarps][8], wl[kWarps][8];  // each warp's maxima, denominators
+  float ws[kWarps][8];                 // each warp's merge weight
   float m[8], lsum[8];
   alignas(16) __half newk[kHeadDim], newv[kHeadDim];  // the row at `position`
   int last;
 };
-// After the key loop the first K tile holds the output and the merge
-// weights.
-static_assert(sizeof(float) * (8 * kHeadDim + 2 * 8 * kMaxDecodeSplits) <=
-                  sizeof(__half) * kDecodeTile * kHeadDim,
-              "output staging fits the K tile");
+// After the key loop the K buffers hold the warps' outputs
+// ([warp][head][dim], FP32) and then the span merge weights.
+static_assert(sizeof(float) *
+                      (kWarps * 8 * kHeadDim + 2 * 8 * kMaxDecodeSplits) <=
+                  sizeof(__half) * kTileBufs * kDecodeTile * kHeadDim,
+              "output staging fits the K buffers");
 
-// 16 bytes global -> shared, zero-filled when !valid (cp.async, L1 bypassed)
+// 16 bytes global -> shared, zero-filled when !valid (cp.async, L1
+// bypassed), under an L2 cache policy (the keys and values of a layer are
+// read once per round)
 __device__ __forceinline__ void cp_async16(void* dst, const void* src,
-                                           bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                   smem_addr(dst)),
-               "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
+                                           bool valid, uint64_t policy) {
+  asm volatile(
+      "cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(valid ? 16 : 0), "l"(policy)
+      : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
-// every group but the newest has landed (this thread's copies)
-__device__ __forceinline__ void cp_async_wait_older() {
-  asm volatile("cp.async.wait_group 1;" ::: "memory");
+// every group but the newest kTileBufs - 1 has landed (this thread's copies)
+__device__ __forceinline__ void cp_async_wait_oldest() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kTileBufs - 1) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// The transpose of an 8 x 8 fp16 matrix held one element pair per thread
+// (the mma fragment layout: thread t has row t / 4, columns 2 (t % 4) and
+// 2 (t % 4) + 1), within the warp.
+__device__ __forceinline__ uint32_t transpose8x8(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;"
+               : "=r"(d)
+               : "r"(a));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
+  return uint32_t(__half_as_ushort(lo)) |
+         (uint32_t(__half_as_ushort(hi)) << 16);
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
@@ -138,9 +166,10 @@ __device__ __forceinline__ void norm_rope(float (&x0)[2], float (&x1)[2],
   }
 }
 
-// Four CTAs per SM (128 registers): a round's spans run in one wave.
+// Two CTAs per SM (96 KB of key tiles each): a round's spans run in about
+// one wave.
 template <int G>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 2)
     decode_attention_kernel(const __grid_constant__ DecodeAttentionParams p) {
   extern __shared__ __align__(128) uint8_t decode_smem_raw[];
   DecodeSmem& s = *reinterpret_cast<DecodeSmem*>(decode_smem_raw);
@@ -148,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   // ---- before the dependency wait: the row table (written before the
   // round), the launch's constants and, with settled rings, the first key
-  // tile
+  // tiles
   const bool op = p.rows == nullptr;
   const int position = op ? p.position : p.rows->position[r];
   const LayerState state =
@@ -175,24 +204,27 @@ __global__ void __launch_bounds__(kThreads, 3)
     rot = lane_rotation(p.freq, p.factors, position, lane);
   }
 
-  // ---- K and V rows of a tile (16-byte pieces) copied into buffer
-  // (tile % kTileBufs), one cp.async group per tile (empty past the span)
-  constexpr int kPieces = kDecodeTile * 16 / kThreads;
+  // ---- this warp's 16 keys of a tile (K and V rows as 16-byte pieces)
+  // copied into buffer (tile % kTileBufs); one cp.async group per tile
+  // (empty past the span)
+  const int wkey = warp * kWarpKeys;  // the warp's first key in a tile
+  const uint64_t policy = l2_evict_first_policy();
   const auto issue_tile = [&](int tile) {
-    const int base = begin + tile * kDecodeTile;
+    const int base = begin + tile * kDecodeTile + wkey;
     if (base < end) {
-      const int n = min(kDecodeTile, end - base);
+      const int n = min(kWarpKeys, end - base);
       const int slot0 = base % capacity;  // ring slot of key `base`
       __half* sk = s.k[tile % kTileBufs];
       __half* sv = s.v[tile % kTileBufs];
 #pragma unroll
-      for (int j = 0; j < kPieces; ++j) {
-        const int c = tid + j * kThreads, key = c / 16, piece = c % 16;
-        const int t = base + min(key, n - 1);
+      for (int j = 0; j < kWarpKeys * 16 / 32; ++j) {
+        const int c = lane + j * 32, key = c / 16, piece = c % 16;
+        const int kk = min(key, n - 1);
+        const int t = base + kk;
         const __half *ks = state.k, *vs = state.v;
-        int slot = slot0 + min(key, n - 1);
+        int slot = slot0 + kk;
         if (slot >= capacity)
-          slot = capacity >= kDecodeTile ? slot - capacity : slot % capacity;
+          slot = capacity >= kWarpKeys ? slot - capacity : slot % capacity;
         size_t row = size_t(slot) * stride;
         if (op && t >= position) {
           ks = p.chunk_k;
@@ -200,10 +232,12 @@ __global__ void __launch_bounds__(kThreads, 3)
           row = size_t(t - position) * stride;
         }
         row += size_t(g) * kHeadDim;
-        cp_async16(&sk[at128(key, piece)],
-                   reinterpret_cast<const uint4*>(ks + row) + piece, key < n);
-        cp_async16(&sv[at128(key, piece)],
-                   reinterpret_cast<const uint4*>(vs + row) + piece, key < n);
+        cp_async16(&sk[at128(wkey + key, piece)],
+                   reinterpret_cast<const uint4*>(ks + row) + piece, key < n,
+                   policy);
+        cp_async16(&sv[at128(wkey + key, piece)],
+                   reinterpret_cast<const uint4*>(vs + row) + piece, key < n,
+                   policy);
       }
     }
     cp_async_commit();
@@ -211,19 +245,31 @@ __global__ void __launch_bounds__(kThreads, 3)
   // with settled rings the first tiles are copied while the previous
   // kernel finishes (the row at `position` is patched in below)
   const bool early = !op && p.ring_settled;
-  if (early) {
-    issue_tile(0);
-    issue_tile(1);
-  }
+  if (early)
+#pragma unroll
+    for (int i = 0; i < kTileBufs; ++i)
+      issue_tile(i);
   grid_dependency_wait();
   allow_dependents();
-  if (!early) {
-    issue_tile(0);
-    issue_tile(1);
-  }
+  if (!early)
+#pragma unroll
+    for (int i = 0; i < kTileBufs; ++i)
+      issue_tile(i);
 
   // ---- query heads of this group (normalised, rotated), as hi + lo fp16
-  // terms; heads G..7 are zero
+  // terms; heads G..7 are zero. The new key and value of the row are read
+  // together with the queries.
+  float nk0[2] = {0, 0}, nk1[2] = {0, 0}, nv[4] = {0, 0, 0, 0};
+  const bool new_row = stores_row && warp == 0;
+  if (new_row) {
+    const float* kx = p.k + size_t(r) * p.ldk + size_t(g) * kHeadDim;
+    const float* vx = p.v + size_t(r) * p.ldk + size_t(g) * kHeadDim;
+    nk0[0] = kx[lane], nk0[1] = kx[lane + 32];
+    nk1[0] = kx[lane + 64], nk1[1] = kx[lane + 96];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      nv[j] = vx[lane + 32 * j];
+  }
   for (int h = warp; h < 8; h += kWarps) {
     float x0[2] = {0, 0}, x1[2] = {0, 0};
     if (h < G) {
@@ -244,19 +290,15 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
   }
   // ---- the new K/V row goes to its ring slot (span holding `position`)
-  if (stores_row && warp == 0) {
-    const float* kx = p.k + size_t(r) * p.ldk + size_t(g) * kHeadDim;
-    const float* vx = p.v + size_t(r) * p.ldk + size_t(g) * kHeadDim;
-    float x0[2] = {kx[lane], kx[lane + 32]};
-    float x1[2] = {kx[lane + 64], kx[lane + 96]};
-    norm_rope(x0, x1, kn, rot, p.eps);
+  if (new_row) {
+    norm_rope(nk0, nk1, kn, rot, p.eps);
     const size_t slot = size_t(position % capacity) * stride +
                         size_t(g) * kHeadDim;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int i = lane + 32 * j;
-      const __half k0 = __float2half_rn(x0[j]), k1 = __float2half_rn(x1[j]);
-      const __half v0 = __float2half_rn(vx[i]), v1 = __float2half_rn(vx[i + 64]);
+      const __half k0 = __float2half_rn(nk0[j]), k1 = __float2half_rn(nk1[j]);
+      const __half v0 = __float2half_rn(nv[j]), v1 = __float2half_rn(nv[j + 2]);
       state.k[slot + i] = k0;
       state.k[slot + i + 64] = k1;
       state.v[slot + i] = v0;
@@ -267,164 +309,165 @@ __global__ void __launch_bounds__(kThreads, 3)
       s.newv[i + 64] = v1;
     }
   }
-  if (tid < kWarps * 8)
-    s.l[tid / 8][tid % 8] = 0;
   __syncthreads();
 
   // fragment coordinates: row fg (and fg + 8), column pair 2 cq, 2 cq + 1
   const int fg = lane / 4, cq = lane % 4;
   // ldmatrix lane roles: matrix mj = lane / 8 takes its row from lane mrow
   const int mj = lane / 8, mrow = lane % 8;
-  // this thread's running maxima of heads 2 cq, 2 cq + 1 (every thread holds
-  // the same values) and its O^T fragments of dimension tiles 2 w, 2 w + 1
-  float mrun[2] = {-INFINITY, -INFINITY};
-  float o[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  // the queries as the B operand of S^T = K Q^T, for the whole span
+  uint32_t qbh[kHeadDim / 16][2], qbl[kHeadDim / 16][2];
+#pragma unroll
+  for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+    ldsm_x2(qbh[ks], &s.qh[at128(mrow, 2 * ks + (mj & 1))]);
+    ldsm_x2(qbl[ks], &s.ql[at128(mrow, 2 * ks + (mj & 1))]);
+  }
+  // this warp's running maxima and denominators of heads 2 cq, 2 cq + 1
+  // (every lane holds the same values) and its O^T fragments: dimension
+  // tile mt, rows 16 mt + fg (+ 8), heads 2 cq, 2 cq + 1
+  float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0, 0};
+  float o[kHeadDim / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < kHeadDim / 16; ++mt)
+    o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0;
 
   for (int tile = 0, base = begin; base < end; ++tile, base += kDecodeTile) {
-    const int n = min(kDecodeTile, end - base);
+    const int n = min(kDecodeTile, end - base) - wkey;  // the warp's keys
     __half* const tk = s.k[tile % kTileBufs];
     __half* const tv = s.v[tile % kTileBufs];
-    cp_async_wait_older();  // this tile's group (the next one may fly)
-    __syncthreads();
-    if (stores_row && position >= base && position < base + n) {
-      // the ring slot may have been copied before this CTA wrote it
-      if (tid < 32) {
+    cp_async_wait_oldest();  // this tile's group (the next ones may fly)
+    __syncwarp();
+    if (n > 0) {
+      if (stores_row && position >= base + wkey &&
+          position < base + wkey + n) {
+        // the ring slot may have been copied before this CTA wrote it
         const int key = position - base;
-        for (int piece = tid % 16; piece < 16; piece += 16) {
-          if (tid < 16)
-            *reinterpret_cast<uint4*>(&tk[at128(key, piece)]) =
-                *reinterpret_cast<const uint4*>(&s.newk[piece * 8]);
-          else
-            *reinterpret_cast<uint4*>(&tv[at128(key, piece)]) =
-                *reinterpret_cast<const uint4*>(&s.newv[piece * 8]);
-        }
+        if (lane < 16)
+          *reinterpret_cast<uint4*>(&tk[at128(key, lane)]) =
+              *reinterpret_cast<const uint4*>(&s.newk[lane * 8]);
+        else
+          *reinterpret_cast<uint4*>(&tv[at128(key, lane - 16)]) =
+              *reinterpret_cast<const uint4*>(&s.newv[(lane - 16) * 8]);
+        __syncwarp();
       }
-      __syncthreads();
-    }
-
-    // ---- S^T = K Q^T: warp w owns keys 16 w .. 16 w + 15
-    float sh[4] = {0, 0, 0, 0}, sl[4] = {0, 0, 0, 0};
-    {
-      const int key = warp * 16 + (mj & 1) * 8 + mrow;
+      // ---- S^T = K Q^T over the warp's 16 keys, two accumulation chains
+      float sa[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+      float sb[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+      const int krow = wkey + (mj & 1) * 8 + mrow;
 #pragma unroll
       for (int ks = 0; ks < kHeadDim / 16; ++ks) {
-        uint32_t a[4], bh[2], bl[2];
-        ldsm_x4(a, &tk[at128(key, 2 * ks + (mj >> 1))]);
-        ldsm_x2(bh, &s.qh[at128(mrow, 2 * ks + (mj & 1))]);
-        ldsm_x2(bl, &s.ql[at128(mrow, 2 * ks + (mj & 1))]);
-        mma_f16(sh, a, bh[0], bh[1]);
-        mma_f16(sl, a, bl[0], bl[1]);
-      }
-    }
-    // this thread: keys k0 = 16 w + fg and k0 + 8, heads 2 cq and 2 cq + 1
-    const int k0 = warp * 16 + fg;
-    float sc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      sc[i] = (sh[i] + sl[i]) * kScoreScale;
-    if (k0 >= n)
-      sc[0] = sc[1] = -INFINITY;
-    if (k0 + 8 >= n)
-      sc[2] = sc[3] = -INFINITY;
-    float t0 = fmaxf(sc[0], sc[2]), t1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-    for (int x = 4; x < 32; x <<= 1) {
-      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, x));
-      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, x));
-    }
-    if (fg == 0) {
-      s.tile_max[warp][2 * cq] = t0;
-      s.tile_max[warp][2 * cq + 1] = t1;
-    }
-    __syncthreads();
-    // ---- online softmax over the tile's keys of every warp
-    float top[2] = {s.tile_max[0][2 * cq], s.tile_max[0][2 * cq + 1]};
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) {
-      top[0] = fmaxf(top[0], s.tile_max[w][2 * cq]);
-      top[1] = fmaxf(top[1], s.tile_max[w][2 * cq + 1]);
-    }
-    float alpha[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float next = fmaxf(mrun[h], top[h]);
-      alpha[h] = expf(mrun[h] - next);  // 0 for the first tile
-      mrun[h] = next;
-    }
-    const float pr[4] = {expf(sc[0] - mrun[0]), expf(sc[1] - mrun[1]),
-                         expf(sc[2] - mrun[0]), expf(sc[3] - mrun[1])};
-    float q0 = pr[0] + pr[2], q1 = pr[1] + pr[3];
-#pragma unroll
-    for (int x = 4; x < 32; x <<= 1) {
-      q0 += __shfl_xor_sync(0xffffffffu, q0, x);
-      q1 += __shfl_xor_sync(0xffffffffu, q1, x);
-    }
-    if (fg == 0) {
-      s.l[warp][2 * cq] = s.l[warp][2 * cq] * alpha[0] + q0;
-      s.l[warp][2 * cq + 1] = s.l[warp][2 * cq + 1] * alpha[1] + q1;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int head = 2 * cq + (i & 1), key = k0 + (i >> 1) * 8;
-      const SplitPair t = split_value(pr[i]);
-      s.ph[at64(head, key / 8) + key % 8] = t.hi;
-      s.pl[at64(head, key / 8) + key % 8] = t.lo;
-    }
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      o[mt][0] *= alpha[0];
-      o[mt][1] *= alpha[1];
-      o[mt][2] *= alpha[0];
-      o[mt][3] *= alpha[1];
-    }
-    __syncthreads();
-    // ---- O^T += V^T P^T: warp w owns dimensions 32 w .. 32 w + 31
-#pragma unroll
-    for (int ks = 0; ks < kDecodeTile / 16; ++ks) {
-      uint32_t bh[2], bl[2];
-      ldsm_x2(bh, &s.ph[at64(mrow, 2 * ks + (mj & 1))]);
-      ldsm_x2(bl, &s.pl[at64(mrow, 2 * ks + (mj & 1))]);
-      const int key = ks * 16 + (mj >> 1) * 8 + mrow;
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
         uint32_t a[4];
-        ldsm_x4_trans(a, &tv[at128(key, 2 * (2 * warp + mt) + (mj & 1))]);
-        mma_f16(o[mt], a, bh[0], bh[1]);
-        mma_f16(o[mt], a, bl[0], bl[1]);
+        ldsm_x4(a, &tk[at128(krow, 2 * ks + (mj >> 1))]);
+        mma_f16(sa[ks & 1], a, qbh[ks][0], qbh[ks][1]);
+        mma_f16(sb[ks & 1], a, qbl[ks][0], qbl[ks][1]);
+      }
+      // this thread: keys fg and fg + 8 of the warp's block, heads 2 cq and
+      // 2 cq + 1
+      float sc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        sc[i] = ((sa[0][i] + sa[1][i]) + (sb[0][i] + sb[1][i])) * kScoreScale;
+      if (fg >= n)
+        sc[0] = sc[1] = -INFINITY;
+      if (fg + 8 >= n)
+        sc[2] = sc[3] = -INFINITY;
+      float t0 = fmaxf(sc[0], sc[2]), t1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+      for (int x = 4; x < 32; x <<= 1) {
+        t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, x));
+        t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, x));
+      }
+      // ---- online softmax over the warp's keys (the block's first key is
+      // live, so the maxima are finite)
+      const float top[2] = {fmaxf(mrun[0], t0), fmaxf(mrun[1], t1)};
+      const float alpha[2] = {expf(mrun[0] - top[0]),  // 0 at the first block
+                              expf(mrun[1] - top[1])};
+      mrun[0] = top[0];
+      mrun[1] = top[1];
+      const float pr[4] = {expf(sc[0] - top[0]), expf(sc[1] - top[1]),
+                           expf(sc[2] - top[0]), expf(sc[3] - top[1])};
+      float q0 = pr[0] + pr[2], q1 = pr[1] + pr[3];
+#pragma unroll
+      for (int x = 4; x < 32; x <<= 1) {
+        q0 += __shfl_xor_sync(0xffffffffu, q0, x);
+        q1 += __shfl_xor_sync(0xffffffffu, q1, x);
+      }
+      lrun[0] = lrun[0] * alpha[0] + q0;
+      lrun[1] = lrun[1] * alpha[1] + q1;
+      // P^T as the B operand: the 16 x 8 (key, head) fragments transposed
+      const SplitPair p0 = split_value(pr[0]), p1 = split_value(pr[1]);
+      const SplitPair p2 = split_value(pr[2]), p3 = split_value(pr[3]);
+      const uint32_t bh0 = transpose8x8(pack_half2(p0.hi, p1.hi));
+      const uint32_t bh1 = transpose8x8(pack_half2(p2.hi, p3.hi));
+      const uint32_t bl0 = transpose8x8(pack_half2(p0.lo, p1.lo));
+      const uint32_t bl1 = transpose8x8(pack_half2(p2.lo, p3.lo));
+      // ---- O^T += V^T P^T over all 128 dimensions
+      const int vrow = wkey + (mj >> 1) * 8 + mrow;
+#pragma unroll
+      for (int mt = 0; mt < kHeadDim / 16; ++mt) {
+        o[mt][0] *= alpha[0];
+        o[mt][1] *= alpha[1];
+        o[mt][2] *= alpha[0];
+        o[mt][3] *= alpha[1];
+        uint32_t a[4];
+        ldsm_x4_trans(a, &tv[at128(vrow, 2 * mt + (mj & 1))]);
+        mma_f16(o[mt], a, bh0, bh1);
+        mma_f16(o[mt], a, bl0, bl1);
       }
     }
-    __syncthreads();  // this tile's buffers and p are free
+    __syncwarp();  // the warp's rows of this buffer are free
     issue_tile(tile + kTileBufs);
   }
 
-  // ---- O (FP32 [head][dim]), maxima and denominators to shared memory
-  float* so = reinterpret_cast<float*>(s.k[0]);
+  // ---- the warps' states merged: O (FP32 [warp][head][dim]), maxima and
+  // denominators through shared memory
+  cp_async_wait_all();
+  __syncthreads();  // every warp is done with the key buffers
+  float* wo = reinterpret_cast<float*>(s.k[0]);
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    const int dim = (2 * warp + mt) * 16 + fg;
-    so[(2 * cq) * kHeadDim + dim] = o[mt][0];
-    so[(2 * cq + 1) * kHeadDim + dim] = o[mt][1];
-    so[(2 * cq) * kHeadDim + dim + 8] = o[mt][2];
-    so[(2 * cq + 1) * kHeadDim + dim + 8] = o[mt][3];
+  for (int mt = 0; mt < kHeadDim / 16; ++mt) {
+    const int dim = mt * 16 + fg;
+    float* w0 = wo + (warp * 8 + 2 * cq) * kHeadDim;
+    float* w1 = w0 + kHeadDim;
+    w0[dim] = o[mt][0];
+    w1[dim] = o[mt][1];
+    w0[dim + 8] = o[mt][2];
+    w1[dim + 8] = o[mt][3];
   }
-  if (warp == 0 && fg == 0) {
-    s.m[2 * cq] = mrun[0];
-    s.m[2 * cq + 1] = mrun[1];
+  if (fg == 0) {
+    s.wm[warp][2 * cq] = mrun[0];
+    s.wm[warp][2 * cq + 1] = mrun[1];
+    s.wl[warp][2 * cq] = lrun[0];
+    s.wl[warp][2 * cq + 1] = lrun[1];
   }
   __syncthreads();
   if (tid < 8) {
-    float l = 0;
+    float top = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w)
-      l += s.l[w][tid];
+      top = fmaxf(top, s.wm[w][tid]);
+    float l = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      // a warp without live keys has maximum -inf and weight 0
+      const float f = s.wm[w][tid] == -INFINITY ? 0.0F : expf(s.wm[w][tid] - top);
+      s.ws[w][tid] = f;
+      l = fmaf(s.wl[w][tid], f, l);
+    }
+    s.m[tid] = top;
     s.lsum[tid] = l;
   }
   __syncthreads();
   const int d = tid;
   float acc[G];
 #pragma unroll
-  for (int h = 0; h < G; ++h)
-    acc[h] = so[h * kHeadDim + d];
+  for (int h = 0; h < G; ++h) {
+    float a = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w)
+      a = fmaf(wo[(w * 8 + h) * kHeadDim + d], s.ws[w][h], a);
+    acc[h] = a;
+  }
   if (used == 1) {
 #pragma unroll
     for (int h = 0; h < G; ++h) {
@@ -468,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   __threadfence();
   // every span's maximum and denominator at once, then the span weights
   // exp(m_sp - max) per head (one thread per head), then the outputs
-  float* mw = so + 8 * kHeadDim;  // [span][8]
+  float* mw = wo + kWarps * 8 * kHeadDim;  // [span][8]
   float* lw = mw + 8 * kMaxDecodeSplits;
   for (int i = tid; i < used * G; i += kThreads) {
     const int sp = i / G, h = i % G;

@@ -568,11 +568,22 @@ void Session::TakeProfile(double* ms, long long* launches) {
 
 // Launches one projection of the round's rows over a packed decode group
 // (Q8_0 models): the same outputs and epilogue as the GemvParams describe.
+// The first bytes of the next projection a launch asks into L2 (its CTAs
+// become resident only after this launch's leave, and read these first).
+constexpr size_t kDecodePrefetchBytes = size_t(8) << 20;
+
 static cudaError_t RunDecode(const GemvParams& g, const DecodeGroup& group,
-                             Model& model, cudaStream_t stream) {
+                             Model& model, cudaStream_t stream,
+                             const DecodeGroup* next = nullptr) {
   DecodeParams p{};
   p.layout = group.layout;
   p.w = group.data;
+  if (next && next->data) {
+    p.prefetch = next->data;
+    p.prefetch_bytes =
+        std::min(kDecodePrefetchBytes, decode_packed_bytes(next->layout)) /
+        16 * 16;
+  }
   p.tokens = g.tokens;
   p.x = g.x;
   for (int j = 0; j < 4; ++j)
@@ -618,9 +629,21 @@ void Session::DecodeRound(std::span<Session* const> batch,
   cudaStream_t s = stream_;
   // a projection of the round's rows through the layer's packed decode
   // group (Q8_0 or BF16)
-  const auto gemv = [&](GemvParams p, const DecodeGroup& group) {
+  // `next`: the projection that follows in the round (its first weights go
+  // to L2 while this one finishes)
+  const auto gemv = [&](GemvParams p, const DecodeGroup& group,
+                        const DecodeGroup* next) {
     Timed(kDecodeProjection,
-          [&] { Check(RunDecode(p, group, *model_, s)); });
+          [&] { Check(RunDecode(p, group, *model_, s, next)); });
+  };
+  // the first projection of the layer after layer i (the LM head after the
+  // last layer when the round computes logits)
+  const auto next_layer = [&](uint32_t i) -> const DecodeGroup* {
+    if (i + 1 < c.n_layers) {
+      const DecodeLayer& n = model_->decode_layer(i + 1);
+      return c.layer_type[i + 1] == LFM3_CONV ? &n.in_proj : &n.qkvg;
+    }
+    return logits ? &model_->decode_head() : nullptr;
   };
   // an earlier round that returned without waiting and has finished reports
   // its device wait failures here
@@ -639,8 +662,9 @@ void Session::DecodeRound(std::span<Session* const> batch,
   }
   const DecodeRows* dev_rows = rows_.as<DecodeRows>();
   // each attention layer's key spans: about equal lengths over the round's
-  // rows, about four CTAs (one wave) per SM, at least 4 key tiles (a
-  // sliding window's 256 keys stay one span, no merge); {tiles per span,
+  // rows, about two CTAs (one wave) per SM; full-attention spans hold at
+  // least 4 key tiles (fewer partial results to merge), sliding-window spans
+  // may hold one (a window's 4 tiles spread over 4 SMs); {tiles per span,
   // spans used}
   std::vector<std::pair<int, int>> spans(c.n_layers, {0, 0});
   for (uint32_t i = 0; i < c.n_layers; ++i) {
@@ -651,9 +675,9 @@ void Session::DecodeRound(std::span<Session* const> batch,
     long key_tiles = 0;
     for (int r = 0; r < B; ++r)
       key_tiles += decode_key_tiles(rows.position[r], window);
-    const long slots = 4L * model_->sms();
+    const long slots = 2L * model_->sms();
     const int span_tiles = int(std::max(
-        4L, (key_tiles * long(c.kv_heads[i]) + slots - 1) / slots));
+        window ? 1L : 4L, (key_tiles * long(c.kv_heads[i]) + slots - 1) / slots));
     int span_grid = 0;
     for (int r = 0; r < B; ++r)
       span_grid = std::max(span_grid,
@@ -719,7 +743,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
         p.layer = int(i);
         p.H = H;
         p.L = int(c.conv_width);
-        gemv(p, dl.in_proj);
+        gemv(p, dl.in_proj, &dl.out_proj);
         GemvParams o{};
         o.kind = kGemvPlain;
         o.K = H;
@@ -727,7 +751,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
         o.n_out = 1;
         o.o[0] = Out(l.out_proj, out, H);
         o.x = a_split_.data();
-        gemv(o, dl.out_proj);
+        gemv(o, dl.out_proj, &dl.gate_up);
       } else {
         const int kv = int(c.kv_heads[i]) * 128;
         GemvParams p{};
@@ -740,7 +764,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
         p.o[2] = Out(l.v, v_.as<float>(), kv);
         p.o[3] = Out(l.attn_gate, gate_.as<float>(), c.heads);
         p.x = z;
-        gemv(p, dl.qkvg);
+        gemv(p, dl.qkvg, &dl.attn_out);
         const bool swa = c.layer_type[i] == LFM3_SLIDING_ATTENTION;
         DecodeAttentionParams ap{};
         ap.q = q_.as<float>();
@@ -778,7 +802,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
         o.n_out = 1;
         o.o[0] = Out(l.attn_out, out, H);
         o.x = a_split_.data();
-        gemv(o, dl.attn_out);
+        gemv(o, dl.attn_out, &dl.gate_up);
       }
       Timed(kRowKernels, [&] {
         Check(launch_residual_norm(
@@ -796,7 +820,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       f.x = z;
       f.split_out = h_split_.data();
       f.split_width = F;
-      gemv(f, dl.gate_up);
+      gemv(f, dl.gate_up, &dl.down);
       GemvParams d{};
       d.kind = kGemvPlain;
       d.K = F;
@@ -804,7 +828,7 @@ void Session::DecodeRound(std::span<Session* const> batch,
       d.n_out = 1;
       d.o[0] = Out(l.down, out, H);
       d.x = h_split_.data();
-      gemv(d, dl.down);
+      gemv(d, dl.down, next_layer(i));
       const bool last = i + 1 == c.n_layers;
       const float* next = static_cast<const float*>(
           last ? w.output_norm.data : w.layers[i + 1].norm.data);

@@ -53,7 +53,7 @@ struct DecodeSmem {
   alignas(16) float tile[kDecMaxMtiles * 128];
   uint64_t full[kDecMaxSlots];
   uint64_t empty[kDecMaxSlots];
-  uint64_t x_full;
+  uint64_t x_full[kDecMaxXChunks];  // kStaged: unit c's input columns landed
 };
 
 // Four biased codes (u = q + 128, one little-endian word) as two half2 of q,
@@ -221,7 +221,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], kDecWarps);
     }
-    mbar_init(&s.x_full, 1);
+    for (int i = 0; i < kDecMaxXChunks; ++i)
+      mbar_init(&s.x_full[i], 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -237,14 +238,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     int slot = 0, issued = 0;
     uint32_t phase = 0;
     bool x_sent = !kStaged;
+    const uint64_t policy = l2_evict_first_policy();  // weights: read once
+    // the inputs in unit-sized column chunks, each on its own barrier, so
+    // the consumers start on unit 0 while the later chunks fly
     const auto send_x = [&] {
       grid_dependency_wait();
       const uint32_t row = uint32_t(p.layout.K) * 4;
-      mbar_arrive_expect_tx(&s.x_full, row * uint32_t(p.tokens));
-      for (int g = 0; g < p.tokens; ++g)
-        bulk_load(s.x + g * kDecXRowBytes,
-                  static_cast<const uint8_t*>(p.x) + size_t(g) * row, row,
-                  &s.x_full);
+      constexpr uint32_t chunk = 32 * kUB * 4;  // one unit's columns
+      for (int c = 0; c < C; ++c) {
+        mbar_arrive_expect_tx(&s.x_full[c], chunk * uint32_t(p.tokens));
+        for (int g = 0; g < p.tokens; ++g)
+          bulk_load(s.x + g * kDecXRowBytes + c * chunk,
+                    static_cast<const uint8_t*>(p.x) + size_t(g) * row +
+                        c * chunk,
+                    chunk, &s.x_full[c]);
+      }
       x_sent = true;
     };
     for (int t = blockIdx.x; t < p.layout.tiles; t += G)
@@ -255,8 +263,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (!mbar_wait(&s.empty[slot], phase ^ 1, kErrGemvEmptyWait))
           return;
         mbar_arrive_expect_tx(&s.full[slot], kW);
-        bulk_load(s.ring + slot * kW, p.w + (size_t(t) * C + c) * kW, kW,
-                  &s.full[slot]);
+        bulk_load_hint(s.ring + slot * kW, p.w + (size_t(t) * C + c) * kW,
+                       kW, &s.full[slot], policy);
         if (++slot == kSlots) {
           slot = 0;
           phase ^= 1;
@@ -264,14 +272,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       }
     if (!x_sent)
       send_x();
+    // this CTA's slice of the next projection's first weights into L2
+    if (p.prefetch_bytes) {
+      const size_t per = (p.prefetch_bytes / G + 15) & ~size_t(15);
+      const size_t lo = per * blockIdx.x;
+      const size_t hi =
+          lo + per < p.prefetch_bytes ? lo + per : p.prefetch_bytes;
+      for (size_t at = lo; at < hi; at += 65536)
+        prefetch_l2(p.prefetch + at,
+                    uint32_t(hi - at < 65536 ? hi - at : 65536));
+    }
     return;
   }
 
   // ---- consumers
   grid_dependency_wait();
-  if constexpr (kStaged)
-    if (!mbar_wait(&s.x_full, 0, kErrGemvFullWait))
-      return;
   const int g = lane >> 2, cq = lane & 3;
   const bool live = g < p.tokens;
   const uint4* xr = static_cast<const uint4*>(p.x);
@@ -310,10 +325,19 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       for (int j = 0; j < 4; ++j)
         acc[m][j] = 0;
     Terms cur, next;
-    fetch(0, cur);
+    if constexpr (!kStaged)
+      fetch(0, cur);
     for (int c = 0; c < C; ++c) {
-      if (c + 1 < C)
+      if constexpr (kStaged) {
+        // shared-memory terms of this unit, once its chunk has landed (the
+        // first tile waits; the barriers stay complete for later tiles)
+        if (t == int(blockIdx.x) &&
+            !mbar_wait(&s.x_full[c], 0, kErrGemvFullWait))
+          return;
+        fetch(c, cur);
+      } else if (c + 1 < C) {
         fetch(c + 1, next);
+      }
       if (!mbar_wait(&s.full[slot], phase, kErrGemvFullWait))
         return;
       const uint8_t* base = s.ring + slot * kW;
@@ -376,7 +400,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         slot = 0;
         phase ^= 1;
       }
-      cur = next;
+      if constexpr (!kStaged)
+        cur = next;
     }
     decode_finish<kKind, kMT>(p, s, acc, t);
   }
@@ -453,11 +478,10 @@ __global__ void decode_pack_kernel(const DecodeLayout l, const uint8_t* s0,
 template <int kKind, int kMT>
 cudaError_t launch_kind(const DecodeParams& p, int grid, cudaStream_t stream,
                         bool pdl) {
-  // inputs of K <= kDecStagedK columns staged in shared memory when CTAs
-  // hold several tiles (read once per CTA instead of once per tile; with
-  // one tile per CTA waiting for all of the inputs up front costs more than
-  // fetching each unit's terms one unit ahead)
-  const bool staged = p.layout.K <= kDecStagedK && p.layout.tiles > grid;
+  // inputs of K <= kDecStagedK columns staged in shared memory: read once
+  // per CTA, all chunks requested at once after the dependency wait, instead
+  // of an L2 round trip per unit
+  const bool staged = p.layout.K <= kDecStagedK;
   auto kernel = staged ? decode_gemv_kernel<kKind, kMT, 16, true, false>
                        : decode_gemv_kernel<kKind, kMT, 16, false, false>;
   if constexpr (kMT == 1)

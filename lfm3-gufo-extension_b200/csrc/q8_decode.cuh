@@ -40,11 +40,13 @@ constexpr int kDecThreads = (kDecWarps + 1) * 32;  // + the producer warp
 // Shared-memory ring: 9 slots of 17 KB units, 6 of 26 KB, 4 of 35 KB.
 constexpr int kDecRingBytes = 156672;
 constexpr int kDecMaxSlots = 9;
-// Projections with K <= kDecStagedK and more tiles than CTAs keep the
-// round's input records in shared memory (one bulk copy per token, rows padded by 16 bytes so the
-// fragment loads hit distinct banks) beside a smaller ring: 8 slots of
-// 17 KB, 5 of 26 KB, 4 of 35 KB.
+// Projections with K <= kDecStagedK keep the round's input records in
+// shared memory (bulk copies of unit-sized column chunks per token, each
+// chunk on its own barrier; rows padded by 16 bytes so the fragment loads
+// hit distinct banks) beside a smaller ring: 8 slots of 17 KB, 5 of 26 KB,
+// 4 of 35 KB.
 constexpr int kDecStagedK = 2048;
+constexpr int kDecMaxXChunks = kDecStagedK / (32 * 8);  // units of >= 8 blocks
 constexpr int kDecXRowBytes = kDecStagedK * 4 + 16;
 constexpr int kDecRingStaged = 139264;
 constexpr int kDecMaxMtiles = 4;
@@ -135,6 +137,12 @@ struct DecodeParams {
   const DecodeRows* rows;
   int layer;
   int L;
+  // Optional: the first prefetch_bytes of the next projection's packed copy,
+  // asked into L2 in equal slices by the CTAs once their own weight copies
+  // are issued, so the next launch's CTAs (resident only after these leave)
+  // read their first units from L2 rather than HBM. 16-byte aligned.
+  const uint8_t* prefetch;
+  size_t prefetch_bytes;
 };
 
 // CTAs of a launch: one per SM, at most one per tile.
