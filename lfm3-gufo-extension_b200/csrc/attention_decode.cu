@@ -261,6 +261,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   // together with the queries.
   float nk0[2] = {0, 0}, nk1[2] = {0, 0}, nv[4] = {0, 0, 0, 0};
   const bool new_row = stores_row && warp == 0;
+  float gate[G];  // the group's gates, used once the span is done
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    gate[h] = p.gate[size_t(r) * p.ldg + g * G + h];
   if (new_row) {
     const float* kx = p.k + size_t(r) * p.ldk + size_t(g) * kHeadDim;
     const float* vx = p.v + size_t(r) * p.ldk + size_t(g) * kHeadDim;
@@ -472,8 +476,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const int head = g * G + h;
-      const float gate = p.gate[size_t(r) * p.ldg + head];
-      const float y = (acc[h] / s.lsum[h]) / (1 + expf(-gate));
+      const float y = (acc[h] / s.lsum[h]) / (1 + expf(-gate[h]));
       if (p.out_split)
         store_split(p.out_split, r, p.heads * kHeadDim, head * kHeadDim + d, y);
       if (p.out_f32)
@@ -558,8 +561,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     const int head = g * G + h;
-    const float gate = p.gate[size_t(r) * p.ldg + head];
-    const float y = (value[h] / s.lsum[h]) / (1 + expf(-gate));
+    const float y = (value[h] / s.lsum[h]) / (1 + expf(-gate[h]));
     if (p.out_split)
       store_split(p.out_split, r, p.heads * kHeadDim, head * kHeadDim + d, y);
     if (p.out_f32)

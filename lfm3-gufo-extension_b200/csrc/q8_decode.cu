@@ -113,9 +113,39 @@ __device__ __forceinline__ void split_bf16(uint32_t hi, uint32_t lo,
   }
 }
 
+// A convolution step's window (the weights and the row's history) read by
+// the thread that will need it before the dependency wait: the row table
+// and each session's history are complete before the round's first kernel,
+// and only this launch's epilogue writes this layer's history.
+constexpr int kConvPreMax = 8;  // widths up to this are preloaded
+struct ConvPre {
+  float w[kConvPreMax], h[kConvPreMax];
+  bool ok;
+};
+template <int kKind, int kMT>
+__device__ void conv_preload(const DecodeParams& p, int t, int tid,
+                             ConvPre& pre) {
+  pre.ok = false;
+  if constexpr (kKind == kDecConv) {
+    constexpr int kCh = 16 * (kMT / 3);
+    const int tok = tid / kCh, c = tid % kCh, ch = t * kCh + c, L = p.L;
+    if (tid >= kCh * 8 || tok >= p.tokens || ch >= p.layout.H ||
+        L > kConvPreMax || t >= p.layout.tiles)
+      return;
+    const float* own = p.rows->layers[tok][p.layer].conv + size_t(ch) * (L - 1);
+    const float* w = p.conv_w + size_t(ch) * L;
+#pragma unroll
+    for (int j = 0; j < kConvPreMax; ++j) {
+      pre.w[j] = j < L ? w[j] : 0.0F;
+      pre.h[j] = j < L - 1 ? own[j] : 0.0F;
+    }
+    pre.ok = true;
+  }
+}
+
 template <int kKind, int kMT>
 __device__ void decode_epilogue(const DecodeParams& p, const float* tile,
-                                int t, int tid) {
+                                int t, int tid, const ConvPre& pre) {
   if constexpr (kKind == kDecPlain) {
     // token-major so consecutive threads store consecutive rows
     for (int e = tid; e < kMT * 128; e += kDecWarps * 32) {
@@ -163,11 +193,25 @@ __device__ void decode_epilogue(const DecodeParams& p, const float* tile,
       const float* w = p.conv_w + size_t(ch) * L;
       const float current = b * x;
       float sum = 0;
-      for (int j = 0; j < L - 1; ++j)
-        sum = fmaf(w[j], own[j], sum);
-      sum = fmaf(w[L - 1], current, sum);
-      for (int j = 0; j < L - 2; ++j)
-        own[j] = own[j + 1];
+      if (pre.ok && e == tid && t == int(blockIdx.x)) {
+#pragma unroll
+        for (int j = 0; j < kConvPreMax; ++j) {
+          if (j < L - 1)
+            sum = fmaf(pre.w[j], pre.h[j], sum);
+          else if (j == L - 1)
+            sum = fmaf(pre.w[j], current, sum);
+        }
+#pragma unroll
+        for (int j = 0; j < kConvPreMax - 2; ++j)
+          if (j < L - 2)
+            own[j] = pre.h[j + 1];
+      } else {
+        for (int j = 0; j < L - 1; ++j)
+          sum = fmaf(w[j], own[j], sum);
+        sum = fmaf(w[L - 1], current, sum);
+        for (int j = 0; j < L - 2; ++j)
+          own[j] = own[j + 1];
+      }
       own[L - 2] = current;
       store_split(p.split_out, tok, p.split_width, ch, sum * cg);
     }
@@ -178,7 +222,8 @@ __device__ void decode_epilogue(const DecodeParams& p, const float* tile,
 // then the epilogue.
 template <int kKind, int kMT, class Smem>
 __device__ void decode_finish(const DecodeParams& p, Smem& s,
-                              const float (&acc)[kMT][4], int t) {
+                              const float (&acc)[kMT][4], int t,
+                              const ConvPre& pre) {
   constexpr int kThreads = kDecWarps * 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, cq = lane & 3;
@@ -198,7 +243,7 @@ __device__ void decode_finish(const DecodeParams& p, Smem& s,
     s.tile[e] = v;
   }
   named_barrier(1, kThreads);
-  decode_epilogue<kKind, kMT>(p, s.tile, t, tid);
+  decode_epilogue<kKind, kMT>(p, s.tile, t, tid, pre);
   named_barrier(1, kThreads);
 }
 
@@ -286,6 +331,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
 
   // ---- consumers
+  ConvPre pre;
+  conv_preload<kKind, kMT>(p, blockIdx.x, tid, pre);
   grid_dependency_wait();
   const int g = lane >> 2, cq = lane & 3;
   const bool live = g < p.tokens;
@@ -403,7 +450,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       if constexpr (!kStaged)
         cur = next;
     }
-    decode_finish<kKind, kMT>(p, s, acc, t);
+    decode_finish<kKind, kMT>(p, s, acc, t, pre);
   }
 }
 
