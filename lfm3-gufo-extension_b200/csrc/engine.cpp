@@ -1225,6 +1225,17 @@ void Session::Prompt(std::span<const uint32_t> tokens, bool want_logits,
           [&] { LaunchLmHead(z_split_.data(), 1, logits_.as<float>()); });
 }
 
+// After a round this session led has finished: its last kernel copied the
+// device error word into the model's host-mapped word, so a round that went
+// through needs no device read (a synchronous copy on every step).
+void Session::ThrowRoundErrors() {
+  if (!model_->RoundErrors())
+    return;
+  model_->ClearRoundErrors();
+  const unsigned e = take_device_error();
+  throw std::runtime_error("device wait gave up, code " + std::to_string(e));
+}
+
 // Waits for everything queued for this session (its own stream also waits
 // for rounds other sessions led) and reports a device wait that gave up.
 void Session::Settle() {
@@ -1494,9 +1505,7 @@ bool Session::Batch(std::span<Session* const> sessions,
           front->Check(cudaStreamWaitEvent(s->stream_, front->round_done_, 0));
     } else {
       front->Check(cudaStreamSynchronize(front->stream_));
-      if (const unsigned e = take_device_error())
-        throw std::runtime_error("device wait gave up, code " +
-                                 std::to_string(e));
+      front->ThrowRoundErrors();
       front->CollectProfile();
     }
     for (size_t r = 0; r < sessions.size(); ++r) {
@@ -1573,9 +1582,7 @@ bool Session::ForwardBatchSample(std::span<Session* const> sessions,
                                  size_t(B) * sizeof(uint32_t),
                                  cudaMemcpyDeviceToHost, front->stream_));
     front->Check(cudaStreamSynchronize(front->stream_));
-    if (const unsigned e = take_device_error())
-      throw std::runtime_error("device wait gave up, code " +
-                               std::to_string(e));
+    front->ThrowRoundErrors();  // the selection kernels do not wait
     front->CollectProfile();
     std::copy(front->sample_host_, front->sample_host_ + B, next.begin());
     return true;

@@ -287,6 +287,8 @@ private:
                     bool device_logits, std::string* error,
                     std::span<const float* const> rows = {});
   void LaunchLmHead(const void* split_rows, int rows, float* out);
+  // a finished round's device wait failures (the host-mapped word), thrown
+  void ThrowRoundErrors();
 
   std::shared_ptr<Model> model_;
   cudaStream_t stream_ = nullptr;

@@ -315,6 +315,37 @@ def test_device_wait_failure_reported_by_next_round(small):
     np.testing.assert_array_equal(a.forward([1, 2, 3]), fresh.forward([1, 2, 3]))
 
 
+@pytest.mark.parametrize("sample", [True, False])
+def test_device_wait_failure_reported_by_synchronous_round(small, sample):
+    """ForwardBatchSample and ForwardBatch (logits) wait for their round and
+    read the failure from the host-mapped word the round's last kernel
+    wrote: the call fails, poisons its sessions and consumes the code."""
+    w, model = small
+    lib = lfm3.library()
+    a, b = model.session(64), model.session(64)
+    a.forward([1, 2, 3], logits=False)
+    b.forward([4, 5], logits=False)
+    torch.cuda.synchronize()
+    lib.lfm3_cuda_take_device_error()
+    lfm3.check(lib.lfm3_cuda_wait_probe(5000, None))
+    torch.cuda.synchronize()
+    with pytest.raises(lfm3.Lfm3Error):
+        if sample:
+            lfm3.Session.forward_batch_sample([a, b], [6, 7],
+                                              lfm3.sampler(0.0, 1, 1.0))
+        else:
+            lfm3.Session.forward_batch([a, b], [6, 7])
+    assert not a.coherent and not b.coherent
+    assert lib.lfm3_cuda_take_device_error() == 0
+    a.reset()
+    b.reset()
+    # a clean round afterwards goes through
+    a.forward([1, 2, 3], logits=False)
+    b.forward([4, 5], logits=False)
+    lfm3.Session.forward_batch_sample([a, b], [6, 7], lfm3.sampler(0.0, 1, 1.0))
+    assert a.coherent and b.coherent
+
+
 # ---- BF16 numerical-reference weights (north-star logits tolerance 2e-2) ------
 BF16_MAX_ABS = 2e-2
 
