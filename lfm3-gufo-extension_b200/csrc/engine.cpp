@@ -566,12 +566,13 @@ void Session::TakeProfile(double* ms, long long* launches) {
 
 // ---- decode round -------------------------------------------------------------
 
-// Launches one projection of the round's rows over a packed decode group
-// (Q8_0 models): the same outputs and epilogue as the GemvParams describe.
 // The first bytes of the next projection a launch asks into L2 (its CTAs
 // become resident only after this launch's leave, and read these first).
 constexpr size_t kDecodePrefetchBytes = size_t(8) << 20;
 
+// Launches one projection of the round's rows over a packed decode group
+// (Q8_0 or BF16 copies): the same outputs and epilogue as the GemvParams
+// describe; `next`, when given, is the projection that follows it.
 static cudaError_t RunDecode(const GemvParams& g, const DecodeGroup& group,
                              Model& model, cudaStream_t stream,
                              const DecodeGroup* next = nullptr) {
