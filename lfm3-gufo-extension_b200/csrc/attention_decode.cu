@@ -35,9 +35,6 @@ constexpr float kScoreScale = 0.0883883476483184405F;  // 1 / sqrt(128)
 __device__ __forceinline__ int at128(int row, int piece) {  // 128-wide rows
   return row * kHeadDim + ((piece ^ (row & 7)) << 3);
 }
-__device__ __forceinline__ int at64(int row, int piece) {  // 64-wide rows
-  return row * kDecodeTile + ((piece ^ (row & 7)) << 3);
-}
 
 // Three key tiles in flight: K and V of tile t in buffer t % 3.
 constexpr int kTileBufs = 3;
