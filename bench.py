@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="no timing: a fixed launch sequence for ncu captures "
                          "(see profile_sequence)")
+    ap.add_argument("--profile-bf16", action="store_true",
+                    help="no timing: the same sequence over BF16 weights "
+                         "(config 4's matrix type)")
     ap.add_argument("--configs", nargs="?", const="2,5,4", default=None,
                     help="BASELINE configs 2, 4 and a one-GPU slice of 5 (a comma "
                          "list selects), one JSON line each (see config_runs); not "
@@ -614,17 +617,21 @@ PROFILE_PROMPT = 64
 PROFILE_WARM_ROUNDS = 3
 
 
-def profile_sequence():
+def profile_sequence(matrix_type=None):
     """A fixed, untimed launch sequence for ncu: 8 sessions prefilled with
     64-token prompts (one prompt pass each, whose last row's logits take one
     LM-head decode_gemv launch), 3 warm decode rounds, then the captured work: one
     decode round of the 8 rows, then one 512-row prompt pass on session 0.
     Before the captured round: 8 + 3 x 97 = 299 decode_gemv launches and
     8 x 96 = 768 q8_prefill_tc_kernel launches (24 layers: 4 projection
-    launches per layer)."""
+    launches per layer). With matrix_type BF16 (--profile-bf16) the weights
+    are BF16: the decode rounds run decode_gemv_kernel's BF16 instantiations
+    and each prompt projection is split_bf16_rows_kernel then
+    q8_prefill_tc_kernel<1>."""
     import torch
     lfm3 = importlib.import_module("lfm3-gufo-extension_b200")
-    weights = lfm3.SyntheticWeights(seed=0)
+    weights = (lfm3.SyntheticWeights(seed=0) if matrix_type is None else
+               lfm3.SyntheticWeights(seed=0, matrix_type=matrix_type))
     cfg = weights.config
     model = lfm3.Model(weights.weights)
     rng = np.random.default_rng([1, 0])
@@ -827,6 +834,10 @@ def main():
         return
     if args.profile:
         profile_sequence()
+        return
+    if args.profile_bf16:
+        profile_sequence(importlib.import_module(
+            "lfm3-gufo-extension_b200").abi.BF16)
         return
     if args.profile_workload:
         profile_workload(args.prompt_max)
