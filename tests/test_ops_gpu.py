@@ -292,6 +292,16 @@ def test_long_decode_history(window):
     run_attention(1, window, P=4999)
 
 
+# Decode rows whose keys end at, just before or just after a warp's 16-key
+# block and a 64-key tile (each warp of the decode kernel owns 16 keys of a
+# tile, so warps with no keys, a partial block and a partial tile all occur).
+@pytest.mark.parametrize("P", [0, 1, 14, 15, 16, 17, 47, 48, 63, 64, 65, 255, 256, 257])
+@pytest.mark.parametrize("window", [0, 256])
+@pytest.mark.parametrize("heads", [(4, 2), (16, 4)])
+def test_decode_key_block_edges(P, window, heads):
+    run_attention(1, window, P=P, H=heads[0], KH=heads[1])
+
+
 @pytest.mark.parametrize("window", [0, 256])
 def test_prompt_over_long_history(window):
     run_attention(40, window, P=17000)
