@@ -357,7 +357,30 @@ void Model::PackDecodeGroups() {
       add(d.attn_out, kDecPlain, A, {&l.attn_out});
     }
     add(d.gate_up, kDecSwiGLU, H, {&l.gate, &l.up});
-    add(d.down, kDecPlain, F, {&l.down});
+    if (!bf16() && F % 1024 == 0 && F > kDecStagedK) {
+      // down over its two column halves as two sources, two m-tiles per
+      // tile: each input record serves two m-tiles; the residual norm adds
+      // the halves' outputs in order
+      DecodeGroup& g = d.down;
+      g.layout = DecodeLayout{};
+      g.layout.kind = kDecPlain;
+      g.layout.K = F / 2;
+      g.layout.H = H;
+      g.layout.n_src = 2;
+      const int row_bytes = F / 32 * 34;
+      for (int j = 0; j < 2; ++j) {
+        g.layout.rows[j] = int(l.down.rows);
+        g.layout.src_ld[j] = row_bytes;
+        g.layout.x_col[j] = j * (F / 2);
+      }
+      g.layout.x_ld = F;
+      Job job{&g, {q8(l.down), q8(l.down) + (F / 2) / 32 * 34}};
+      if (!decode_layout(g.layout, sms_) || g.layout.first_mtile[1] % g.layout.mt)
+        throw std::invalid_argument("decode projection shape not supported");
+      jobs.push_back(job);
+    } else {
+      add(d.down, kDecPlain, F, {&l.down});
+    }
   }
   add(decode_head_, kDecPlain, H, {&device_.output});
   size_t total = 0;
@@ -430,6 +453,7 @@ Session::Session(std::shared_ptr<Model> model, uint32_t context)
     rows_ = DeviceBuffer(sizeof(DecodeRows));
     x_ = DeviceBuffer(R * H * 4);
     out_ = DeviceBuffer(R * H * 4);
+    out2_ = DeviceBuffer(size_t(kMaxBatch) * H * 4);
     p_ = DeviceBuffer(R * 3 * H * 4);
     q_ = DeviceBuffer(R * A * 4);
     k_ = DeviceBuffer(R * KV * 4);
@@ -822,12 +846,17 @@ void Session::DecodeRound(std::span<Session* const> batch,
       f.split_out = h_split_.data();
       f.split_width = F;
       gemv(f, dl.gate_up, &dl.down);
+      // down, over two column halves when its group is split (the second
+      // half's rows go to out2_, added by the norm)
+      const bool halves = dl.down.layout.x_ld != 0;
       GemvParams d{};
       d.kind = kGemvPlain;
       d.K = F;
       d.tokens = B;
-      d.n_out = 1;
+      d.n_out = halves ? 2 : 1;
       d.o[0] = Out(l.down, out, H);
+      if (halves)
+        d.o[1] = Out(l.down, out2_.as<float>(), H);
       d.x = h_split_.data();
       gemv(d, dl.down, next_layer(i));
       const bool last = i + 1 == c.n_layers;
@@ -837,7 +866,8 @@ void Session::DecodeRound(std::span<Session* const> batch,
         Check(launch_residual_norm(
             out, static_cast<const float*>(l.post_ffn_norm.data), x, next,
             NormOut{last ? z32_.as<float>() : nullptr, z, nullptr, nullptr}, B,
-            H, c.eps, s, true));
+            H, c.eps, s, true, nullptr,
+            halves ? out2_.as<float>() : nullptr));
       });
     }
     if (logits)

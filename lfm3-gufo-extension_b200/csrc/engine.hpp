@@ -304,7 +304,8 @@ private:
   DeviceBuffer layer_table_;  // LayerState[n_layers]
   DeviceBuffer frontier_, logits_;
   // workspace (this session's passes, and rounds it leads)
-  DeviceBuffer ids_, rows_, x_, out_, p_, q_, k_, v_, gate_, a_, ff_,
+  DeviceBuffer ids_, rows_, x_, out_,
+      out2_ /* a K-split decode projection's second half */, p_, q_, k_, v_, gate_, a_, ff_,
       half_, scale_, z_split_, a_split_, h_split_, z32_, batch_logits_,
       chunk_k_, chunk_v_, attn_partials_,
       attn_tickets_, prompt_scratch_, split_partial_, zf_;

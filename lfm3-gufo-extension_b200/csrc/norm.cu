@@ -147,6 +147,13 @@ __global__ void __launch_bounds__(kNormThreads)
       const float4 c1 = *reinterpret_cast<const float4*>(br + 4);
       b[j][0] = c0.x, b[j][1] = c0.y, b[j][2] = c0.z, b[j][3] = c0.w;
       b[j][4] = c1.x, b[j][5] = c1.y, b[j][6] = c1.z, b[j][7] = c1.w;
+      if (split.second) {  // the other half of a K split, added second
+        const float* br2 = split.second + size_t(row) * H + k0;
+        const float4 e0 = *reinterpret_cast<const float4*>(br2);
+        const float4 e1 = *reinterpret_cast<const float4*>(br2 + 4);
+        b[j][0] += e0.x, b[j][1] += e0.y, b[j][2] += e0.z, b[j][3] += e0.w;
+        b[j][4] += e1.x, b[j][5] += e1.y, b[j][6] += e1.z, b[j][7] += e1.w;
+      }
     } else if (split.partial) {
       // the branch is scale[row] * (sum over K splits, in split order)
       const int tile = (k0 >> 8) * split.token_tiles + (row >> 8);
@@ -412,15 +419,21 @@ cudaError_t launch_residual_norm(const float* branch, const float* post_w,
                                  float* x, const float* norm_w, NormOut out,
                                  int rows, int H, float eps,
                                  cudaStream_t stream, bool pdl,
-                                 const SplitBranch* split) {
+                                 const SplitBranch* split,
+                                 const float* branch2) {
   if (H % 8 || H > kNormThreads * 8 * kNormMaxGroups)
     return cudaErrorInvalidValue;
   SplitBranch sb{};
   if (split) {
     sb = *split;
     if (branch || !sb.partial || sb.splits < 1 ||
-        sb.token_tiles < (rows + 255) / 256 || H % 256)
+        sb.token_tiles < (rows + 255) / 256 || H % 256 || sb.second)
       return cudaErrorInvalidValue;
+  }
+  if (branch2) {
+    if (!branch || split)
+      return cudaErrorInvalidValue;
+    sb.second = branch2;
   }
   if (!rows)
     return cudaSuccess;

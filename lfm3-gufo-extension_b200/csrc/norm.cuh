@@ -26,6 +26,9 @@ struct SplitBranch {
   const float* scale;
   int splits;
   int token_tiles;
+  // with a plain branch: a second FP32 branch [rows][H] added after it (the
+  // other half of a decode projection split over K)
+  const float* second;
 };
 
 // x += RMSNorm_post(branch) (when branch, or split; post_w may be null:
@@ -35,7 +38,8 @@ cudaError_t launch_residual_norm(const float* branch, const float* post_w,
                                  float* x, const float* norm_w, NormOut out,
                                  int rows, int H, float eps,
                                  cudaStream_t stream, bool pdl,
-                                 const SplitBranch* split = nullptr);
+                                 const SplitBranch* split = nullptr,
+                                 const float* branch2 = nullptr);
 
 // x[r] = embedding row ids[r] (F32 / F16 / BF16 / Q8_0 rows), then out =
 // RMSNorm(x) * norm_w. hip/ops.hip:858-875 fused with the first norm.

@@ -337,7 +337,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int g = lane >> 2, cq = lane & 3;
   const bool live = g < p.tokens;
   const uint4* xr = static_cast<const uint4*>(p.x);
-  const int records = p.layout.K / 8;
+  // input records per row, and the first record of the tile's source
+  const int records = (p.layout.x_ld ? p.layout.x_ld : p.layout.K) / 8;
+  int xrec0 = 0;
   // the hi and lo input terms of token g for this warp's blocks of unit c
   struct Terms {
     uint4 hi[kPerWarp], lo[kPerWarp];
@@ -355,7 +357,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           x.hi[i] = rec[0];
           x.lo[i] = rec[1];
         } else {
-          const uint4* rec = xr + (size_t(g) * records + kb * 4 + cq) * 2;
+          const uint4* rec =
+              xr + (size_t(g) * records + xrec0 + kb * 4 + cq) * 2;
           x.hi[i] = __ldg(rec);
           x.lo[i] = __ldg(rec + 1);
         }
@@ -371,6 +374,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         acc[m][j] = 0;
+    if constexpr (kKind == kDecPlain && !kStaged) {
+      int j = 0, row0 = 0;
+      decode_mtile_source(p.layout, t, 0, j, row0);
+      xrec0 = p.layout.x_col[j] / 8;
+    }
     Terms cur, next;
     if constexpr (!kStaged)
       fetch(0, cur);
@@ -477,8 +485,9 @@ __global__ void decode_pack_bf16_kernel(const DecodeLayout l, const uint8_t* s0,
   for (int h = 0; h < 2; ++h) {
     const int row = row0 + g + 8 * h;
     uint4 v = make_uint4(0, 0, 0, 0);
+    const size_t ld = l.src_ld[j] ? size_t(l.src_ld[j]) / 2 : size_t(l.K);
     if (valid && row < l.rows[j])
-      v = *reinterpret_cast<const uint4*>(src + (size_t(row) * l.K + kb * 32 + 8 * c) * 2);
+      v = *reinterpret_cast<const uint4*>(src + (size_t(row) * ld + kb * 32 + 8 * c) * 2);
     *reinterpret_cast<uint4*>(out + 512 * h + lane * 16) = v;
   }
 }
@@ -498,7 +507,7 @@ __global__ void decode_pack_kernel(const DecodeLayout l, const uint8_t* s0,
   int j = 0, row0 = 0;
   const bool valid = decode_mtile_source(l, t, m, j, row0);
   const uint8_t* src = j == 0 ? s0 : j == 1 ? s1 : j == 2 ? s2 : s3;
-  const size_t row_bytes = size_t(KB) * 34;
+  const size_t row_bytes = l.src_ld[j] ? size_t(l.src_ld[j]) : size_t(KB) * 34;
   union {
     uint8_t b[16];
     uint4 v;
@@ -528,7 +537,7 @@ cudaError_t launch_kind(const DecodeParams& p, int grid, cudaStream_t stream,
   // inputs of K <= kDecStagedK columns staged in shared memory: read once
   // per CTA, all chunks requested at once after the dependency wait, instead
   // of an L2 round trip per unit
-  const bool staged = p.layout.K <= kDecStagedK;
+  const bool staged = p.layout.K <= kDecStagedK && !p.layout.x_ld;
   auto kernel = staged ? decode_gemv_kernel<kKind, kMT, 16, true, false>
                        : decode_gemv_kernel<kKind, kMT, 16, false, false>;
   if constexpr (kMT == 1)
@@ -652,6 +661,14 @@ cudaError_t launch_decode_gemv(const DecodeParams& p, int grid,
       reinterpret_cast<uintptr_t>(p.x) % 16 ||
       reinterpret_cast<uintptr_t>(p.w) % 16)
     return cudaErrorInvalidValue;
+  if (l.x_ld) {  // a K split: Plain, whole tiles per source, columns in range
+    if (l.kind != kDecPlain || l.x_ld % 8)
+      return cudaErrorInvalidValue;
+    for (int j = 0; j < l.n_src; ++j)
+      if (l.first_mtile[j] % l.mt || l.x_col[j] % 8 || l.x_col[j] < 0 ||
+          l.x_col[j] + l.K > l.x_ld)
+        return cudaErrorInvalidValue;
+  }
   if (l.kind == kDecPlain) {
     for (int j = 0; j < l.n_src; ++j)
       if (!p.o[j].out)

@@ -74,6 +74,13 @@ struct DecodeLayout {
   int rows[4];  // rows of each source matrix
   int H;        // Conv: channels (in_proj has 3H rows)
   int bf16;     // BF16 matrices (1024-byte records) instead of Q8_0
+  // Plain sources that are column ranges of wider matrices (a K split):
+  // source j's rows are src_ld[j] bytes apart (0: K / 32 x 34, or 2 K for
+  // BF16) and read the input columns x_col[j] .. x_col[j] + K - 1 of input
+  // rows x_ld wide (0: K). No tile may span two such sources.
+  int src_ld[4];
+  int x_col[4];
+  int x_ld;
 };
 
 // Source matrix j and first row of m-tile m of tile t; false for padding.
